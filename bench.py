@@ -1,0 +1,349 @@
+#!/usr/bin/env python
+"""lfm2moe MoE-FFN throughput on B200 (tokens/s), against the reference CPU path.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+A step is one MoE-FFN layer forward over one batch of T tokens (config 2 by
+default: the T=8 speculative-verify batch, D=2048, E=32, top-4, I=1792, Q4_K
+experts).  Weights are generated on the device from the seeded synthetic
+generator.  Consecutive steps cycle through a ring of distinct layers whose
+weights total more than the 126 MB L2, so no step re-reads weights the
+previous steps left in L2.
+
+Printed JSON (one line, rank 0):
+  value      tokens/s over all ranks, inputs resident in HBM, device-timed (CUDA
+             events on the launch stream, max over ranks);
+  e2e        the same metric through the public host-buffer API
+             (lfm_gpu_moe_forward with host x: H2D + layer + D2H per step);
+  roofline   the dominant kernel's algorithmic bytes per launch / its mean
+             event-timed duration, against MEASURED_PEAKS.json's HBM copy rate;
+  cpu_baseline  the reference's own CPU path (oracle/_ref, built from the
+             reference sources) on this host's cores, on a bounded sample.
+Multi-GPU (torchrun): each rank runs its own replica of the step on its own
+tokens ("scaling": "weak"); no collective is on the data path yet.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+Q4K = 144
+METRIC = "MoE-FFN tok/s: decode %HBM roofline, prefill %int8 TC peak, 1/2/4/8 B200"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def config_dict(cfg_id, cfg, ring, extra=None):
+    d = {"workload": f"cfg{cfg_id}: {cfg['name']} (lfm2moe FFN layer, D={cfg['D']} E={cfg['E']} top-{cfg['K']} "
+                     f"I={cfg['I']}, Q4_K experts, T={cfg['T']} tokens per step)",
+         "tokens_per_step": cfg["T"], "D": cfg["D"], "E": cfg["E"], "K": cfg["K"], "I": cfg["I"],
+         "layers_in_ring": ring,
+         "l2": f"steps cycle a ring of {ring} distinct layers "
+               f"({ring * expert_bytes(cfg) * cfg['E'] / 1e9:.2f} GB of expert weights > 126 MB L2); "
+               "no step re-reads weights of the previous steps"}
+    if extra:
+        d.update(extra)
+    return d
+
+
+def expert_bytes(cfg):
+    D, I = cfg["D"], cfg["I"]
+    return (2 * I * (D // 256) + D * (I // 256)) * Q4K
+
+
+def layer_seeds(layer):
+    from laii_b200 import synth
+    return [synth.layer_seed(s, layer) for s in (synth.SEED_GATE, synth.SEED_UP, synth.SEED_DOWN,
+                                                   synth.SEED_ROUTER, synth.SEED_BIAS)]
+
+
+def cpu_baseline(cfg, seconds=12.0, threads=0):
+    """The reference's CPU MoE FFN (built from its sources) on this host, bounded sample."""
+    from laii_b200 import synth
+    from oracle.oracle import REF_SO, Oracle, Reference
+    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0)
+    T = cfg["T"]
+    x = synth.make_hidden(T, cfg["D"], seed_offset=0)
+    if os.path.exists(REF_SO):
+        R = Reference(threads)
+        kind, cores, fwd = "reference", R.n_threads, (lambda xx: R.moe_forward(L, xx, capture=False))
+        label = f"{R.isa}; {R.cpu}"
+    else:
+        O = Oracle()
+        kind, cores, fwd = "port", 1, (lambda xx: O.moe_forward(L, xx))
+        label = "scalar oracle port"
+    fwd(x)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fwd(x)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    tok_s = n * T / el
+    return {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"{n} calls x {T} tokens (cfg layer 0 weights, one lfm2_forward_moe_ffn_1x4 call per token), "
+                      f"{el:.1f} s; {label}; nproc={os.cpu_count()}"}
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from laii_b200 import synth
+    from oracle.oracle import REF_SO, Oracle, Reference
+    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0)
+    T = cfg["T"]
+    x = synth.make_hidden(T, cfg["D"], seed_offset=0)
+    if os.path.exists(REF_SO):
+        R = Reference(0)
+        kind, cores = "reference", R.n_threads
+        fwd = lambda xx: R.moe_forward(L, xx, capture=False)  # noqa: E731
+        label = f"{R.isa}; {R.cpu}"
+    else:
+        O = Oracle()
+        kind, cores = "port", 1
+        fwd = lambda xx: O.moe_forward(L, xx)  # noqa: E731
+        label = "scalar oracle port"
+    for _ in range(args.warmup):
+        fwd(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fwd(x)
+    el = time.perf_counter() - t0
+    v = T * args.steps / el
+    out = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "q4_k x q8_k int, fp32 accum", "data": "synthetic (seeded)",
+           "config": config_dict(args.config, cfg, 1),
+           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
+                            "sample": f"{args.steps} steps x {T} tokens, one lfm2_forward_moe_ffn_1x4 call per "
+                                      f"token; {label}; nproc={os.cpu_count()}"},
+           "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args, cfg):
+    import torch
+    ws, rank, local = dist_setup()
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+
+    D, E, K, I, T = cfg["D"], cfg["E"], cfg["K"], cfg["I"], cfg["T"]
+    R = args.ring
+    g = GpuMoE(local)
+    for l in range(R):
+        g.synth_layer(l, D, E, K, I, layer_seeds(l))
+    g.reserve(T)
+    x0 = synth.make_hidden(T, D, seed_offset=rank * T)
+    x = torch.from_numpy(x0.copy()).cuda()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(i):
+        g.forward_device(i % R, x.data_ptr(), T, stream=sp)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    st0 = g.last_stats()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    st1 = g.last_stats()
+    loads = st1["expert_loads"] - st0["expert_loads"]
+    kernels_per_step = st1["kernels_launched"]
+    if ws > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = ws * T * args.steps / (ms / 1e3)
+
+    # algorithmic bytes: active experts' gate/up/down + router + x in/out
+    eb = expert_bytes(cfg)
+    layer_bytes = loads * eb + args.steps * (E * D * 4 + 2 * T * D * 4)
+    pk = peaks()
+    layer_frac = layer_bytes / (ms / 1e3) / (pk["hbm_gbs"] * 1e9)
+
+    # per-kernel pass (event-bracketed launches inside the library) for the roofline of the dominant kernel
+    g.profile(True)
+    stp = g.last_stats()
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    prof = g.profile_read()
+    g.profile(False)
+    stq = g.last_stats()
+    ploads = stq["expert_loads"] - stp["expert_loads"]
+    dom = max(prof, key=lambda k: prof[k][1])
+    n_launch, tot_ms = prof[dom]
+    gu_bytes = 2 * I * (D // 256) * Q4K
+    dn_bytes = D * (I // 256) * Q4K
+    per_launch_bytes = {"gateup": ploads * gu_bytes / n_launch + T * D * 1.140625,
+                        "down": ploads * dn_bytes / n_launch + T * K * I * 1.140625 + T * K * D * 4}
+    ach = per_launch_bytes.get(dom, 0.0) / (tot_ms / n_launch / 1e3) / 1e9
+    total_prof = sum(v[1] for v in prof.values())
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", f"traffic_{dom}_cfg{args.config}.json")
+    if os.path.exists(tfile):
+        traffic = json.load(open(tfile)).get("dram_bytes_per_launch")
+
+    # end to end through the public host-buffer API (H2D + forward + D2H per call)
+    pinned = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
+    xh = pinned.numpy()
+    xh[:] = x0
+    n_e2e = max(10, min(args.steps, 500))
+    for i in range(3):
+        g.forward(i % R, xh)
+    if ws > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        g.forward(i % R, xh)
+    e2e_s = time.perf_counter() - t0
+    if ws > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = ws * T * n_e2e / e2e_s
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, seconds=args.cpu_seconds)
+
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "q4_k x q8_k int (dp4a), fp32 accum", "data": "synthetic (seeded)",
+               "config": config_dict(args.config, cfg, R, {"parallelism": f"replicas x{ws}" if ws > 1 else "single",
+                                                           "layer_hbm_frac": round(layer_frac, 4),
+                                                           "unique_experts_per_step": loads / args.steps}),
+               "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": ach / pk["hbm_gbs"], "traffic": traffic, "peak_src": pk["src"] + " (burst copy)",
+                            "share": tot_ms / total_prof,
+                            "kernel_ms": {k: round(v[1] / v[0] * 1e3, 2) for k, v in prof.items()},
+                            "kernel_ms_unit": "us per launch"},
+               "cpu_baseline": cpu,
+               "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
+               "gpu_launches": kernels_per_step * args.steps,
+               "clocks": clk}
+        print(json.dumps(out), flush=True)
+    g.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ring", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    from laii_b200.synth import CONFIGS
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * lfm_gpu_moe.h -- C-ABI of the B200 (sm_100a) lfm2moe sparse-MoE FFN.
+ *
+ * Drop-in boundary for laii's CPU MoE FFN.  The reference call it replaces is
+ *
+ *   void lfm2_forward_moe_ffn_1x4(LFM2ThreadPool *pool, float *x, float *xb,
+ *        float *hb, block_q8_K_t *xq_scratch, const LFM2Layer *layer,
+ *        const LFM2MoELayerExt *moe, uint32_t D, float eps);
+ *                                    (tools/lfm2_moe_checkpoint.c:312-320)
+ *
+ * which updates one token's hidden state in place:
+ *   x += sum_k w_k * Down_{e_k}( SwiGLU( Gate_{e_k} xq, Up_{e_k} xq ) )
+ * with xq = Q8_K(RMSNorm(x) * ffn_norm), (e_k, w_k) = sigmoid + exp_probs_b
+ * biased top-K with normalised unbiased weights.  This library does the same
+ * for T tokens at once, on device-resident weights, with no CPU fallback:
+ * every entry point either runs on the GPU or returns an error status.
+ *
+ * Conventions (from the reference's public C API, include/lfm2.h:40-48, and
+ * its Vulkan offload, src/lfm_gpu/lfm_gpu_engine.h:37-44):
+ *  - status codes: 0 = OK, negative = error; lfm_gpu_moe_last_error() has text;
+ *  - caller-owned host buffers; the handle owns all device memory;
+ *  - weights are copied to HBM once at upload (not per call, unlike the Vulkan path);
+ *  - one host thread per handle; calls on a handle are not re-entrant
+ *    (as the reference thread pool, tools/lfm2_threadpool.c:303-324);
+ *  - tensors use GGUF layout: 3-D expert tensors [E][rows][cols/256] of
+ *    144-byte Q4_K blocks (tools/lfm2_moe_checkpoint.c:54-58, :110-127).
+ *
+ * All functions are plain C (no CUDA or torch types); `stream` arguments are a
+ * cudaStream_t passed as void* (NULL = the handle's own stream).
+ */
+#ifndef LFM_GPU_MOE_H
+#define LFM_GPU_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lfm_gpu_moe lfm_gpu_moe_t;
+
+/* Mirrors lfm2_status_t (include/lfm2.h:40-48) for the codes they share. */
+typedef enum {
+    LFM_GPU_OK = 0,
+    LFM_GPU_ERR_INVALID_ARG = -1,   /* bad shape, pointer, layer index          */
+    LFM_GPU_ERR_UNSUPPORTED = -2,   /* weight type / shape this build lacks      */
+    LFM_GPU_ERR_NOT_READY = -3,     /* layer not uploaded                        */
+    LFM_GPU_ERR_OOM = -4,           /* cudaMalloc failed (same code as LFM2_ERR_OOM) */
+    LFM_GPU_ERR_CUDA = -7,          /* CUDA runtime error                        */
+    LFM_GPU_ERR_COMM = -8,          /* expert-parallel exchange failed           */
+    LFM_GPU_ERR_TIMEOUT = -9,       /* a bounded device wait ran out             */
+    LFM_GPU_ERR_DEVICE_CHECK = -10  /* a device-side bounds check tripped        */
+} lfm_gpu_status_t;
+
+#define LFM_GPU_MOE_MAX_EXPERTS 256
+#define LFM_GPU_MOE_MAX_TOP_K 8
+#define LFM_GPU_MOE_MAX_LAYERS 64
+
+/* Create a handle bound to CUDA device `device_id` (its own stream, no layers).
+ * Replaces: nothing in the reference (its CPU path needs no device handle);
+ * the Vulkan analogue is lfm_gpu_engine_init (src/lfm_gpu/lfm_gpu_engine.h:37). */
+lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id);
+
+/* Free all device memory of the handle.  Replaces lfm_gpu_engine_free
+ * (src/lfm_gpu/lfm_gpu_engine.h:38). */
+void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h);
+
+/* Text of the last error on this handle ("" if none). */
+const char *lfm_gpu_moe_last_error(const lfm_gpu_moe_t *h);
+
+/* Upload one lfm2moe layer (copied into HBM).  Replaces the binding of
+ * lfm2_bind_moe_layer (tools/lfm2_moe_checkpoint.c:70-102) plus the mmap'd
+ * tensor data it points at:
+ *   ffn_norm    fp32 [D]               blk.l.ffn_norm.weight (NULL = all ones)
+ *   router_w    fp32 [E][D]            blk.l.ffn_gate_inp.weight
+ *   exp_probs_b fp32 [E] or NULL       blk.l.exp_probs_b(.bias)
+ *   gate_exps   Q4_K [E][I][D/256]     blk.l.ffn_gate_exps.weight
+ *   up_exps     Q4_K [E][I][D/256]     blk.l.ffn_up_exps.weight
+ *   down_exps   Q4_K [E][D][I/256]     blk.l.ffn_down_exps.weight
+ * w_type must be 12 (GGML_TYPE_Q4_K).  D and I multiples of 256, E <= 256,
+ * K <= 8.  norm_topk_prob / routed_scale as LFM2MoELayerExt (reference
+ * defaults true / 1.0f, tools/lfm2_moe_checkpoint.c:98-100). */
+lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                          uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                          const float *router_w, const float *exp_probs_b,
+                                          const void *gate_exps, const void *up_exps,
+                                          const void *down_exps, uint32_t w_type,
+                                          int norm_topk_prob, float routed_scale);
+
+/* Upload a dense SwiGLU FFN layer (the leading layers of an lfm2moe stack,
+ * run by lfm2_forward_ffn_fused_1x4, tools/lfm2_decode_1x4.c:1070-1104):
+ * gate/up Q4_K [I][D/256], down Q4_K [D][I/256]. */
+lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t I,
+                                          float eps, const float *ffn_norm, const void *gate,
+                                          const void *up, const void *down, uint32_t w_type);
+
+/* Fill layer `layer` on the device from the seeded synthetic generator
+ * (byte-identical to the host generator; no host copy of the weights).
+ * Experts N(0, w_std) -> Q4_K, router N(0, router_std), exp_probs_b either
+ * the given host array [E] or N(0, bias_std).  Seeds: see laii_b200/synth.py.
+ * No counterpart in the reference (benchmark input generation). */
+lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                         uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
+                                         float w_std, float router_std, float bias_std,
+                                         const float *exp_probs_b);
+
+/* Reserve scratch for up to max_tokens tokens per forward (forward grows it on
+ * demand; reserve first when the forward is to be captured in a CUDA graph). */
+lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens);
+
+/* x[T][D] += MoE(x) for layer `layer` (or x += DenseFFN(x) for a dense layer),
+ * the batched counterpart of lfm2_forward_moe_ffn_1x4 (tools/lfm2_moe_checkpoint.c:312).
+ * x_on_device = 0: x is host memory; the call copies in, runs and copies back
+ * before returning.  x_on_device = 1: x is device memory; the call is
+ * asynchronous on `stream`. */
+lfm_gpu_status_t lfm_gpu_moe_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                     int x_on_device, void *stream);
+
+/* Layers [first, first + n) in order on the same x (an FFN-only stack). */
+lfm_gpu_status_t lfm_gpu_moe_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x,
+                                           uint32_t T, int x_on_device, void *stream);
+
+/* Routing only, for parity checks: RMSNorm + Q8_K + router + top-K of host
+ * x[T][D] -> expert ids [T][K], weights [T][K] and, if q8_out != NULL, the
+ * Q8_K blocks of the normalised input [T][D/256] (292-byte GGUF layout).
+ * Counterpart of lfm2_rmsnorm_quantize_q8_K_simd + lfm2_moe_route_sigmoid_topk
+ * (tools/lfm2_moe_checkpoint.c:328-333).  Synchronous. */
+lfm_gpu_status_t lfm_gpu_moe_debug_route(lfm_gpu_moe_t *h, uint32_t layer, const float *x, uint32_t T,
+                                         uint32_t *idx_out, float *w_out, void *q8_out);
+
+/* Integer partial sums of the Q4_K x Q8_K kernel used by the expert GEMVs, for
+ * parity: host Q4_K rows w[n_rows][n_cols/256] against host Q8_K vectors
+ * xq[n_vec][n_cols/256]; outputs (host) per (vec, row, super-block):
+ * sub_dots[..][8] = sum over each 32-weight sub-block of q4*q8,
+ * acc = sum_j sc_j*sub_dot_j, mins = sum_j m_j*(bsum pair j), and the fp32 row
+ * results rows_out[n_vec][n_rows].  Counterpart of the Q4_K x Q8_K row kernels
+ * (tools/lfm2_cpuid_quants.c:421-457, :1189-1257).  Synchronous. */
+lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void *w, uint32_t n_rows,
+                                            uint32_t n_cols, const void *xq, uint32_t n_vec,
+                                            int32_t *sub_dots, int32_t *acc, int32_t *mins,
+                                            float *rows_out);
+
+/* Wait for all work on the handle's stream and report any device-side error
+ * (bounds check or timeout) raised since the last call. */
+lfm_gpu_status_t lfm_gpu_moe_sync(lfm_gpu_moe_t *h);
+
+/* Launch statistics of the last forward: kernels launched and the routing
+ * summary (unique experts touched, largest expert segment). */
+typedef struct {
+    uint32_t kernels_launched;    /* kernels of the last forward call                 */
+    uint32_t tokens;              /* T of the last forward call                       */
+    uint32_t unique_experts;      /* experts touched by the last MoE layer run        */
+    uint32_t max_segment;         /* largest per-expert token count of that layer     */
+    uint64_t expert_loads;        /* sum of unique experts over all MoE layer runs
+                                     since the handle was created (each is one pass
+                                     over that expert's gate/up/down bytes)           */
+    uint64_t layer_runs;          /* MoE layer runs counted in expert_loads           */
+} lfm_gpu_moe_stats_t;
+
+/* Synchronous (waits for the handle's stream).  The analogue of the reference's
+ * lfm2_perf_stats_t (include/lfm2.h:99-107) for this path. */
+lfm_gpu_status_t lfm_gpu_moe_last_stats(const lfm_gpu_moe_t *h, lfm_gpu_moe_stats_t *out);
+
+/* Per-kernel device time: with profiling on, every kernel a forward launches
+ * is bracketed by CUDA events on the launch stream; profile_read waits for the
+ * stream, adds up the elapsed times per kernel name and clears the records.
+ * No counterpart in the reference (its bench main uses wall clock,
+ * tools/lfm2_moe_checkpoint.c:706-723). */
+typedef struct {
+    char name[32];
+    uint32_t launches;
+    double total_ms;
+} lfm_gpu_moe_kernel_time_t;
+
+lfm_gpu_status_t lfm_gpu_moe_profile(lfm_gpu_moe_t *h, int enable);
+lfm_gpu_status_t lfm_gpu_moe_profile_read(lfm_gpu_moe_t *h, lfm_gpu_moe_kernel_time_t *out, uint32_t cap,
+                                          uint32_t *n_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LFM_GPU_MOE_H */

@@ -1,0 +1,593 @@
+/*
+ * C-ABI implementation of include/lfm_gpu_moe.h: handle lifecycle, weight
+ * upload into HBM, scratch management and the forward orchestration
+ *   K1 route -> K2 dispatch -> K3 gate|up+SwiGLU -> Q8_K(h) -> K3 down -> K4 combine
+ * for one lfm2moe layer (tools/lfm2_moe_checkpoint.c:312-365, batched over T
+ * tokens) or one dense SwiGLU layer (tools/lfm2_decode_1x4.c:1070-1104).
+ * There is no CPU path: every failure is returned as a status.
+ */
+#include <cuda_runtime.h>
+#include <new>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "../../include/lfm_gpu_moe.h"
+#include "moe_internal.h"
+
+#define LFM_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+struct LayerSlot {
+    bool present = false;
+    MoeLayerDev dev{};
+    void *bufs[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+};
+
+struct Workspace {
+    uint32_t T = 0, D = 0, E = 0, K = 0, I = 0;
+    void *base = nullptr;
+    size_t bytes = 0;
+    float *x = nullptr;       /* [T][D] staging for host x            */
+    Q8Rows xq{};              /* [T] x D                              */
+    RouteTables rt{};
+    float *h = nullptr;       /* [T*K][I]                              */
+    Q8Rows hq{};              /* [T*K] x I                             */
+    float *y = nullptr;       /* [T*K][D]                              */
+};
+
+}  // namespace
+
+namespace {
+enum KernelId { K_ROUTE, K_DISPATCH, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_DENSE_TABLES, K_COUNT };
+const char *const kKernelNames[K_COUNT] = {"route", "dispatch", "gateup", "quant_h", "down", "combine",
+                                           "dense_tables"};
+struct ProfRec {
+    int kid;
+    cudaEvent_t a, b;
+};
+}  // namespace
+
+struct lfm_gpu_moe {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    char err[512] = {0};
+    LayerSlot layers[LFM_GPU_MOE_MAX_LAYERS];
+    Workspace ws;
+    uint32_t *dev_err = nullptr;  /* device error word, zeroed at creation */
+    uint32_t *tok_count = nullptr;
+    uint32_t tok_count_cap = 0;
+    unsigned long long *loads = nullptr;  /* device [2]: expert loads, MoE layer runs */
+    lfm_gpu_moe_stats_t stats{};
+    bool prof = false;
+    std::vector<ProfRec> recs;
+};
+
+namespace {
+
+lfm_gpu_status_t fail(lfm_gpu_moe_t *h, lfm_gpu_status_t st, const char *fmt, ...) {
+    if (h) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(h->err, sizeof h->err, fmt, ap);
+        va_end(ap);
+    }
+    return st;
+}
+
+lfm_gpu_status_t cuda_fail(lfm_gpu_moe_t *h, cudaError_t e, const char *what) {
+    const lfm_gpu_status_t st = e == cudaErrorMemoryAllocation ? LFM_GPU_ERR_OOM : LFM_GPU_ERR_CUDA;
+    return fail(h, st, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define LFM_CUDA(h, call)                                    \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail((h), e_, #call); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+void free_layer(LayerSlot &L) {
+    for (void *&p : L.bufs) {
+        if (p) cudaFree(p);
+        p = nullptr;
+    }
+    L.present = false;
+    L.dev = MoeLayerDev{};
+}
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+/* Make sure the workspace covers T tokens for the given layer shape. */
+lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint32_t E, uint32_t K, uint32_t I) {
+    Workspace &w = h->ws;
+    if (w.base && T <= w.T && D <= w.D && E <= w.E && K <= w.K && I <= w.I) return LFM_GPU_OK;
+    T = T > w.T ? T : w.T; D = D > w.D ? D : w.D; E = E > w.E ? E : w.E;
+    K = K > w.K ? K : w.K; I = I > w.I ? I : w.I;
+    if (E < 1) E = 1;
+    if (K < 1) K = 1;
+    const size_t TK = (size_t)T * K;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_x = take(sizeof(float) * T * D);
+    const size_t o_xq = take((size_t)T * D);
+    const size_t o_xd = take(sizeof(float) * T * (D / 256));
+    const size_t o_xb = take(sizeof(int16_t) * T * (D / 256) * 16);
+    const size_t o_idx = take(sizeof(int32_t) * TK);
+    const size_t o_w = take(sizeof(float) * TK);
+    const size_t o_cnt = take(sizeof(int32_t) * E);
+    const size_t o_off = take(sizeof(int32_t) * (E + 1));
+    const size_t o_perm = take(sizeof(int32_t) * TK);
+    const size_t o_inv = take(sizeof(int32_t) * TK);
+    const size_t o_cur = take(sizeof(int32_t) * E);
+    const size_t o_sum = take(sizeof(int32_t) * 4);
+    const size_t o_log = take(sizeof(float) * T * E);
+    const size_t o_h = take(sizeof(float) * TK * I);
+    const size_t o_hq = take(TK * I);
+    const size_t o_hd = take(sizeof(float) * TK * (I / 256));
+    const size_t o_hb = take(sizeof(int16_t) * TK * (I / 256) * 16);
+    const size_t o_y = take(sizeof(float) * TK * D);
+    void *base = nullptr;
+    /* the old workspace may still be read by queued work on any stream */
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(h, e, "workspace sync");
+    e = cudaMalloc(&base, off);
+    if (e != cudaSuccess) return cuda_fail(h, e, "workspace cudaMalloc");
+    if (w.base) cudaFree(w.base);
+    if (T > h->tok_count_cap) {
+        uint32_t *tc = nullptr;
+        e = cudaMalloc(&tc, sizeof(uint32_t) * T);
+        if (e != cudaSuccess) { cudaFree(base); w.base = nullptr; w.T = 0; return cuda_fail(h, e, "counter cudaMalloc"); }
+        e = cudaMemset(tc, 0, sizeof(uint32_t) * T);
+        if (e != cudaSuccess) { cudaFree(base); cudaFree(tc); w.base = nullptr; w.T = 0; return cuda_fail(h, e, "counter memset"); }
+        if (h->tok_count) cudaFree(h->tok_count);
+        h->tok_count = tc;
+        h->tok_count_cap = T;
+    }
+    uint8_t *b = static_cast<uint8_t *>(base);
+    w.base = base; w.bytes = off;
+    w.T = T; w.D = D; w.E = E; w.K = K; w.I = I;
+    w.x = reinterpret_cast<float *>(b + o_x);
+    w.xq = Q8Rows{reinterpret_cast<int8_t *>(b + o_xq), reinterpret_cast<float *>(b + o_xd),
+                  reinterpret_cast<int16_t *>(b + o_xb), 0};
+    w.rt.idx = reinterpret_cast<int32_t *>(b + o_idx);
+    w.rt.w = reinterpret_cast<float *>(b + o_w);
+    w.rt.counts = reinterpret_cast<int32_t *>(b + o_cnt);
+    w.rt.offsets = reinterpret_cast<int32_t *>(b + o_off);
+    w.rt.perm = reinterpret_cast<int32_t *>(b + o_perm);
+    w.rt.inv = reinterpret_cast<int32_t *>(b + o_inv);
+    w.rt.cursor = reinterpret_cast<int32_t *>(b + o_cur);
+    w.rt.summary = reinterpret_cast<int32_t *>(b + o_sum);
+    w.rt.logits = reinterpret_cast<float *>(b + o_log);
+    w.rt.tok_count = h->tok_count;
+    w.rt.err = h->dev_err;
+    w.rt.loads = h->loads;
+    w.h = reinterpret_cast<float *>(b + o_h);
+    w.hq = Q8Rows{reinterpret_cast<int8_t *>(b + o_hq), reinterpret_cast<float *>(b + o_hd),
+                  reinterpret_cast<int16_t *>(b + o_hb), 0};
+    w.y = reinterpret_cast<float *>(b + o_y);
+    return LFM_GPU_OK;
+}
+
+lfm_gpu_status_t check_layer_shape(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E, uint32_t K,
+                                   uint32_t I) {
+    if (layer >= LFM_GPU_MOE_MAX_LAYERS) return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer %u out of range", layer);
+    if (D == 0 || D % 256 || I == 0 || I % 256)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "D=%u and I=%u must be positive multiples of 256", D, I);
+    if (D > 16384 || I > 32768) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "D=%u / I=%u above this build's limits", D, I);
+    if (E == 0 || E > LFM_GPU_MOE_MAX_EXPERTS) return fail(h, LFM_GPU_ERR_INVALID_ARG, "E=%u not in 1..256", E);
+    if (K == 0 || K > LFM_GPU_MOE_MAX_TOP_K || K > E)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "K=%u not in 1..min(8,E)", K);
+    return LFM_GPU_OK;
+}
+
+/* Launch one kernel, bracketed by events when profiling is on. */
+template <typename F>
+cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
+    if (!h->prof) {
+        ++h->stats.kernels_launched;
+        return launch();
+    }
+    ProfRec r{kid, nullptr, nullptr};
+    cudaError_t e = cudaEventCreate(&r.a);
+    if (e == cudaSuccess) e = cudaEventCreate(&r.b);
+    if (e == cudaSuccess) e = cudaEventRecord(r.a, s);
+    if (e == cudaSuccess) e = launch();
+    if (e == cudaSuccess) e = cudaEventRecord(r.b, s);
+    if (e == cudaSuccess) {
+        h->recs.push_back(r);
+        ++h->stats.kernels_launched;
+    } else {
+        if (r.a) cudaEventDestroy(r.a);
+        if (r.b) cudaEventDestroy(r.b);
+    }
+    return e;
+}
+
+/* One layer forward on device x; `stream` already resolved. */
+lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s) {
+    const MoeLayerDev &L = S.dev;
+    Workspace &w = h->ws;  /* sized for the whole call by forward_common */
+    Q8Rows xq = w.xq; xq.cols = L.D;
+    Q8Rows hq = w.hq; hq.cols = L.I;
+    if (L.dense) {
+        MoeLayerDev rl = L; rl.E = 0; rl.K = 1;
+        MoeLayerDev el = L; el.E = 1; el.K = 1;
+        RouteTables rt = w.rt; rt.loads = nullptr;  /* dense layers are not expert loads */
+        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(rl, x, T, xq, rt, s); }));
+        LFM_CUDA(h, timed(h, K_DENSE_TABLES, s, [&] { return lfm_launch_dense_tables(T, rt, s); }));
+        LFM_CUDA(h, timed(h, K_DISPATCH, s, [&] { return lfm_launch_dispatch(el, T, rt, s); }));
+        LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(el, T, xq, rt, w.h, s); }));
+        LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T, L.I, hq, s); }));
+        LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(el, T, hq, rt, w.y, s); }));
+        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(el, x, T, rt, w.y, s); }));
+        return LFM_GPU_OK;
+    }
+    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s); }));
+    LFM_CUDA(h, timed(h, K_DISPATCH, s, [&] { return lfm_launch_dispatch(L, T, w.rt, s); }));
+    LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, T, xq, w.rt, w.h, s); }));
+    LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * L.K, L.I, hq, s); }));
+    LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, T, hq, w.rt, w.y, s); }));
+    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s); }));
+    return LFM_GPU_OK;
+}
+
+lfm_gpu_status_t read_device_error(lfm_gpu_moe_t *h) {
+    uint32_t e = 0;
+    LFM_CUDA(h, cudaMemcpy(&e, h->dev_err, sizeof e, cudaMemcpyDeviceToHost));
+    if (e == 0) return LFM_GPU_OK;
+    LFM_CUDA(h, cudaMemset(h->dev_err, 0, sizeof(uint32_t)));
+    if (e & LFM_DEVERR_TIMEOUT) return fail(h, LFM_GPU_ERR_TIMEOUT, "device wait timed out (0x%x)", e);
+    return fail(h, LFM_GPU_ERR_DEVICE_CHECK, "device bounds check tripped (0x%x)", e);
+}
+
+}  // namespace
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) {
+    if (!out) return LFM_GPU_ERR_INVALID_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device_id < 0 || device_id >= n) return LFM_GPU_ERR_INVALID_ARG;
+    lfm_gpu_moe_t *h = new (std::nothrow) lfm_gpu_moe_t();
+    if (!h) return LFM_GPU_ERR_OOM;
+    h->device = device_id;
+    DeviceGuard g(device_id);
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&h->dev_err, sizeof(uint32_t)) != cudaSuccess ||
+        cudaMemset(h->dev_err, 0, sizeof(uint32_t)) != cudaSuccess ||
+        cudaMalloc(&h->loads, 2 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(h->loads, 0, 2 * sizeof(unsigned long long)) != cudaSuccess) {
+        lfm_gpu_moe_destroy(h);
+        return LFM_GPU_ERR_CUDA;
+    }
+    *out = h;
+    return LFM_GPU_OK;
+}
+
+LFM_API void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h) {
+    if (!h) return;
+    DeviceGuard g(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (LayerSlot &L : h->layers) free_layer(L);
+    if (h->ws.base) cudaFree(h->ws.base);
+    if (h->tok_count) cudaFree(h->tok_count);
+    if (h->dev_err) cudaFree(h->dev_err);
+    if (h->loads) cudaFree(h->loads);
+    for (ProfRec &r : h->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+LFM_API const char *lfm_gpu_moe_last_error(const lfm_gpu_moe_t *h) { return h ? h->err : "null handle"; }
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                  uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                  const float *router_w, const float *exp_probs_b,
+                                                  const void *gate_exps, const void *up_exps,
+                                                  const void *down_exps, uint32_t w_type, int norm_topk_prob,
+                                                  float routed_scale) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
+    if (st != LFM_GPU_OK) return st;
+    if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "expert weight type %u (only Q4_K=12)", w_type);
+    if (!router_w || !gate_exps || !up_exps || !down_exps) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
+    DeviceGuard g(h->device);
+    LayerSlot &S = h->layers[layer];
+    free_layer(S);
+    const size_t nbd = D / 256, nbi = I / 256;
+    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * E,
+                          (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
+                          (size_t)E * D * nbi * LFM_Q4K_BYTES};
+    const void *src[6] = {ffn_norm, router_w, exp_probs_b, gate_exps, up_exps, down_exps};
+    for (int i = 0; i < 6; ++i) {
+        if (i == 0 && !ffn_norm) continue;
+        if (i == 2 && !exp_probs_b) continue;
+        cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
+        if (e == cudaSuccess) e = cudaMemcpy(S.bufs[i], src[i], sz[i], cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "layer upload"); }
+    }
+    S.dev = MoeLayerDev{D, E, K, I, 0, eps, routed_scale, norm_topk_prob ? 1 : 0,
+                        static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
+                        static_cast<float *>(S.bufs[2]), static_cast<const uint8_t *>(S.bufs[3]),
+                        static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5])};
+    S.present = true;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t I,
+                                                  float eps, const float *ffn_norm, const void *gate,
+                                                  const void *up, const void *down, uint32_t w_type) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    lfm_gpu_status_t st = check_layer_shape(h, layer, D, 1, 1, I);
+    if (st != LFM_GPU_OK) return st;
+    if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "dense weight type %u (only Q4_K=12)", w_type);
+    if (!gate || !up || !down) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
+    DeviceGuard g(h->device);
+    LayerSlot &S = h->layers[layer];
+    free_layer(S);
+    const size_t nbd = D / 256, nbi = I / 256;
+    const size_t sz[4] = {sizeof(float) * D, (size_t)I * nbd * LFM_Q4K_BYTES, (size_t)I * nbd * LFM_Q4K_BYTES,
+                          (size_t)D * nbi * LFM_Q4K_BYTES};
+    const void *src[4] = {ffn_norm, gate, up, down};
+    const int slot[4] = {0, 3, 4, 5};
+    for (int i = 0; i < 4; ++i) {
+        if (i == 0 && !ffn_norm) continue;
+        cudaError_t e = cudaMalloc(&S.bufs[slot[i]], sz[i]);
+        if (e == cudaSuccess) e = cudaMemcpy(S.bufs[slot[i]], src[i], sz[i], cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "dense upload"); }
+    }
+    S.dev = MoeLayerDev{D, 0, 0, I, 1, eps, 1.0f, 0, static_cast<float *>(S.bufs[0]), nullptr, nullptr,
+                        static_cast<const uint8_t *>(S.bufs[3]), static_cast<const uint8_t *>(S.bufs[4]),
+                        static_cast<const uint8_t *>(S.bufs[5])};
+    S.present = true;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                 uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
+                                                 float w_std, float router_std, float bias_std,
+                                                 const float *exp_probs_b) {
+    if (!h || !seeds) return LFM_GPU_ERR_INVALID_ARG;
+    lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
+    if (st != LFM_GPU_OK) return st;
+    DeviceGuard g(h->device);
+    LayerSlot &S = h->layers[layer];
+    free_layer(S);
+    const size_t nbd = D / 256, nbi = I / 256;
+    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * E,
+                          (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
+                          (size_t)E * D * nbi * LFM_Q4K_BYTES};
+    for (int i = 0; i < 6; ++i) {
+        cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
+        if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "synth layer cudaMalloc"); }
+    }
+    cudaStream_t s = h->stream;
+    cudaError_t e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[0]), D, 0, 1.0f, 0.0f, s);
+    if (e == cudaSuccess) e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[1]), (uint64_t)E * D, seeds[3], 0.0f, router_std, s);
+    if (e == cudaSuccess) {
+        if (exp_probs_b) e = cudaMemcpyAsync(S.bufs[2], exp_probs_b, sizeof(float) * E, cudaMemcpyHostToDevice, s);
+        else e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[2]), E, seeds[4], 0.0f, bias_std, s);
+    }
+    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[3]), (uint64_t)E * I * nbd, seeds[0], w_std, s);
+    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[4]), (uint64_t)E * I * nbd, seeds[1], w_std, s);
+    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[5]), (uint64_t)E * D * nbi, seeds[2], w_std, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "synth layer"); }
+    S.dev = MoeLayerDev{D, E, K, I, 0, eps, 1.0f, 1, static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
+                        static_cast<float *>(S.bufs[2]), static_cast<const uint8_t *>(S.bufs[3]),
+                        static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5])};
+    S.present = true;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    if (max_tokens == 0 || max_tokens > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "max_tokens %u not in 1..65535", max_tokens);
+    uint32_t D = 0, E = 1, K = 1, I = 0;
+    for (const LayerSlot &S : h->layers) {
+        if (!S.present) continue;
+        D = S.dev.D > D ? S.dev.D : D;
+        I = S.dev.I > I ? S.dev.I : I;
+        E = S.dev.E > E ? S.dev.E : E;
+        K = S.dev.K > K ? S.dev.K : K;
+    }
+    if (D == 0) return fail(h, LFM_GPU_ERR_NOT_READY, "reserve before any layer upload");
+    DeviceGuard g(h->device);
+    return ensure_workspace(h, max_tokens, D, E, K, I);
+}
+
+static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x, uint32_t T,
+                                       int x_on_device, void *stream) {
+    if (!h || !x) return LFM_GPU_ERR_INVALID_ARG;
+    if (T == 0) return LFM_GPU_OK;
+    if (T > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "T=%u above 65535 tokens per call", T);
+    if (n == 0 || first >= LFM_GPU_MOE_MAX_LAYERS || n > LFM_GPU_MOE_MAX_LAYERS - first)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer range [%u, %u+%u) invalid", first, first, n);
+    uint32_t D = 0, E = 1, K = 1, I = 0;
+    for (uint32_t l = first; l < first + n; ++l) {
+        const LayerSlot &S = h->layers[l];
+        if (!S.present) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", l);
+        if (D && S.dev.D != D) return fail(h, LFM_GPU_ERR_INVALID_ARG, "layers disagree on D");
+        D = S.dev.D;
+        E = S.dev.E > E ? S.dev.E : E;
+        K = S.dev.K > K ? S.dev.K : K;
+        I = S.dev.I > I ? S.dev.I : I;
+    }
+    DeviceGuard g(h->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    lfm_gpu_status_t st = ensure_workspace(h, T, D, E, K, I);
+    if (st != LFM_GPU_OK) return st;
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+    float *xd = x;
+    if (!x_on_device) {
+        xd = h->ws.x;
+        LFM_CUDA(h, cudaMemcpyAsync(xd, x, sizeof(float) * T * D, cudaMemcpyHostToDevice, s));
+    }
+    for (uint32_t l = first; l < first + n; ++l) {
+        st = forward_layer(h, h->layers[l], xd, T, s);
+        if (st != LFM_GPU_OK) return st;
+    }
+    if (!x_on_device) {
+        LFM_CUDA(h, cudaMemcpyAsync(x, xd, sizeof(float) * T * D, cudaMemcpyDeviceToHost, s));
+        LFM_CUDA(h, cudaStreamSynchronize(s));
+        return read_device_error(h);
+    }
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                             int x_on_device, void *stream) {
+    return forward_common(h, layer, 1, x, T, x_on_device, stream);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x,
+                                                   uint32_t T, int x_on_device, void *stream) {
+    return forward_common(h, first, n, x, T, x_on_device, stream);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_route(lfm_gpu_moe_t *h, uint32_t layer, const float *x, uint32_t T,
+                                                 uint32_t *idx_out, float *w_out, void *q8_out) {
+    if (!h || !x || !idx_out || !w_out) return LFM_GPU_ERR_INVALID_ARG;
+    if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present || h->layers[layer].dev.dense)
+        return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u is not an uploaded MoE layer", layer);
+    if (T == 0 || T > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "T=%u not in 1..65535", T);
+    const MoeLayerDev &L = h->layers[layer].dev;
+    DeviceGuard g(h->device);
+    lfm_gpu_status_t st = ensure_workspace(h, T, L.D, L.E, L.K, L.I);
+    if (st != LFM_GPU_OK) return st;
+    cudaStream_t s = h->stream;
+    Workspace &w = h->ws;
+    Q8Rows xq = w.xq; xq.cols = L.D;
+    LFM_CUDA(h, cudaMemcpyAsync(w.x, x, sizeof(float) * T * L.D, cudaMemcpyHostToDevice, s));
+    LFM_CUDA(h, lfm_launch_route(L, w.x, T, xq, w.rt, s));
+    LFM_CUDA(h, cudaMemcpyAsync(idx_out, w.rt.idx, sizeof(int32_t) * T * L.K, cudaMemcpyDeviceToHost, s));
+    LFM_CUDA(h, cudaMemcpyAsync(w_out, w.rt.w, sizeof(float) * T * L.K, cudaMemcpyDeviceToHost, s));
+    if (q8_out) {
+        /* pack into the y buffer (T*K*D*4 bytes >= T*(D/256)*292), then copy out */
+        uint8_t *tmp = reinterpret_cast<uint8_t *>(w.y);
+        LFM_CUDA(h, lfm_launch_q8_to_gguf(xq, T, tmp, s));
+        LFM_CUDA(h, cudaMemcpyAsync(q8_out, tmp, (size_t)T * (L.D / 256) * LFM_Q8K_BYTES, cudaMemcpyDeviceToHost, s));
+    }
+    LFM_CUDA(h, cudaStreamSynchronize(s));
+    return read_device_error(h);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void *w, uint32_t n_rows,
+                                                    uint32_t n_cols, const void *xq, uint32_t n_vec,
+                                                    int32_t *sub_dots, int32_t *acc, int32_t *mins,
+                                                    float *rows_out) {
+    if (!h || !w || !xq || !sub_dots || !acc || !mins || !rows_out) return LFM_GPU_ERR_INVALID_ARG;
+    if (n_cols == 0 || n_cols % 256 || n_cols > 32768 || n_rows == 0 || n_vec == 0 || n_vec > 65535)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "bad debug shape rows=%u cols=%u vecs=%u", n_rows, n_cols, n_vec);
+    DeviceGuard g(h->device);
+    const size_t nb = n_cols / 256;
+    const size_t wb = (size_t)n_rows * nb * LFM_Q4K_BYTES, xb = (size_t)n_vec * nb * LFM_Q8K_BYTES;
+    const size_t no = (size_t)n_vec * n_rows;
+    size_t off = 0;
+    auto take = [&](size_t b) { const size_t o = off; off += align256(b); return o; };
+    const size_t o_w = take(wb), o_x = take(xb), o_qs = take((size_t)n_vec * n_cols), o_d = take(4 * n_vec * nb),
+                 o_bs = take(32 * n_vec * nb), o_sd = take(4 * no * nb * 8), o_a = take(4 * no * nb),
+                 o_m = take(4 * no * nb), o_r = take(4 * no);
+    uint8_t *buf = nullptr;
+    LFM_CUDA(h, cudaMalloc(&buf, off));
+    cudaStream_t s = h->stream;
+    Q8Rows q{reinterpret_cast<int8_t *>(buf + o_qs), reinterpret_cast<float *>(buf + o_d),
+             reinterpret_cast<int16_t *>(buf + o_bs), n_cols};
+    cudaError_t e = cudaMemcpyAsync(buf + o_w, w, wb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(buf + o_x, xq, xb, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = lfm_launch_gguf_to_q8(buf + o_x, n_vec, q, s);
+    if (e == cudaSuccess)
+        e = lfm_launch_debug_q4k_rows(buf + o_w, n_rows, n_cols, q, n_vec, reinterpret_cast<int32_t *>(buf + o_sd),
+                                      reinterpret_cast<int32_t *>(buf + o_a), reinterpret_cast<int32_t *>(buf + o_m),
+                                      reinterpret_cast<float *>(buf + o_r), s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(sub_dots, buf + o_sd, 4 * no * nb * 8, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(acc, buf + o_a, 4 * no * nb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(mins, buf + o_m, 4 * no * nb, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(rows_out, buf + o_r, 4 * no, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(buf);
+    if (e != cudaSuccess) return cuda_fail(h, e, "debug_q4k_rows");
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_sync(lfm_gpu_moe_t *h) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    DeviceGuard g(h->device);
+    LFM_CUDA(h, cudaStreamSynchronize(h->stream));
+    LFM_CUDA(h, cudaDeviceSynchronize());
+    return read_device_error(h);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_last_stats(const lfm_gpu_moe_t *hc, lfm_gpu_moe_stats_t *out) {
+    lfm_gpu_moe_t *h = const_cast<lfm_gpu_moe_t *>(hc);
+    if (!h || !out) return LFM_GPU_ERR_INVALID_ARG;
+    DeviceGuard g(h->device);
+    *out = h->stats;
+    LFM_CUDA(h, cudaDeviceSynchronize());
+    unsigned long long ld[2] = {0, 0};
+    LFM_CUDA(h, cudaMemcpy(ld, h->loads, sizeof ld, cudaMemcpyDeviceToHost));
+    out->expert_loads = ld[0];
+    out->layer_runs = ld[1];
+    if (h->ws.base) {
+        int32_t sm[4] = {0, 0, 0, 0};
+        LFM_CUDA(h, cudaMemcpy(sm, h->ws.rt.summary, sizeof sm, cudaMemcpyDeviceToHost));
+        out->unique_experts = (uint32_t)sm[0];
+        out->max_segment = (uint32_t)sm[1];
+    }
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_profile(lfm_gpu_moe_t *h, int enable) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    h->prof = enable != 0;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_profile_read(lfm_gpu_moe_t *h, lfm_gpu_moe_kernel_time_t *out, uint32_t cap,
+                                                  uint32_t *n_out) {
+    if (!h || (!out && cap) || !n_out) return LFM_GPU_ERR_INVALID_ARG;
+    DeviceGuard g(h->device);
+    LFM_CUDA(h, cudaDeviceSynchronize());
+    double ms[K_COUNT] = {0};
+    uint32_t cnt[K_COUNT] = {0};
+    cudaError_t err = cudaSuccess;
+    for (ProfRec &r : h->recs) {
+        float t = 0.0f;
+        cudaError_t e = cudaEventElapsedTime(&t, r.a, r.b);
+        if (e != cudaSuccess && err == cudaSuccess) err = e;
+        ms[r.kid] += t;
+        cnt[r.kid] += 1;
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    h->recs.clear();
+    if (err != cudaSuccess) return cuda_fail(h, err, "profile events");
+    uint32_t n = 0;
+    for (int k = 0; k < K_COUNT; ++k) {
+        if (!cnt[k]) continue;
+        if (n < cap) {
+            snprintf(out[n].name, sizeof out[n].name, "%s", kKernelNames[k]);
+            out[n].launches = cnt[k];
+            out[n].total_ms = ms[k];
+        }
+        ++n;
+    }
+    *n_out = n;
+    return LFM_GPU_OK;
+}

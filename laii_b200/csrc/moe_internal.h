@@ -1,0 +1,90 @@
+/*
+ * Internal (non-exported) interfaces of liblfm_gpu_moe.so: device-side data
+ * layouts of the MoE-FFN path and the kernel launchers each .cu provides.
+ *
+ * HBM layout (per layer, see lfm_gpu_moe.cu):
+ *   gate/up  Q4_K [E][I][D/256]  144-byte GGUF blocks, uploaded as-is
+ *   down     Q4_K [E][D][I/256]
+ *   router   fp32 [E][D], bias fp32 [E], ffn_norm fp32 [D]
+ * Activations are kept as split Q8_K rows (qs int8 [rows][cols], d fp32
+ * [rows][cols/256], bsums int16 [rows][cols/256][16]): same numbers as
+ * block_q8_K, but 16-byte aligned rows for vector loads.
+ */
+#ifndef LFM_MOE_INTERNAL_H
+#define LFM_MOE_INTERNAL_H
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "lfm_formats.h"
+
+#define LFM_GPU_MAX_TOPK_DEV 8
+#define LFM_GPU_MAX_EXPERTS_DEV 256
+
+/* Device error word bits (read by lfm_gpu_moe_sync). */
+#define LFM_DEVERR_EXPERT_ID 0x1u   /* routing produced an expert id >= E     */
+#define LFM_DEVERR_SEGMENT 0x2u     /* dispatch segment out of range           */
+#define LFM_DEVERR_TIMEOUT 0x4u     /* a bounded device wait ran out           */
+
+struct Q8Rows {
+    int8_t *qs;      /* [rows][cols]      */
+    float *d;        /* [rows][cols/256]  */
+    int16_t *bs;     /* [rows][cols/256][16] */
+    uint32_t cols;
+};
+
+/* Routing / dispatch tables for one forward. */
+struct RouteTables {
+    int32_t *idx;        /* [T*K] expert id of assignment a = t*K + k           */
+    float *w;            /* [T*K] combine weight                                */
+    int32_t *counts;     /* [E]   assignments per expert                         */
+    int32_t *offsets;    /* [E+1] exclusive prefix of counts                     */
+    int32_t *perm;       /* [T*K] slot -> assignment (grouped by expert)        */
+    int32_t *inv;        /* [T*K] assignment -> slot                             */
+    int32_t *cursor;     /* [E]   scatter cursors (scratch)                      */
+    int32_t *summary;    /* [4]   unique experts, max segment, -, -             */
+    uint32_t *tok_count; /* [T]   per-token arrival counters (kept at zero)      */
+    float *logits;       /* [T*E] router logits                                  */
+    uint32_t *err;       /* device error word                                    */
+    unsigned long long *loads; /* [2] running sum of unique experts, layer runs  */
+};
+
+struct MoeLayerDev {
+    uint32_t D, E, K, I, dense;
+    float eps, routed_scale;
+    int norm_topk;
+    float *ffn_norm;
+    float *router_w;
+    float *bias;         /* NULL when the layer has no exp_probs_b */
+    const uint8_t *gate; /* Q4_K blocks */
+    const uint8_t *up;
+    const uint8_t *down;
+};
+
+/* k_route.cu */
+cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
+                             const RouteTables &rt, cudaStream_t s);
+cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
+/* dense layer: every token to "expert 0" with weight 1 (x + down exactly) */
+cudaError_t lfm_launch_dense_tables(uint32_t T, const RouteTables &rt, cudaStream_t s);
+
+/* k_expert.cu */
+cudaError_t lfm_launch_gateup(const MoeLayerDev &L, uint32_t T, Q8Rows xq, const RouteTables &rt, float *h,
+                              cudaStream_t s);
+cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s);
+cudaError_t lfm_launch_down(const MoeLayerDev &L, uint32_t T, Q8Rows hq, const RouteTables &rt, float *y,
+                            cudaStream_t s);
+cudaError_t lfm_launch_combine(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt,
+                               const float *y, cudaStream_t s);
+cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_t n_cols, Q8Rows xq,
+                                      uint32_t n_vec, int32_t *sub_dots, int32_t *acc, int32_t *mins,
+                                      float *rows_out, cudaStream_t s);
+cudaError_t lfm_launch_q8_to_gguf(Q8Rows q, uint32_t rows, uint8_t *out, cudaStream_t s);
+cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cudaStream_t s);
+
+/* k_synth.cu */
+cudaError_t lfm_launch_synth_q4k(uint8_t *out, uint64_t n_blocks, uint64_t seed, float stddev, cudaStream_t s);
+cudaError_t lfm_launch_synth_f32(float *out, uint64_t n, uint64_t seed, float mean, float stddev,
+                                 cudaStream_t s);
+
+#endif /* LFM_MOE_INTERNAL_H */

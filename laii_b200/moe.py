@@ -1,0 +1,156 @@
+"""Python host API over the C-ABI of liblfm_gpu_moe.so (include/lfm_gpu_moe.h).
+
+Mirrors the reference's MoE-FFN boundary: ``forward(layer, x)`` is
+``lfm2_forward_moe_ffn_1x4`` (tools/lfm2_moe_checkpoint.c:312) batched over
+the rows of x -- x is updated in place, x += MoE(x) -- and ``upload_layer``
+takes the tensors ``lfm2_bind_moe_layer`` binds (:70-102) in GGUF layout.
+Errors come back as ``MoEError`` carrying the library's status code; there is
+no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import numpy as np
+
+from . import _native
+from .synth import DenseLayer, MoELayer, Q8K_BYTES
+
+GGML_TYPE_Q4_K = 12
+
+STATUS = {0: "OK", -1: "INVALID_ARG", -2: "UNSUPPORTED", -3: "NOT_READY", -4: "OOM", -7: "CUDA", -8: "COMM",
+          -9: "TIMEOUT", -10: "DEVICE_CHECK"}
+
+
+class MoEError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"lfm_gpu_moe status {status} ({STATUS.get(status, '?')}): {message}")
+        self.status = status
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+class GpuMoE:
+    """One handle on one CUDA device (owns weights and scratch in HBM)."""
+
+    def __init__(self, device: int = 0):
+        self._lib = _native.load_gpu()
+        h = ctypes.c_void_p()
+        st = self._lib.lfm_gpu_moe_create(ctypes.byref(h), device)
+        if st != 0:
+            raise MoEError(st, f"cannot create a handle on device {device}")
+        self._h = h
+        self.device = device
+        self.layers = {}
+
+    # -- lifecycle -------------------------------------------------------
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.lfm_gpu_moe_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int):
+        if st != 0:
+            raise MoEError(st, self._lib.lfm_gpu_moe_last_error(self._h).decode(errors="replace"))
+
+    # -- weights ---------------------------------------------------------
+    def upload_layer(self, layer: int, L: MoELayer):
+        keep = [np.ascontiguousarray(a) for a in (L.ffn_norm, L.router_w, L.gate, L.up, L.down)]
+        bias = None if L.bias is None else np.ascontiguousarray(L.bias, dtype=np.float32)
+        self._check(self._lib.lfm_gpu_moe_upload_layer(
+            self._h, layer, L.D, L.E, L.K, L.I, L.eps, _ptr(keep[0]), _ptr(keep[1]), _ptr(bias), _ptr(keep[2]),
+            _ptr(keep[3]), _ptr(keep[4]), GGML_TYPE_Q4_K, int(L.norm_topk_prob), L.routed_scale))
+        self.layers[layer] = ("moe", L.D, L.E, L.K, L.I)
+
+    def upload_dense(self, layer: int, L: DenseLayer):
+        keep = [np.ascontiguousarray(a) for a in (L.ffn_norm, L.gate, L.up, L.down)]
+        self._check(self._lib.lfm_gpu_moe_upload_dense(self._h, layer, L.D, L.I, L.eps, *[_ptr(k) for k in keep],
+                                                       GGML_TYPE_Q4_K))
+        self.layers[layer] = ("dense", L.D, 0, 0, L.I)
+
+    def synth_layer(self, layer: int, D: int, E: int, K: int, I: int, seeds, w_std=0.02, router_std=0.02,
+                    bias_std=0.1, bias: Optional[np.ndarray] = None, eps: float = 1e-5):
+        arr = (ctypes.c_uint64 * 5)(*[int(s) & 0xFFFFFFFFFFFFFFFF for s in seeds])
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._check(self._lib.lfm_gpu_moe_synth_layer(self._h, layer, D, E, K, I, eps, arr, w_std, router_std,
+                                                      bias_std, _ptr(b)))
+        self.layers[layer] = ("moe", D, E, K, I)
+
+    def reserve(self, max_tokens: int):
+        self._check(self._lib.lfm_gpu_moe_reserve(self._h, max_tokens))
+
+    # -- compute ---------------------------------------------------------
+    def forward(self, layer: int, x: np.ndarray) -> np.ndarray:
+        """x[T, D] (host, fp32, C-contiguous) += MoE(x), in place; returns x."""
+        if x.dtype != np.float32 or not x.flags.c_contiguous:
+            raise ValueError("x must be a C-contiguous float32 array")
+        T = x.shape[0] if x.ndim == 2 else 1
+        self._check(self._lib.lfm_gpu_moe_forward(self._h, layer, _ptr(x), T, 0, None))
+        return x
+
+    def forward_stack(self, first: int, n: int, x: np.ndarray) -> np.ndarray:
+        if x.dtype != np.float32 or not x.flags.c_contiguous:
+            raise ValueError("x must be a C-contiguous float32 array")
+        T = x.shape[0] if x.ndim == 2 else 1
+        self._check(self._lib.lfm_gpu_moe_forward_stack(self._h, first, n, _ptr(x), T, 0, None))
+        return x
+
+    def forward_device(self, layer: int, x_dev_ptr: int, T: int, stream: int = 0, n_layers: int = 1):
+        """Asynchronous forward on a device pointer (e.g. a torch tensor's data_ptr())."""
+        self._check(self._lib.lfm_gpu_moe_forward_stack(self._h, layer, n_layers, ctypes.c_void_p(x_dev_ptr), T, 1,
+                                                        ctypes.c_void_p(stream) if stream else None))
+
+    def sync(self):
+        self._check(self._lib.lfm_gpu_moe_sync(self._h))
+
+    def debug_route(self, layer: int, x: np.ndarray) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T, D = x.shape
+        K = self.layers[layer][3]
+        idx = np.zeros((T, K), np.uint32)
+        w = np.zeros((T, K), np.float32)
+        q8 = np.zeros(T * (D // 256) * Q8K_BYTES, np.uint8)
+        self._check(self._lib.lfm_gpu_moe_debug_route(self._h, layer, _ptr(x), T, _ptr(idx), _ptr(w), _ptr(q8)))
+        return idx, w, q8
+
+    def debug_q4k_rows(self, w: np.ndarray, n_rows: int, n_cols: int, xq: np.ndarray, n_vec: int):
+        nb = n_cols // 256
+        sub = np.zeros((n_vec, n_rows, nb, 8), np.int32)
+        acc = np.zeros((n_vec, n_rows, nb), np.int32)
+        mins = np.zeros((n_vec, n_rows, nb), np.int32)
+        out = np.zeros((n_vec, n_rows), np.float32)
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        xq = np.ascontiguousarray(xq, dtype=np.uint8)
+        self._check(self._lib.lfm_gpu_moe_debug_q4k_rows(self._h, _ptr(w), n_rows, n_cols, _ptr(xq), n_vec,
+                                                         _ptr(sub), _ptr(acc), _ptr(mins), _ptr(out)))
+        return sub, acc, mins, out
+
+    def profile(self, enable: bool = True):
+        self._check(self._lib.lfm_gpu_moe_profile(self._h, int(enable)))
+
+    def profile_read(self) -> dict:
+        """{kernel name: (launches, total ms)} since the last read; clears the records."""
+        buf = (_native.KernelTime * 16)()
+        n = ctypes.c_uint32()
+        self._check(self._lib.lfm_gpu_moe_profile_read(self._h, buf, 16, ctypes.byref(n)))
+        return {buf[i].name.decode(): (buf[i].launches, buf[i].total_ms) for i in range(min(n.value, 16))}
+
+    def last_stats(self) -> dict:
+        s = _native.Stats()
+        self._check(self._lib.lfm_gpu_moe_last_stats(self._h, ctypes.byref(s)))
+        return {f: getattr(s, f) for f, _ in _native.Stats._fields_}
