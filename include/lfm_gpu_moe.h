@@ -26,7 +26,7 @@
  *    144-byte Q4_K blocks (tools/lfm2_moe_checkpoint.c:54-58, :110-127).
  *
  * All functions are plain C (no CUDA or torch types); `stream` arguments are a
- * cudaStream_t passed as void* (NULL = the handle's own stream).
+ * cudaStream_t passed as void* (NULL = the CUDA default stream, as in CUDA).
  */
 #ifndef LFM_GPU_MOE_H
 #define LFM_GPU_MOE_H
@@ -130,7 +130,8 @@ lfm_gpu_status_t lfm_gpu_moe_debug_route(lfm_gpu_moe_t *h, uint32_t layer, const
                                          uint32_t *idx_out, float *w_out, void *q8_out);
 
 /* Integer partial sums of the Q4_K x Q8_K kernel used by the expert GEMVs, for
- * parity: host Q4_K rows w[n_rows][n_cols/256] against host Q8_K vectors
+ * parity: host Q4_K rows w[n_rows][n_cols/256] (n_rows a multiple of 8, the
+ * kernel's row group) against host Q8_K vectors
  * xq[n_vec][n_cols/256]; outputs (host) per (vec, row, super-block):
  * sub_dots[..][8] = sum over each 32-weight sub-block of q4*q8,
  * acc = sum_j sc_j*sub_dot_j, mins = sum_j m_j*(bsum pair j), and the fp32 row
@@ -140,6 +141,13 @@ lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void *w, uin
                                             uint32_t n_cols, const void *xq, uint32_t n_vec,
                                             int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                             float *rows_out);
+
+/* Copy tensor `which` of an uploaded layer back to host memory, for checking
+ * uploads and the device generator: 0 ffn_norm, 1 router_w, 2 exp_probs_b,
+ * 3 gate, 4 up, 5 down (`bytes` must equal the tensor's size).  Synchronous.
+ * No counterpart in the reference. */
+lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
+                                              size_t bytes);
 
 /* Wait for all work on the handle's stream and report any device-side error
  * (bounds check or timeout) raised since the last call. */

@@ -44,6 +44,7 @@ GPU_API = [
     ("lfm_gpu_moe_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_int, c_vp]),
     ("lfm_gpu_moe_debug_route", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_debug_q4k_rows", c_int, [c_vp, c_vp, c_u32, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp, c_vp]),
+    ("lfm_gpu_moe_debug_read_layer", c_int, [c_vp, c_u32, c_u32, c_vp, ctypes.c_size_t]),
     ("lfm_gpu_moe_sync", c_int, [c_vp]),
     ("lfm_gpu_moe_last_stats", c_int, [c_vp, ctypes.POINTER(Stats)]),
     ("lfm_gpu_moe_profile", c_int, [c_vp, c_int]),

@@ -1,307 +1,289 @@
 /*
- * K3 grouped Q4_K expert GEMVs (decode / verify path) and K4 combine.
+ * K3 grouped Q4_K expert GEMVs and K4 combine (decode / verify path).
  *
- * Work is grouped by expert: block (e, row tile) streams its rows of expert e
- * once and applies them to every token routed to e (in chunks of 8 tokens
- * whose Q8_K activations are staged in shared memory).  One warp computes one
- * weight row: lane 4*bl + g owns 32 bytes of nibbles (group g = sub-blocks 2g
- * and 2g+1) of super-block 8p + bl, loaded as 128-bit streaming loads, and
- * forms the sub-block dots with __dp4a.  The integer super-block sums
- *   acc = sum_j sc_j * dot_j,  mins = sum_j m_j * (bsum_{2j} + bsum_{2j+1})
- * are exact (any summation order), and the fp32 update per super-block is the
- * reference 4-row AVX-VNNI kernel's, in super-block order:
- *   sum = fma(d8*d, acc, fma(-(d8*dmin), mins, sum))
- * (tools/lfm2_cpuid_quants.c:1189-1257; Q4_K x Q8_K math :421-457).
- *
- * gate|up: h = (g / (1 + exp(-g))) * u per (token, expert, row)
- *   (tools/lfm2_decode_1x4.c:976-985), then k_quant_rows makes Q8_K(h) per 256
- *   (tools/lfm2_cpuid_quants.c:584-631).
- * down: y[slot][r] = Down_e[r] . Q8_K(h_slot).
- * combine: x[t][r] = fma(w_k, y[slot(t,k)][r], x[t][r]) for k = 0..K-1 in
- *   order (tools/lfm2_moe_checkpoint.c:266-269, :338-364).
+ * Work: the dispatch tables list (active expert u, 8-token chunk c) pairs.
+ * Each pair's weight rows are split in items of 8 rows; the flattened list of
+ * (pair, item) is cut into one contiguous range per block of a persistent grid
+ * (one block per SM).  Within a block:
+ *   - a producer warp streams each item's rows (8 gate + 8 up rows for K3a,
+ *     8 down rows for K3b: 1152 B / 1008 B per row at D=2048 / I=1792) into a
+ *     ring of shared-memory stages with 1-D bulk copies (cp.async.bulk on the
+ *     TMA engine, evict-first L2 policy) completing on mbarriers;
+ *   - consumer warp w takes items w, w+8, ... of the block through stages it
+ *     owns (consumed in order); one warp computes a whole item with lfm_q4k_rows8 (4 lanes per row, super-blocks in order,
+ *     exact integer sub-block sums, the reference's fp32 update order), the
+ *     chunk's activations read through the read-only cache;
+ *   - gate|up: h = (g / (1 + exp(-g))) * u   (tools/lfm2_decode_1x4.c:976-985);
+ *   - down: y[slot][r].
+ * k_quant_rows then makes Q8_K(h) per 256 (tools/lfm2_cpuid_quants.c:584-631)
+ * and k_combine applies x[t][r] = fma(w_k, y[slot(t,k)][r], x[t][r]) for
+ * k = 0..K-1 in order (tools/lfm2_moe_checkpoint.c:266-269, :338-364); all
+ * kernels chain with programmatic dependent launch.
+ * Every mbarrier wait is bounded (lfm_mbar_wait); after a timeout the block
+ * stops issuing copies, lets the ones in flight land, and leaves its range
+ * with the device error word set.
  */
 #include "moe_device.cuh"
 #include "moe_internal.h"
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kRowsPerBlock = 64;
-constexpr int kChunk = 8;  /* tokens per staged activation chunk */
+/* gate|up: 8 warp pairs (gate warp + up warp per item); down: 12 warps. */
+template <int kMats> struct GemvShape {
+    static constexpr int kConsumers = kMats == 2 ? 16 : 12;  /* consumer warps */
+    static constexpr int kPerItem = kMats;                    /* warps sharing one item */
+    static constexpr int kThreads = (kConsumers + 1) * 32;
+};
+constexpr int kRows = LFM_GEMV_ROWS; /* rows per item (8) */
+constexpr int kCh = LFM_GEMV_CHUNK;
+constexpr int kMaxStages = 32;
 
-struct ActView {
-    const int8_t *qs;    /* [kChunk][cols] */
-    const float *d;      /* [kChunk][nb]   */
-    const int16_t *bs;   /* [kChunk][nb][16] */
-    uint32_t cols, nb;
+__device__ __forceinline__ int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
+struct GemvShared {
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
+    float gx[8][kRows][kCh]; /* gate results handed from the gate warp to the up warp of a pair */
+    int pair_ok[8][2];        /* per-pair go/no-go, written only by that pair's two warps */
+    int abort;
 };
 
-/* Per-warp scratch used to hand the 8 per-super-block integer sums of each
- * token to the lane that runs that token's fp32 chain. */
-struct WarpXfer {
-    int2 ints[kChunk][8];
-    float2 scales[8];
+struct GemvArgs {
+    MoeLayerDev L;
+    Q8Rows act;        /* activation rows: xq (token-indexed) or hq (slot-indexed) */
+    RouteTables rt;
+    float *out;        /* h [slots][I] or y [slots][D] */
+    uint32_t stages;   /* stages in use = lanes_of_work * depth */
+    uint32_t groups;   /* active consumer groups (warp pairs for gate|up, warps for down) */
 };
 
-struct RowDebug {
-    int32_t *sub_dots;  /* [nb][8] for the current (vec,row) or NULL */
-    int32_t *acc;       /* [nb] */
-    int32_t *mins;      /* [nb] */
-};
+template <int kMats>
+__global__ void __launch_bounds__(GemvShape<kMats>::kThreads, 1) k_gemv(GemvArgs A) {
+    using Sh = GemvShape<kMats>;
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ GemvShared sh;
+    const MoeLayerDev &L = A.L;
+    const uint32_t rows_total = kMats == 2 ? L.I : L.D;
+    const uint32_t cols = kMats == 2 ? L.D : L.I;
+    const uint32_t nb = cols / 256;
+    const uint32_t row_bytes = nb * LFM_Q4K_BYTES;
+    const uint32_t rs = lfm_stage_stride(row_bytes);
+    const uint32_t stage_bytes = kMats * kRows * rs;
+    const uint32_t G = A.groups;          /* consumer groups in use */
+    const uint32_t depth = A.stages / G;  /* private stages per group */
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t K = lfm_layer_K(L);
 
-/* Dot of one Q4_K row with nt (<= kChunk) staged Q8_K activation rows.
- * Returns, in lane t < nt, the fp32 result for token t. */
-template <bool kDebug>
-__device__ __forceinline__ float q4k_row_dot(const uint8_t *__restrict__ row, const ActView &a, int nt,
-                                             WarpXfer &xf, RowDebug dbg) {
-    const int lane = threadIdx.x & 31;
-    const int bl = lane >> 2, g = lane & 3;
-    float sum = 0.0f;
-    for (uint32_t p = 0; p * 8 < a.nb; ++p) {
-        const uint32_t b = p * 8 + bl;
-        const bool valid = b < a.nb;
-        uint4 hdr = make_uint4(0, 0, 0, 0), q0 = hdr, q1 = hdr;
-        if (valid) {
-            const uint8_t *blk = row + (size_t)b * LFM_Q4K_BYTES;
-            hdr = lfm_ldg_stream(blk);
-            q0 = lfm_ldg_stream(blk + 16 + 32 * g);
-            q1 = lfm_ldg_stream(blk + 32 + 32 * g);
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < A.stages; ++s) {
+            lfm_mbar_init(&sh.full[s], 1);
+            lfm_mbar_init(&sh.empty[s], 1);
         }
-        int sc_lo, m_lo, sc_hi, m_hi;
-        lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc_lo, m_lo, sc_hi, m_hi);
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        if (g == 0 && valid)
-            xf.scales[bl] = make_float2(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu)), lfm_h2f((uint16_t)(hdr.x >> 16)));
-        for (int t = 0; t < nt; ++t) {
-            int acc = 0, mins = 0;
-            if (valid) {
-                const uint4 *q8 = reinterpret_cast<const uint4 *>(a.qs + (size_t)t * a.cols + 256 * b + 64 * g);
-                const uint4 x0 = q8[0], x1 = q8[1], x2 = q8[2], x3 = q8[3];
-                const int xl[8] = {(int)x0.x, (int)x0.y, (int)x0.z, (int)x0.w, (int)x1.x, (int)x1.y, (int)x1.z, (int)x1.w};
-                const int xh[8] = {(int)x2.x, (int)x2.y, (int)x2.z, (int)x2.w, (int)x3.x, (int)x3.y, (int)x3.z, (int)x3.w};
-                int dlo = 0, dhi = 0;
+        sh.abort = 0;
+        lfm_fence_mbar_init();
+    }
+    __syncthreads();
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* routing tables and activations come from the preceding kernels */
+
+    const uint32_t gpp = rows_total / kRows; /* items per (expert, chunk) pair */
+    const uint64_t n_items = (uint64_t)__ldcg(A.rt.summary + 3) * gpp;
+    const uint64_t i0 = n_items * blockIdx.x / gridDim.x;
+    const uint64_t i1 = n_items * (blockIdx.x + 1) / gridDim.x;
+    const uint8_t *W0 = kMats == 2 ? L.gate : L.down;
+    const uint8_t *W1 = L.up;
+
+    /* Stage ownership: local item k belongs to group k%G, which owns stages
+     * (k%G)*depth .. +depth-1 and consumes them strictly in order, so no wait
+     * can target a phase two ahead of a barrier (parity waits would alias). */
+    auto stage_of = [&](uint64_t k, uint32_t &ph) -> uint32_t {
+        const uint64_t q = k / G;
+        ph = (uint32_t)(q / depth);
+        return (uint32_t)(k % G) * depth + (uint32_t)(q % depth);
+    };
+
+    if (warp == Sh::kConsumers) {
+        /* ---------------- producer ---------------- */
+        if (lane == 0) {
+            const uint64_t policy = lfm_policy_evict_first();
+            uint64_t k = 0, pj = ~0ull;
+            int e = 0;
+            for (uint64_t i = i0; i < i1; ++i, ++k) {
+                if (i / gpp != pj) { /* the expert changes once per gpp items */
+                    pj = i / gpp;
+                    e = __ldcg(A.rt.act + __ldcg(A.rt.pairs + pj).x);
+                }
+                uint32_t ph;
+                const uint32_t s = stage_of(k, ph);
+                if (ph >= 1 && !lfm_mbar_wait(&sh.empty[s], (ph - 1) & 1u, A.rt.err)) {
+                    atomicExch(&sh.abort, 1);
+                    break;
+                }
+                if (ld_volatile(&sh.abort)) break;
+                const size_t row0 = (size_t)e * rows_total + (size_t)(i % gpp) * kRows;
+                uint8_t *dst = dsm + (size_t)s * stage_bytes;
+                lfm_mbar_arrive_tx(&sh.full[s], kMats * kRows * row_bytes);
+                for (int m = 0; m < kMats; ++m) {
+                    const uint8_t *src = (m == 0 ? W0 : W1) + row0 * row_bytes;
+                    uint8_t *d = dst + (size_t)m * kRows * rs;
+                    if (rs == row_bytes) {
+                        lfm_bulk_g2s(d, src, kRows * row_bytes, &sh.full[s], policy);
+                    } else {
+                        for (int r = 0; r < kRows; ++r)
+                            lfm_bulk_g2s(d + (size_t)r * rs, src + (size_t)r * row_bytes, row_bytes, &sh.full[s], policy);
+                    }
+                }
+            }
+            /* leave no copy in flight into this block's shared memory: the last
+             * G*depth items issued cover every stage's newest phase */
+            const uint64_t span = (uint64_t)G * depth;
+            for (uint64_t q = k > span ? k - span : 0; q < k; ++q) {
+                uint32_t ph;
+                const uint32_t s = stage_of(q, ph);
+                lfm_mbar_wait(&sh.full[s], ph & 1u, A.rt.err);
+            }
+        }
+        return;
+    }
+
+    /* ---------------- consumers ---------------- */
+    const uint32_t grp = (uint32_t)warp / Sh::kPerItem;  /* consumer group */
+    const int mat = warp % Sh::kPerItem;                  /* gate|up: 0 gate, 1 up */
+    if (grp >= G) return;
+    const int r = lane >> 2, g = lane & 3;
+    int64_t cur_pair = -1;
+    int rows[kCh];
+    int nt = 0, slot0 = 0;
+    for (uint64_t k = grp, i = i0 + grp; i < i1; k += G, i += G) {
+        const int64_t j = (int64_t)(i / gpp);
+        if (j != cur_pair) {
+            const int2 pr = __ldcg(A.rt.pairs + j);
+            const uint32_t e = (uint32_t)__ldcg(A.rt.act + pr.x);
+            const uint32_t n_e = (uint32_t)__ldcg(A.rt.counts + e);
+            const uint32_t off_e = (uint32_t)__ldcg(A.rt.offsets + e);
+            slot0 = (int)off_e + pr.y * kCh;
+            nt = min(kCh, (int)n_e - pr.y * kCh);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    dlo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), xl[i], dlo);
-                    dhi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), xh[i], dhi);
+            for (int t = 0; t < kCh; ++t)
+                rows[t] = t < nt ? (kMats == 2 ? __ldcg(A.rt.perm + slot0 + t) / (int)K : slot0 + t) : 0;
+            cur_pair = j;
+        }
+        uint32_t ph;
+        const uint32_t s = stage_of(k, ph);
+        bool ok = !ld_volatile(&sh.abort) && lfm_mbar_wait(&sh.full[s], ph & 1u, A.rt.err);
+        ok = __all_sync(LFM_FULL_MASK, ok); /* the row dots shuffle across the whole warp */
+        if (kMats == 2) {
+            /* both warps of the pair decide together from slots only they write,
+             * so they always take the same number of pair barriers */
+            if (lane == 0) sh.pair_ok[grp][mat] = ok ? 1 : 0;
+            lfm_bar_sync(1 + (int)grp, 64);
+            ok = sh.pair_ok[grp][0] && sh.pair_ok[grp][1];
+            lfm_bar_sync(1 + (int)grp, 64); /* both read the slots before either rewrites them */
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(&sh.abort, 1);
+            break;
+        }
+        const uint8_t *st = dsm + (size_t)s * stage_bytes + (size_t)mat * kRows * rs;
+        const uint32_t row0 = (uint32_t)(i % gpp) * kRows;
+        float s0[kCh], s1[kCh];
+        lfm_q4k_rows8<1, false>(st, nullptr, rs, nb, A.act, rows, nt, s0, s1, RowDebug{});
+        if (kMats == 2) {
+            if (mat == 0) {
+#pragma unroll
+                for (int t = 0; t < kCh; ++t)
+                    if ((t & 3) == g && t < nt) sh.gx[grp][r][t] = s0[t];
+            }
+            lfm_bar_sync(1 + (int)grp, 64); /* gate results visible; both warps done reading the stage */
+            if (mat == 1) {
+                if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
+#pragma unroll
+                for (int t = 0; t < kCh; ++t) {
+                    if ((t & 3) == g && t < nt) {
+                        const float gv = sh.gx[grp][r][t];
+                        const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, lfm_expf(-gv)));
+                        A.out[(size_t)(slot0 + t) * L.I + row0 + r] = __fmul_rn(silu, s0[t]);
+                    }
                 }
-                const int16_t *bsp = a.bs + ((size_t)t * a.nb + b) * 16 + 4 * g;
-                const uint2 bw = *reinterpret_cast<const uint2 *>(bsp);
-                const int b0 = (int)(int16_t)(bw.x & 0xFFFFu), b1 = (int)(int16_t)(bw.x >> 16);
-                const int b2 = (int)(int16_t)(bw.y & 0xFFFFu), b3 = (int)(int16_t)(bw.y >> 16);
-                acc = sc_lo * dlo + sc_hi * dhi;
-                mins = m_lo * (b0 + b1) + m_hi * (b2 + b3);
-                if (kDebug && dbg.sub_dots) {
-                    dbg.sub_dots[b * 8 + 2 * g] = dlo;
-                    dbg.sub_dots[b * 8 + 2 * g + 1] = dhi;
-                }
             }
-            acc += __shfl_xor_sync(LFM_FULL_MASK, acc, 1);
-            acc += __shfl_xor_sync(LFM_FULL_MASK, acc, 2);
-            mins += __shfl_xor_sync(LFM_FULL_MASK, mins, 1);
-            mins += __shfl_xor_sync(LFM_FULL_MASK, mins, 2);
-            if (g == 0 && valid) {
-                xf.ints[t][bl] = make_int2(acc, mins);
-                if (kDebug && dbg.acc) { dbg.acc[b] = acc; dbg.mins[b] = mins; }
-            }
-        }
-        __syncwarp();
-        if (lane < nt) {
-            const uint32_t nbl = min(8u, a.nb - p * 8);
-            for (uint32_t j = 0; j < nbl; ++j) {
-                const uint32_t bb = p * 8 + j;
-                const float d8 = a.d[(size_t)lane * a.nb + bb];
-                if (d8 == 0.0f) continue;
-                const int2 v = xf.ints[lane][j];
-                const float2 sc = xf.scales[j];
-                const float dd = __fmul_rn(d8, sc.x);
-                const float dm = __fmul_rn(d8, sc.y);
-                sum = __fmaf_rn(dd, (float)v.x, __fmaf_rn(-dm, (float)v.y, sum));
-            }
-        }
-        __syncwarp();
-    }
-    return sum;
-}
-
-/* Stage the Q8_K rows of nt tokens into shared memory (16-byte copies). */
-__device__ void stage_rows(Q8Rows src, const int *rows, int nt, uint32_t nb, int8_t *sqs, float *sd,
-                           int16_t *sbs) {
-    const uint32_t cols = src.cols;
-    const uint32_t qv = cols / 16, bv = nb * 2;  /* uint4 per row: qs, bsums */
-    for (uint32_t i = threadIdx.x; i < (uint32_t)nt * qv; i += blockDim.x) {
-        const uint32_t t = i / qv, c = i % qv;
-        reinterpret_cast<uint4 *>(sqs + (size_t)t * cols)[c] =
-            reinterpret_cast<const uint4 *>(src.qs + (size_t)rows[t] * cols)[c];
-    }
-    for (uint32_t i = threadIdx.x; i < (uint32_t)nt * bv; i += blockDim.x) {
-        const uint32_t t = i / bv, c = i % bv;
-        reinterpret_cast<uint4 *>(sbs + (size_t)t * nb * 16)[c] =
-            reinterpret_cast<const uint4 *>(src.bs + (size_t)rows[t] * nb * 16)[c];
-    }
-    for (uint32_t i = threadIdx.x; i < (uint32_t)nt * nb; i += blockDim.x) {
-        const uint32_t t = i / nb, c = i % nb;
-        sd[(size_t)t * nb + c] = src.d[(size_t)rows[t] * nb + c];
-    }
-}
-
-__host__ __device__ constexpr size_t act_smem_bytes(uint32_t cols) {
-    return (size_t)kChunk * cols + (size_t)kChunk * (cols / 256) * 32 + (size_t)kChunk * (cols / 256) * 4;
-}
-
-__global__ void __launch_bounds__(kThreads) k_gateup(MoeLayerDev L, Q8Rows xq, RouteTables rt,
-                                                     float *__restrict__ h) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ WarpXfer xfer[kWarps];
-    __shared__ int tok[kChunk];
-    const uint32_t e = blockIdx.x;
-    const int n = rt.counts[e];
-    if (n == 0) return;
-    const int base = rt.offsets[e];
-    const uint32_t D = L.D, I = L.I, nb = D / 256;
-    const uint32_t r0 = blockIdx.y * kRowsPerBlock;
-    const uint32_t r1 = min(I, r0 + kRowsPerBlock);
-    int8_t *sqs = reinterpret_cast<int8_t *>(smem);
-    int16_t *sbs = reinterpret_cast<int16_t *>(smem + (size_t)kChunk * D);
-    float *sd = reinterpret_cast<float *>(smem + (size_t)kChunk * D + (size_t)kChunk * nb * 32);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t row_bytes = (size_t)nb * LFM_Q4K_BYTES;
-    const uint8_t *G = L.gate + (size_t)e * I * row_bytes;
-    const uint8_t *U = L.up + (size_t)e * I * row_bytes;
-    const ActView av{sqs, sd, sbs, D, nb};
-    for (int c0 = 0; c0 < n; c0 += kChunk) {
-        const int nt = min(kChunk, n - c0);
-        __syncthreads();
-        if (threadIdx.x < nt) tok[threadIdx.x] = rt.perm[base + c0 + threadIdx.x] / (int)L.K;
-        __syncthreads();
-        stage_rows(xq, tok, nt, nb, sqs, sd, sbs);
-        __syncthreads();
-        for (uint32_t r = r0 + warp; r < r1; r += kWarps) {
-            const float gv = q4k_row_dot<false>(G + (size_t)r * row_bytes, av, nt, xfer[warp], RowDebug{});
-            const float uv = q4k_row_dot<false>(U + (size_t)r * row_bytes, av, nt, xfer[warp], RowDebug{});
-            if (lane < nt) {
-                const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, lfm_expf(-gv)));
-                h[(size_t)(base + c0 + lane) * I + r] = __fmul_rn(silu, uv);
-            }
+        } else {
+            __syncwarp();
+            if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
+#pragma unroll
+            for (int t = 0; t < kCh; ++t)
+                if ((t & 3) == g && t < nt) A.out[(size_t)(slot0 + t) * L.D + row0 + r] = s0[t];
         }
     }
 }
 
-__global__ void __launch_bounds__(kThreads) k_down(MoeLayerDev L, Q8Rows hq, RouteTables rt,
-                                                   float *__restrict__ y) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ WarpXfer xfer[kWarps];
-    __shared__ int slot[kChunk];
-    const uint32_t e = blockIdx.x;
-    const int n = rt.counts[e];
-    if (n == 0) return;
-    const int base = rt.offsets[e];
-    const uint32_t D = L.D, I = L.I, nb = I / 256;
-    const uint32_t r0 = blockIdx.y * kRowsPerBlock;
-    const uint32_t r1 = min(D, r0 + kRowsPerBlock);
-    int8_t *sqs = reinterpret_cast<int8_t *>(smem);
-    int16_t *sbs = reinterpret_cast<int16_t *>(smem + (size_t)kChunk * I);
-    float *sd = reinterpret_cast<float *>(smem + (size_t)kChunk * I + (size_t)kChunk * nb * 32);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t row_bytes = (size_t)nb * LFM_Q4K_BYTES;
-    const uint8_t *W = L.down + (size_t)e * D * row_bytes;
-    const ActView av{sqs, sd, sbs, I, nb};
-    for (int c0 = 0; c0 < n; c0 += kChunk) {
-        const int nt = min(kChunk, n - c0);
-        __syncthreads();
-        if (threadIdx.x < nt) slot[threadIdx.x] = base + c0 + threadIdx.x;
-        __syncthreads();
-        stage_rows(hq, slot, nt, nb, sqs, sd, sbs);
-        __syncthreads();
-        for (uint32_t r = r0 + warp; r < r1; r += kWarps) {
-            const float v = q4k_row_dot<false>(W + (size_t)r * row_bytes, av, nt, xfer[warp], RowDebug{});
-            if (lane < nt) y[(size_t)(base + c0 + lane) * D + r] = v;
-        }
-    }
-}
-
-/* Q8_K of fp32 rows: one warp per 256-element block, 8 elements per lane
- * (d = max/127, q = RNE(x*(127/max)), bsums of unsaturated codes). */
-__global__ void __launch_bounds__(kThreads) k_quant_rows(const float *__restrict__ src, uint32_t rows,
-                                                         uint32_t cols, Q8Rows dst) {
+/* Q8_K of fp32 rows: one warp per 256-element block. */
+__global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ src, uint32_t rows, uint32_t cols,
+                                                    Q8Rows dst) {
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait();
     const uint32_t nb = cols / 256;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t gw = blockIdx.x * kWarps + warp;
+    const uint32_t gw = blockIdx.x * 8 + warp;
     if (gw >= rows * nb) return;
     const uint32_t r = gw / nb, b = gw % nb;
     const float4 *p = reinterpret_cast<const float4 *>(src + (size_t)r * cols + 256 * b + 8 * lane);
-    const float4 a0 = p[0], a1 = p[1];
+    const float4 a0 = __ldcg(p), a1 = __ldcg(p + 1);
     const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = lfm_warp_max(amax);
-    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    int part = 0;
-    if (amax != 0.0f) {
-        const float s = __fdiv_rn(127.0f, amax);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { q[i] = __float2int_rn(__fmul_rn(v[i], s)); part += q[i]; }
-    }
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        lo |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[i])) << (8 * i);
-        hi |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[4 + i])) << (8 * i);
-    }
-    *reinterpret_cast<uint2 *>(dst.qs + (size_t)r * cols + 256 * b + 8 * lane) = make_uint2(lo, hi);
-    const int pair = part + __shfl_xor_sync(LFM_FULL_MASK, part, 1);
-    if ((lane & 1) == 0) dst.bs[((size_t)r * nb + b) * 16 + (lane >> 1)] = (int16_t)pair;
-    if (lane == 0) dst.d[(size_t)r * nb + b] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
+    lfm_quant_block_warp(v, dst, r, b);
 }
 
-__global__ void __launch_bounds__(256) k_combine(float *__restrict__ x, uint32_t D, uint32_t K, RouteTables rt,
+/* Combine: x[t][r] = fma chain over k in order.  Block (rb, t) covers 4
+ * consecutive columns per thread (float4); all K loads are issued first. */
+__global__ void __launch_bounds__(128) k_combine(float *__restrict__ x, uint32_t D, uint32_t K, RouteTables rt,
                                                  const float *__restrict__ y) {
-    const uint32_t t = blockIdx.x;
-    __shared__ int s_slot[LFM_GPU_MAX_TOPK_DEV];
-    __shared__ float s_w[LFM_GPU_MAX_TOPK_DEV];
-    if (threadIdx.x < K) {
-        s_slot[threadIdx.x] = rt.inv[(size_t)t * K + threadIdx.x];
-        s_w[threadIdx.x] = rt.w[(size_t)t * K + threadIdx.x];
-    }
-    __syncthreads();
-    float *xt = x + (size_t)t * D;
-    for (uint32_t r = threadIdx.x; r < D; r += blockDim.x) {
-        float v = xt[r];
-        for (uint32_t k = 0; k < K; ++k) {
-            const int s = s_slot[k];
-            if (s >= 0) v = __fmaf_rn(s_w[k], y[(size_t)s * D + r], v);
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait();
+    const uint32_t t = blockIdx.y;
+    const uint32_t r = (blockIdx.x * 128 + threadIdx.x) * 4;
+    if (r >= D) return;
+    int sl[LFM_GPU_MAX_TOPK_DEV];
+    float wk[LFM_GPU_MAX_TOPK_DEV];
+    float4 yv[LFM_GPU_MAX_TOPK_DEV];
+#pragma unroll
+    for (int k = 0; k < LFM_GPU_MAX_TOPK_DEV; ++k) {
+        if (k < (int)K) {
+            sl[k] = __ldcg(rt.inv + (size_t)t * K + k);
+            wk[k] = __ldcg(rt.w + (size_t)t * K + k);
         }
-        xt[r] = v;
     }
+#pragma unroll
+    for (int k = 0; k < LFM_GPU_MAX_TOPK_DEV; ++k)
+        if (k < (int)K && sl[k] >= 0) yv[k] = __ldcg(reinterpret_cast<const float4 *>(y + (size_t)sl[k] * D + r));
+    float4 v = *reinterpret_cast<float4 *>(x + (size_t)t * D + r);
+#pragma unroll
+    for (int k = 0; k < LFM_GPU_MAX_TOPK_DEV; ++k) {
+        if (k < (int)K && sl[k] >= 0) {
+            v.x = __fmaf_rn(wk[k], yv[k].x, v.x);
+            v.y = __fmaf_rn(wk[k], yv[k].y, v.y);
+            v.z = __fmaf_rn(wk[k], yv[k].z, v.z);
+            v.w = __fmaf_rn(wk[k], yv[k].w, v.w);
+        }
+    }
+    *reinterpret_cast<float4 *>(x + (size_t)t * D + r) = v;
 }
 
-/* Debug: every (vector, row) pair through q4k_row_dot with its integer parts. */
-__global__ void __launch_bounds__(kThreads) k_debug_rows(const uint8_t *__restrict__ w, uint32_t n_rows,
-                                                         uint32_t n_cols, Q8Rows xq, uint32_t n_vec,
-                                                         int32_t *sub_dots, int32_t *acc, int32_t *mins,
-                                                         float *rows_out) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ WarpXfer xfer[kWarps];
-    __shared__ int vrow[1];
+/* Debug: every (vector, 8-row block) through lfm_q4k_rows8 with its integer parts. */
+__global__ void __launch_bounds__(256) k_debug_rows(const uint8_t *__restrict__ w, uint32_t n_rows, uint32_t n_cols,
+                                                    Q8Rows xq, int32_t *sub_dots, int32_t *acc, int32_t *mins,
+                                                    float *rows_out) {
     const uint32_t nb = n_cols / 256;
     const uint32_t v = blockIdx.x;
-    int8_t *sqs = reinterpret_cast<int8_t *>(smem);
-    int16_t *sbs = reinterpret_cast<int16_t *>(smem + (size_t)kChunk * n_cols);
-    float *sd = reinterpret_cast<float *>(smem + (size_t)kChunk * n_cols + (size_t)kChunk * nb * 32);
-    if (threadIdx.x == 0) vrow[0] = (int)v;
-    __syncthreads();
-    stage_rows(xq, vrow, 1, nb, sqs, sd, sbs);
-    __syncthreads();
-    const ActView av{sqs, sd, sbs, n_cols, nb};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t row_bytes = (size_t)nb * LFM_Q4K_BYTES;
-    for (uint32_t r = blockIdx.y * kWarps + warp; r < n_rows; r += gridDim.y * kWarps) {
-        const size_t o = (size_t)v * n_rows + r;
+    int rows[kCh];
+#pragma unroll
+    for (int t = 0; t < kCh; ++t) rows[t] = (int)v;
+    for (uint32_t rb = (blockIdx.y * 8 + warp) * kRows; rb < n_rows; rb += gridDim.y * 8 * kRows) {
+        const size_t o = (size_t)v * n_rows + rb;
         RowDebug dbg{sub_dots + o * nb * 8, acc + o * nb, mins + o * nb};
-        const float s = q4k_row_dot<true>(w + r * row_bytes, av, 1, xfer[warp], dbg);
-        if (lane == 0) rows_out[o] = s;
+        float s0[kCh], s1[kCh];
+        lfm_q4k_rows8<1, true>(w + rb * row_bytes, nullptr, (uint32_t)row_bytes, nb, xq, rows, 1, s0, s1, dbg);
+        if ((lane & 3) == 0) rows_out[o + (lane >> 2)] = s0[0];
     }
 }
 
@@ -342,57 +324,100 @@ __global__ void k_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q) {
     }
 }
 
-cudaError_t set_smem(const void *fn, size_t bytes) {
-    if (bytes <= 48 * 1024) return cudaSuccess;
-    return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+cudaError_t launch_ex(const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, void **args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+constexpr size_t kSmemBudget = 220 * 1024;
+
+/* Consumer groups and stages: as many groups as stages allow (at most the
+ * kernel's), then a whole number of private stages per group. */
+void gemv_plan(uint32_t cols, uint32_t mats, uint32_t &groups, uint32_t &stages) {
+    const size_t stage = (size_t)mats * kRows * lfm_stage_stride(cols / 256 * LFM_Q4K_BYTES);
+    size_t n = (kSmemBudget - sizeof(GemvShared) - 1024) / stage;
+    if (n > kMaxStages) n = kMaxStages;
+    const uint32_t gmax = mats == 2 ? (uint32_t)GemvShape<2>::kConsumers / 2 : (uint32_t)GemvShape<1>::kConsumers;
+    groups = (uint32_t)(n < gmax ? n : gmax);
+    stages = groups ? (uint32_t)(n / groups * groups) : 0;
 }
 
 }  // namespace
 
-cudaError_t lfm_launch_gateup(const MoeLayerDev &L, uint32_t T, Q8Rows xq, const RouteTables &rt, float *h,
-                              cudaStream_t s) {
-    (void)T;
-    const size_t smem = act_smem_bytes(L.D);
-    cudaError_t e = set_smem((const void *)k_gateup, smem);
+/* Raise a kernel's dynamic shared-memory limit once per device (host side). */
+cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const dim3 grid(L.E, (L.I + kRowsPerBlock - 1) / kRowsPerBlock);
-    k_gateup<<<grid, kThreads, smem, s>>>(L, xq, rt, h);
-    return cudaGetLastError();
+    size_t &c = cache16[dev & 15];
+    if (smem <= c) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) c = smem;
+    return e;
 }
 
-cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s) {
+size_t lfm_gemv_smem(uint32_t cols, uint32_t mats) {
+    uint32_t groups, stages;
+    gemv_plan(cols, mats, groups, stages);
+    return (size_t)stages * mats * kRows * lfm_stage_stride(cols / 256 * LFM_Q4K_BYTES);
+}
+
+static cudaError_t launch_gemv(const void *fn, uint32_t cols, uint32_t mats, GemvArgs &a, int grid, cudaStream_t s,
+                               bool pdl) {
+    static size_t cache[2][16];
+    gemv_plan(cols, mats, a.groups, a.stages);
+    if (a.groups == 0) return cudaErrorInvalidValue;
+    const size_t smem = lfm_gemv_smem(cols, mats);
+    cudaError_t e = lfm_smem_attr(fn, smem, cache[mats - 1]);
+    if (e != cudaSuccess) return e;
+    void *args[] = {&a};
+    const int threads = mats == 2 ? GemvShape<2>::kThreads : GemvShape<1>::kThreads;
+    return launch_ex(fn, dim3(grid), dim3(threads), smem, s, pdl, args);
+}
+
+cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables &rt, float *h, int grid,
+                              cudaStream_t s, bool pdl) {
+    GemvArgs a{L, xq, rt, h, 0, 0};
+    return launch_gemv((const void *)k_gemv<2>, L.D, 2, a, grid, s, pdl);
+}
+
+cudaError_t lfm_launch_down(const MoeLayerDev &L, Q8Rows hq, const RouteTables &rt, float *y, int grid,
+                            cudaStream_t s, bool pdl) {
+    GemvArgs a{L, hq, rt, y, 0, 0};
+    return launch_gemv((const void *)k_gemv<1>, L.I, 1, a, grid, s, pdl);
+}
+
+cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s, bool pdl) {
     if (rows == 0) return cudaSuccess;
     const uint32_t warps = rows * (cols / 256);
-    k_quant_rows<<<(warps + kWarps - 1) / kWarps, kThreads, 0, s>>>(h, rows, cols, hq);
-    return cudaGetLastError();
-}
-
-cudaError_t lfm_launch_down(const MoeLayerDev &L, uint32_t T, Q8Rows hq, const RouteTables &rt, float *y,
-                            cudaStream_t s) {
-    (void)T;
-    const size_t smem = act_smem_bytes(L.I);
-    cudaError_t e = set_smem((const void *)k_down, smem);
-    if (e != cudaSuccess) return e;
-    const dim3 grid(L.E, (L.D + kRowsPerBlock - 1) / kRowsPerBlock);
-    k_down<<<grid, kThreads, smem, s>>>(L, hq, rt, y);
-    return cudaGetLastError();
+    void *args[] = {(void *)&h, &rows, &cols, &hq};
+    return launch_ex((const void *)k_quant_rows, dim3((warps + 7) / 8), dim3(256), 0, s, pdl, args);
 }
 
 cudaError_t lfm_launch_combine(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, const float *y,
-                               cudaStream_t s) {
+                               cudaStream_t s, bool pdl) {
     if (T == 0) return cudaSuccess;
-    k_combine<<<T, 256, 0, s>>>(x, L.D, L.K, rt, y);
-    return cudaGetLastError();
+    uint32_t D = L.D, K = lfm_layer_K(L);
+    RouteTables r = rt;
+    void *args[] = {&x, &D, &K, &r, (void *)&y};
+    return launch_ex((const void *)k_combine, dim3((D / 4 + 127) / 128, T), dim3(128), 0, s, pdl, args);
 }
 
 cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_t n_cols, Q8Rows xq,
                                       uint32_t n_vec, int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                       float *rows_out, cudaStream_t s) {
-    const size_t smem = act_smem_bytes(n_cols);
-    cudaError_t e = set_smem((const void *)k_debug_rows, smem);
-    if (e != cudaSuccess) return e;
-    const uint32_t gy = min(64u, (n_rows + kWarps - 1) / kWarps);
-    k_debug_rows<<<dim3(n_vec, gy), kThreads, smem, s>>>(w, n_rows, n_cols, xq, n_vec, sub_dots, acc, mins, rows_out);
+    if (n_rows % kRows) return cudaErrorInvalidValue;
+    const uint32_t gy = min(64u, (n_rows / kRows + 7) / 8);
+    k_debug_rows<<<dim3(n_vec, gy), 256, 0, s>>>(w, n_rows, n_cols, xq, sub_dots, acc, mins, rows_out);
     return cudaGetLastError();
 }
 

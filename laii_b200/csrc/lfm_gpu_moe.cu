@@ -15,7 +15,7 @@
 
 #include <vector>
 
-#include "../../include/lfm_gpu_moe.h"
+#include "lfm_gpu_moe.h"
 #include "moe_internal.h"
 
 #define LFM_API extern "C" __attribute__((visibility("default")))
@@ -26,12 +26,14 @@ struct LayerSlot {
     bool present = false;
     MoeLayerDev dev{};
     void *bufs[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t sizes[7] = {0, 0, 0, 0, 0, 0, 0};
 };
 
 struct Workspace {
     uint32_t T = 0, D = 0, E = 0, K = 0, I = 0;
     void *base = nullptr;
     size_t bytes = 0;
+    size_t counters_bytes = 0; /* leading zero-kept counter region      */
     float *x = nullptr;       /* [T][D] staging for host x            */
     Q8Rows xq{};              /* [T] x D                              */
     RouteTables rt{};
@@ -43,13 +45,20 @@ struct Workspace {
 }  // namespace
 
 namespace {
-enum KernelId { K_ROUTE, K_DISPATCH, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_DENSE_TABLES, K_COUNT };
-const char *const kKernelNames[K_COUNT] = {"route", "dispatch", "gateup", "quant_h", "down", "combine",
-                                           "dense_tables"};
+enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_COUNT };
+const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
 };
+/* One captured forward: layers [first, first+n) on x for T tokens. */
+struct GraphEntry {
+    uint32_t first, n, T;
+    float *x;
+    uint32_t kernels;
+    cudaGraphExec_t exec;
+};
+constexpr size_t kMaxGraphs = 64;
 }  // namespace
 
 struct lfm_gpu_moe {
@@ -59,12 +68,13 @@ struct lfm_gpu_moe {
     LayerSlot layers[LFM_GPU_MOE_MAX_LAYERS];
     Workspace ws;
     uint32_t *dev_err = nullptr;  /* device error word, zeroed at creation */
-    uint32_t *tok_count = nullptr;
-    uint32_t tok_count_cap = 0;
+    int sm_count = 148;
     unsigned long long *loads = nullptr;  /* device [2]: expert loads, MoE layer runs */
     lfm_gpu_moe_stats_t stats{};
     bool prof = false;
     std::vector<ProfRec> recs;
+    bool use_graphs = true;
+    std::vector<GraphEntry> graphs;
 };
 
 namespace {
@@ -107,13 +117,23 @@ void free_layer(LayerSlot &L) {
         if (p) cudaFree(p);
         p = nullptr;
     }
+    for (size_t &z : L.sizes) z = 0;
     L.present = false;
     L.dev = MoeLayerDev{};
 }
 
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-/* Make sure the workspace covers T tokens for the given layer shape. */
+/* Captured forwards hold device pointers (weights, workspace, x): drop them
+ * whenever one of those can change. */
+void drop_graphs(lfm_gpu_moe_t *h) {
+    for (GraphEntry &g : h->graphs) cudaGraphExecDestroy(g.exec);
+    h->graphs.clear();
+}
+
+/* Make sure the workspace covers T tokens for the given layer shape.  The
+ * completion counters (tok_count, done) live in one zeroed
+ * region; kernels return every counter to zero when they finish with it. */
 lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint32_t E, uint32_t K, uint32_t I) {
     Workspace &w = h->ws;
     if (w.base && T <= w.T && D <= w.D && E <= w.E && K <= w.K && I <= w.I) return LFM_GPU_OK;
@@ -122,8 +142,13 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     if (E < 1) E = 1;
     if (K < 1) K = 1;
     const size_t TK = (size_t)T * K;
+    const size_t n_pairs = E + (TK + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    /* counters first: one memset covers them */
+    const size_t o_tc = take(sizeof(uint32_t) * T);
+    const size_t o_done = take(sizeof(uint32_t));
+    const size_t counters_end = off;
     const size_t o_x = take(sizeof(float) * T * D);
     const size_t o_xq = take((size_t)T * D);
     const size_t o_xd = take(sizeof(float) * T * (D / 256));
@@ -134,7 +159,8 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_off = take(sizeof(int32_t) * (E + 1));
     const size_t o_perm = take(sizeof(int32_t) * TK);
     const size_t o_inv = take(sizeof(int32_t) * TK);
-    const size_t o_cur = take(sizeof(int32_t) * E);
+    const size_t o_act = take(sizeof(int32_t) * E);
+    const size_t o_pairs = take(sizeof(int2) * n_pairs);
     const size_t o_sum = take(sizeof(int32_t) * 4);
     const size_t o_log = take(sizeof(float) * T * E);
     const size_t o_h = take(sizeof(float) * TK * I);
@@ -148,19 +174,12 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     if (e != cudaSuccess) return cuda_fail(h, e, "workspace sync");
     e = cudaMalloc(&base, off);
     if (e != cudaSuccess) return cuda_fail(h, e, "workspace cudaMalloc");
+    e = cudaMemset(base, 0, counters_end);
+    if (e != cudaSuccess) { cudaFree(base); return cuda_fail(h, e, "workspace memset"); }
     if (w.base) cudaFree(w.base);
-    if (T > h->tok_count_cap) {
-        uint32_t *tc = nullptr;
-        e = cudaMalloc(&tc, sizeof(uint32_t) * T);
-        if (e != cudaSuccess) { cudaFree(base); w.base = nullptr; w.T = 0; return cuda_fail(h, e, "counter cudaMalloc"); }
-        e = cudaMemset(tc, 0, sizeof(uint32_t) * T);
-        if (e != cudaSuccess) { cudaFree(base); cudaFree(tc); w.base = nullptr; w.T = 0; return cuda_fail(h, e, "counter memset"); }
-        if (h->tok_count) cudaFree(h->tok_count);
-        h->tok_count = tc;
-        h->tok_count_cap = T;
-    }
+    drop_graphs(h);
     uint8_t *b = static_cast<uint8_t *>(base);
-    w.base = base; w.bytes = off;
+    w.base = base; w.bytes = off; w.counters_bytes = counters_end;
     w.T = T; w.D = D; w.E = E; w.K = K; w.I = I;
     w.x = reinterpret_cast<float *>(b + o_x);
     w.xq = Q8Rows{reinterpret_cast<int8_t *>(b + o_xq), reinterpret_cast<float *>(b + o_xd),
@@ -171,10 +190,12 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.rt.offsets = reinterpret_cast<int32_t *>(b + o_off);
     w.rt.perm = reinterpret_cast<int32_t *>(b + o_perm);
     w.rt.inv = reinterpret_cast<int32_t *>(b + o_inv);
-    w.rt.cursor = reinterpret_cast<int32_t *>(b + o_cur);
+    w.rt.act = reinterpret_cast<int32_t *>(b + o_act);
+    w.rt.pairs = reinterpret_cast<int2 *>(b + o_pairs);
     w.rt.summary = reinterpret_cast<int32_t *>(b + o_sum);
+    w.rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
+    w.rt.done = reinterpret_cast<uint32_t *>(b + o_done);
     w.rt.logits = reinterpret_cast<float *>(b + o_log);
-    w.rt.tok_count = h->tok_count;
     w.rt.err = h->dev_err;
     w.rt.loads = h->loads;
     w.h = reinterpret_cast<float *>(b + o_h);
@@ -189,7 +210,8 @@ lfm_gpu_status_t check_layer_shape(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D,
     if (layer >= LFM_GPU_MOE_MAX_LAYERS) return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer %u out of range", layer);
     if (D == 0 || D % 256 || I == 0 || I % 256)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "D=%u and I=%u must be positive multiples of 256", D, I);
-    if (D > 16384 || I > 32768) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "D=%u / I=%u above this build's limits", D, I);
+    if (D > LFM_GPU_MAX_D || I > 16384)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "D=%u / I=%u above this build's limits (8192 / 16384)", D, I);
     if (E == 0 || E > LFM_GPU_MOE_MAX_EXPERTS) return fail(h, LFM_GPU_ERR_INVALID_ARG, "E=%u not in 1..256", E);
     if (K == 0 || K > LFM_GPU_MOE_MAX_TOP_K || K > E)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "K=%u not in 1..min(8,E)", K);
@@ -219,31 +241,24 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
     return e;
 }
 
-/* One layer forward on device x; `stream` already resolved. */
+/* One layer forward on device x; `stream` already resolved.
+ *   route(+dispatch) -> gate|up(+SwiGLU) -> h->Q8_K -> down -> combine
+ * chained with programmatic dependent launch.
+ * Profiling brackets each launch with events, which breaks the PDL overlap,
+ * so it is turned off while profiling. */
 lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s) {
     const MoeLayerDev &L = S.dev;
     Workspace &w = h->ws;  /* sized for the whole call by forward_common */
     Q8Rows xq = w.xq; xq.cols = L.D;
     Q8Rows hq = w.hq; hq.cols = L.I;
-    if (L.dense) {
-        MoeLayerDev rl = L; rl.E = 0; rl.K = 1;
-        MoeLayerDev el = L; el.E = 1; el.K = 1;
-        RouteTables rt = w.rt; rt.loads = nullptr;  /* dense layers are not expert loads */
-        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(rl, x, T, xq, rt, s); }));
-        LFM_CUDA(h, timed(h, K_DENSE_TABLES, s, [&] { return lfm_launch_dense_tables(T, rt, s); }));
-        LFM_CUDA(h, timed(h, K_DISPATCH, s, [&] { return lfm_launch_dispatch(el, T, rt, s); }));
-        LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(el, T, xq, rt, w.h, s); }));
-        LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T, L.I, hq, s); }));
-        LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(el, T, hq, rt, w.y, s); }));
-        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(el, x, T, rt, w.y, s); }));
-        return LFM_GPU_OK;
-    }
-    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s); }));
-    LFM_CUDA(h, timed(h, K_DISPATCH, s, [&] { return lfm_launch_dispatch(L, T, w.rt, s); }));
-    LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, T, xq, w.rt, w.h, s); }));
-    LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * L.K, L.I, hq, s); }));
-    LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, T, hq, w.rt, w.y, s); }));
-    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s); }));
+    const bool pdl = !h->prof;
+    const int grid = h->sm_count;
+    const uint32_t K = lfm_layer_K(L);
+    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, xq, w.rt, w.h, grid, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * K, L.I, hq, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, hq, w.rt, w.y, grid, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, pdl); }));
     return LFM_GPU_OK;
 }
 
@@ -252,6 +267,8 @@ lfm_gpu_status_t read_device_error(lfm_gpu_moe_t *h) {
     LFM_CUDA(h, cudaMemcpy(&e, h->dev_err, sizeof e, cudaMemcpyDeviceToHost));
     if (e == 0) return LFM_GPU_OK;
     LFM_CUDA(h, cudaMemset(h->dev_err, 0, sizeof(uint32_t)));
+    /* an abandoned forward can leave completion counters part-way: clear them */
+    if (h->ws.base) LFM_CUDA(h, cudaMemset(h->ws.base, 0, h->ws.counters_bytes));
     if (e & LFM_DEVERR_TIMEOUT) return fail(h, LFM_GPU_ERR_TIMEOUT, "device wait timed out (0x%x)", e);
     return fail(h, LFM_GPU_ERR_DEVICE_CHECK, "device bounds check tripped (0x%x)", e);
 }
@@ -267,6 +284,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
     if (!h) return LFM_GPU_ERR_OOM;
     h->device = device_id;
     DeviceGuard g(device_id);
+    if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess ||
+        h->sm_count <= 0)
+        h->sm_count = 148;
     if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&h->dev_err, sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(h->dev_err, 0, sizeof(uint32_t)) != cudaSuccess ||
@@ -283,9 +303,9 @@ LFM_API void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h) {
     if (!h) return;
     DeviceGuard g(h->device);
     if (h->stream) cudaStreamSynchronize(h->stream);
+    drop_graphs(h);
     for (LayerSlot &L : h->layers) free_layer(L);
     if (h->ws.base) cudaFree(h->ws.base);
-    if (h->tok_count) cudaFree(h->tok_count);
     if (h->dev_err) cudaFree(h->dev_err);
     if (h->loads) cudaFree(h->loads);
     for (ProfRec &r : h->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
@@ -307,6 +327,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
     if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "expert weight type %u (only Q4_K=12)", w_type);
     if (!router_w || !gate_exps || !up_exps || !down_exps) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
     DeviceGuard g(h->device);
+    drop_graphs(h);
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
@@ -320,6 +341,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
         cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
         if (e == cudaSuccess) e = cudaMemcpy(S.bufs[i], src[i], sz[i], cudaMemcpyHostToDevice);
         if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "layer upload"); }
+        S.sizes[i] = sz[i];
     }
     S.dev = MoeLayerDev{D, E, K, I, 0, eps, routed_scale, norm_topk_prob ? 1 : 0,
                         static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
@@ -338,6 +360,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t lay
     if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "dense weight type %u (only Q4_K=12)", w_type);
     if (!gate || !up || !down) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
     DeviceGuard g(h->device);
+    drop_graphs(h);
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
@@ -350,6 +373,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t lay
         cudaError_t e = cudaMalloc(&S.bufs[slot[i]], sz[i]);
         if (e == cudaSuccess) e = cudaMemcpy(S.bufs[slot[i]], src[i], sz[i], cudaMemcpyHostToDevice);
         if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "dense upload"); }
+        S.sizes[slot[i]] = sz[i];
     }
     S.dev = MoeLayerDev{D, 0, 0, I, 1, eps, 1.0f, 0, static_cast<float *>(S.bufs[0]), nullptr, nullptr,
                         static_cast<const uint8_t *>(S.bufs[3]), static_cast<const uint8_t *>(S.bufs[4]),
@@ -366,6 +390,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t laye
     lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
     if (st != LFM_GPU_OK) return st;
     DeviceGuard g(h->device);
+    drop_graphs(h);
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
@@ -375,6 +400,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t laye
     for (int i = 0; i < 6; ++i) {
         cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
         if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "synth layer cudaMalloc"); }
+        S.sizes[i] = sz[i];
     }
     cudaStream_t s = h->stream;
     cudaError_t e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[0]), D, 0, 1.0f, 0.0f, s);
@@ -411,6 +437,47 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_toke
     return ensure_workspace(h, max_tokens, D, E, K, I);
 }
 
+/* Replay (capturing on first use) the graph of layers [first, first+n) on x.
+ * Capture runs on the handle's own stream (never the caller's, which may be
+ * the legacy default stream); the replay is launched on the caller's stream. */
+static lfm_gpu_status_t run_graph(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x, uint32_t T,
+                                  cudaStream_t s) {
+    GraphEntry *hit = nullptr;
+    for (GraphEntry &g : h->graphs)
+        if (g.first == first && g.n == n && g.T == T && g.x == x) { hit = &g; break; }
+    if (!hit) {
+        /* first call with this key: run eagerly (kernel attributes get set
+         * outside any capture), then capture the same launches for replay */
+        for (uint32_t l = first; l < first + n; ++l) {
+            lfm_gpu_status_t st = forward_layer(h, h->layers[l], x, T, s);
+            if (st != LFM_GPU_OK) return st;
+        }
+        if (h->graphs.size() >= kMaxGraphs) {
+            cudaGraphExecDestroy(h->graphs.front().exec);
+            h->graphs.erase(h->graphs.begin());
+        }
+        LFM_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        const uint32_t k0 = h->stats.kernels_launched;
+        lfm_gpu_status_t st = LFM_GPU_OK;
+        for (uint32_t l = first; l < first + n && st == LFM_GPU_OK; ++l)
+            st = forward_layer(h, h->layers[l], x, T, h->stream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+        if (st != LFM_GPU_OK) { if (graph) cudaGraphDestroy(graph); return st; }
+        if (ce != cudaSuccess) return cuda_fail(h, ce, "cudaStreamEndCapture");
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return cuda_fail(h, ie, "cudaGraphInstantiate");
+        h->graphs.push_back(GraphEntry{first, n, T, x, h->stats.kernels_launched - k0, exec});
+        h->stats.kernels_launched = k0;
+        return LFM_GPU_OK;
+    }
+    LFM_CUDA(h, cudaGraphLaunch(hit->exec, s));
+    h->stats.kernels_launched += hit->kernels;
+    return LFM_GPU_OK;
+}
+
 static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x, uint32_t T,
                                        int x_on_device, void *stream) {
     if (!h || !x) return LFM_GPU_ERR_INVALID_ARG;
@@ -429,7 +496,7 @@ static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_
         I = S.dev.I > I ? S.dev.I : I;
     }
     DeviceGuard g(h->device);
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);  /* NULL = the CUDA default stream */
     lfm_gpu_status_t st = ensure_workspace(h, T, D, E, K, I);
     if (st != LFM_GPU_OK) return st;
     h->stats = lfm_gpu_moe_stats_t{};
@@ -439,9 +506,14 @@ static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_
         xd = h->ws.x;
         LFM_CUDA(h, cudaMemcpyAsync(xd, x, sizeof(float) * T * D, cudaMemcpyHostToDevice, s));
     }
-    for (uint32_t l = first; l < first + n; ++l) {
-        st = forward_layer(h, h->layers[l], xd, T, s);
+    if (h->use_graphs && !h->prof) {
+        st = run_graph(h, first, n, xd, T, s);
         if (st != LFM_GPU_OK) return st;
+    } else {
+        for (uint32_t l = first; l < first + n; ++l) {
+            st = forward_layer(h, h->layers[l], xd, T, s);
+            if (st != LFM_GPU_OK) return st;
+        }
     }
     if (!x_on_device) {
         LFM_CUDA(h, cudaMemcpyAsync(x, xd, sizeof(float) * T * D, cudaMemcpyDeviceToHost, s));
@@ -475,7 +547,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_route(lfm_gpu_moe_t *h, uint32_t laye
     Workspace &w = h->ws;
     Q8Rows xq = w.xq; xq.cols = L.D;
     LFM_CUDA(h, cudaMemcpyAsync(w.x, x, sizeof(float) * T * L.D, cudaMemcpyHostToDevice, s));
-    LFM_CUDA(h, lfm_launch_route(L, w.x, T, xq, w.rt, s));
+    LFM_CUDA(h, lfm_launch_route(L, w.x, T, xq, w.rt, s, false));
     LFM_CUDA(h, cudaMemcpyAsync(idx_out, w.rt.idx, sizeof(int32_t) * T * L.K, cudaMemcpyDeviceToHost, s));
     LFM_CUDA(h, cudaMemcpyAsync(w_out, w.rt.w, sizeof(float) * T * L.K, cudaMemcpyDeviceToHost, s));
     if (q8_out) {
@@ -493,7 +565,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void
                                                     int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                                     float *rows_out) {
     if (!h || !w || !xq || !sub_dots || !acc || !mins || !rows_out) return LFM_GPU_ERR_INVALID_ARG;
-    if (n_cols == 0 || n_cols % 256 || n_cols > 32768 || n_rows == 0 || n_vec == 0 || n_vec > 65535)
+    if (n_cols == 0 || n_cols % 256 || n_cols > 32768 || n_rows == 0 || n_rows % 8 || n_vec == 0 || n_vec > 65535)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "bad debug shape rows=%u cols=%u vecs=%u", n_rows, n_cols, n_vec);
     DeviceGuard g(h->device);
     const size_t nb = n_cols / 256;
@@ -523,6 +595,21 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     cudaFree(buf);
     if (e != cudaSuccess) return cuda_fail(h, e, "debug_q4k_rows");
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
+                                                      size_t bytes) {
+    if (!h || !out || which > 5) return LFM_GPU_ERR_INVALID_ARG;
+    if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
+        return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
+    const LayerSlot &S = h->layers[layer];
+    if (!S.bufs[which]) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u has no tensor %u", layer, which);
+    if (bytes != S.sizes[which])
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "tensor %u is %zu bytes, not %zu", which, S.sizes[which], bytes);
+    DeviceGuard g(h->device);
+    LFM_CUDA(h, cudaStreamSynchronize(h->stream));
+    LFM_CUDA(h, cudaMemcpy(out, S.bufs[which], bytes, cudaMemcpyDeviceToHost));
     return LFM_GPU_OK;
 }
 

@@ -23,6 +23,16 @@
 
 #define LFM_SPLITMIX_GAMMA 0x9E3779B97F4A7C15ull
 
+/* IEEE round-to-nearest division on both sides (the device compiler does not
+ * always round a division by a constant correctly). */
+#if defined(__CUDA_ARCH__)
+#define LFM_FDIV(a, b) __fdiv_rn((a), (b))
+#define LFM_DDIV(a, b) __ddiv_rn((a), (b))
+#else
+#define LFM_FDIV(a, b) ((a) / (b))
+#define LFM_DDIV(a, b) ((a) / (b))
+#endif
+
 /* splitmix64 output number `ctr` (0-based) of the stream started at `seed`. */
 LFM_HD uint64_t lfm_rng_u64(uint64_t seed, uint64_t ctr) {
     uint64_t z = seed + (ctr + 1ull) * LFM_SPLITMIX_GAMMA;
@@ -41,12 +51,12 @@ LFM_HD double lfm_det_log(double x) {
     double m;
     memcpy(&m, &bits, sizeof m);
     if (m > 1.4142135623730951) { m = m * 0.5; e += 1; }
-    const double s = (m - 1.0) / (m + 1.0);
+    const double s = LFM_DDIV(m - 1.0, m + 1.0);
     const double s2 = s * s;
     double term = s, sum = s;
     for (int k = 1; k <= 13; ++k) {
         term = term * s2;
-        sum = sum + term / (double)(2 * k + 1);
+        sum = sum + LFM_DDIV(term, (double)(2 * k + 1));
     }
     return 2.0 * sum + (double)e * 0.69314718055994530942;
 }
@@ -62,9 +72,9 @@ LFM_HD double lfm_det_normal(uint64_t seed, uint64_t idx) {
         const double s = u * u + v * v;
         if (s > 0.0 && s < 1.0) {
 #if defined(__CUDA_ARCH__)
-            const double f = __dsqrt_rn(-2.0 * lfm_det_log(s) / s);
+            const double f = __dsqrt_rn(LFM_DDIV(-2.0 * lfm_det_log(s), s));
 #else
-            const double f = sqrt(-2.0 * lfm_det_log(s) / s);
+            const double f = sqrt(LFM_DDIV(-2.0 * lfm_det_log(s), s));
 #endif
             return (idx & 1ull) ? v * f : u * f;
         }
@@ -97,18 +107,18 @@ LFM_HD void lfm_q4k_quantize_block(const float *x, lfm_block_q4_K *out) {
         }
         if (lo > 0.0f) lo = 0.0f;   /* the offset term -dmin*m is never positive */
         if (hi < lo) hi = lo;
-        step[j] = (hi - lo) / 15.0f;
+        step[j] = LFM_FDIV(hi - lo, 15.0f);
         off[j] = -lo;
         max_step = step[j] > max_step ? step[j] : max_step;
         max_off = off[j] > max_off ? off[j] : max_off;
     }
-    const uint16_t dh = lfm_float_to_half(max_step / 63.0f);
-    const uint16_t mh = lfm_float_to_half(max_off / 63.0f);
+    const uint16_t dh = lfm_float_to_half(LFM_FDIV(max_step, 63.0f));
+    const uint16_t mh = lfm_float_to_half(LFM_FDIV(max_off, 63.0f));
     const float d = lfm_half_to_float(dh), dmin = lfm_half_to_float(mh);
     int sc[8], mn[8];
     for (int j = 0; j < 8; ++j) {
-        float a = d > 0.0f ? lfm_rne(step[j] / d) : 0.0f;
-        float b = dmin > 0.0f ? lfm_rne(off[j] / dmin) : 0.0f;
+        float a = d > 0.0f ? lfm_rne(LFM_FDIV(step[j], d)) : 0.0f;
+        float b = dmin > 0.0f ? lfm_rne(LFM_FDIV(off[j], dmin)) : 0.0f;
         sc[j] = a > 63.0f ? 63 : (int)a;
         mn[j] = b > 63.0f ? 63 : (int)b;
     }
@@ -126,7 +136,7 @@ LFM_HD void lfm_q4k_quantize_block(const float *x, lfm_block_q4_K *out) {
         for (int i = 0; i < 32; ++i) {
             int v = 0;
             if (s > 0.0f) {
-                const float r = lfm_rne((x[32 * j + i] + o) / s);
+                const float r = lfm_rne(LFM_FDIV(x[32 * j + i] + o, s));
                 v = r < 0.0f ? 0 : (r > 15.0f ? 15 : (int)r);
             }
             q[32 * j + i] = (uint8_t)v;

@@ -5,6 +5,10 @@
  * a*b+c below is two roundings unless written as __fmaf_rn; that lets the
  * kernels follow the reference's evaluation order exactly (the reference runs
  * with FTZ/DAZ set, include/lfm2_simd_avx2.h:49-80).
+ *
+ * Waits: every mbarrier wait is bounded by wall time (%globaltimer); on
+ * timeout the kernel records LFM_DEVERR_TIMEOUT in the device error word and
+ * abandons its work instead of hanging.
  */
 #ifndef LFM_MOE_DEVICE_CUH
 #define LFM_MOE_DEVICE_CUH
@@ -13,8 +17,12 @@
 #include <stdint.h>
 
 #include "lfm_formats.h"
+#include "moe_internal.h"
 
 #define LFM_FULL_MASK 0xFFFFFFFFu
+
+/* Bound on any single wait inside a kernel (ns). */
+#define LFM_WAIT_LIMIT_NS 200000000ull
 
 /* exp(x) rounded to fp32 from a double-precision evaluation.  The reference
  * calls glibc expf (an error bound of about half an ulp); going through double
@@ -41,42 +49,280 @@ __device__ __forceinline__ float lfm_warp_max(float v) {
     return v;
 }
 
-__device__ __forceinline__ int lfm_warp_sum_i(int v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(LFM_FULL_MASK, v, o);
-    return v;
-}
-
 /* 6-bit scale and min of sub-blocks 2g and 2g+1 from the 12 scale bytes
- * (given as three 32-bit words).  Same unpacking as lfm_q4k_scale_min. */
+ * (three little-endian words s0 = bytes 0-3, s1 = 4-7, s2 = 8-11), without
+ * branching on g.  Sub-block j < 4 keeps scale/min in the low 6 bits of byte j
+ * and byte j+4; j >= 4 keeps the low nibbles in byte j+4 and the top 2 bits in
+ * bits 6-7 of bytes j-4 (scale) and j (min) -- the layout lfm_q4k_scale_min
+ * reads.  sh = 16*(g&1) selects the byte pair for both halves. */
 __device__ __forceinline__ void lfm_q4k_pair_scales(uint32_t s0, uint32_t s1, uint32_t s2, int g, int &sc_lo,
                                                     int &m_lo, int &sc_hi, int &m_hi) {
-    uint8_t s[12];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        s[i] = (uint8_t)(s0 >> (8 * i));
-        s[4 + i] = (uint8_t)(s1 >> (8 * i));
-        s[8 + i] = (uint8_t)(s2 >> (8 * i));
-    }
-    int j = 2 * g;
-    if (j < 4) {
-        sc_lo = s[j] & 63; m_lo = s[j + 4] & 63;
-        sc_hi = s[j + 1] & 63; m_hi = s[j + 5] & 63;
+    const uint32_t sh = 16u * (uint32_t)(g & 1);
+    const uint32_t a0 = s0 >> sh, a1 = s1 >> sh, a2 = s2 >> sh;
+    if (g < 2) {  /* uniform per quarter-warp group of 4 lanes; both sides are a handful of ops */
+        sc_lo = (int)(a0 & 63u);
+        sc_hi = (int)((a0 >> 8) & 63u);
+        m_lo = (int)(a1 & 63u);
+        m_hi = (int)((a1 >> 8) & 63u);
     } else {
-        sc_lo = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-        m_lo = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-        sc_hi = (s[j + 5] & 0x0F) | ((s[j - 3] >> 6) << 4);
-        m_hi = (s[j + 5] >> 4) | ((s[j + 1] >> 6) << 4);
+        sc_lo = (int)((a2 & 15u) | (((a0 >> 6) & 3u) << 4));
+        sc_hi = (int)(((a2 >> 8) & 15u) | (((a0 >> 14) & 3u) << 4));
+        m_lo = (int)(((a2 >> 4) & 15u) | (((a1 >> 6) & 3u) << 4));
+        m_hi = (int)(((a2 >> 12) & 15u) | (((a1 >> 14) & 3u) << 4));
     }
 }
 
-/* 128-bit read-only streaming load (weights are read once per forward). */
-__device__ __forceinline__ uint4 lfm_ldg_stream(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
+/* ------------------------------------------------------------------------
+ * mbarrier + bulk-copy (TMA, non-tensor) + programmatic dependent launch
+ * ------------------------------------------------------------------------ */
+__device__ __forceinline__ uint32_t lfm_smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void lfm_mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(lfm_smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void lfm_fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void lfm_mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(lfm_smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void lfm_mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(lfm_smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool lfm_mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(lfm_smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t lfm_globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* Wait for phase `parity` of `bar`, for at most LFM_WAIT_LIMIT_NS.  On
+ * timeout: set the error bit and return false. */
+__device__ __forceinline__ bool lfm_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err) {
+    if (lfm_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = lfm_globaltimer();
+    while (!lfm_mbar_try_wait(bar, parity)) {
+        if (lfm_globaltimer() - t0 > LFM_WAIT_LIMIT_NS) {
+            atomicOr(err, LFM_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+/* L2 policy for data read exactly once (expert weights). */
+__device__ __forceinline__ uint64_t lfm_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+/* Global -> shared bulk copy completing on `bar` (16-byte aligned, bytes % 16 == 0). */
+__device__ __forceinline__ void lfm_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                             uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            lfm_smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(lfm_smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void lfm_bulk_g2s_plain(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     lfm_smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(lfm_smem_u32(bar))
+                 : "memory");
+}
+
+/* Programmatic dependent launch: wait for the preceding kernel's results /
+ * let the next kernel start its prologue. */
+__device__ __forceinline__ void lfm_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void lfm_pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+/* Named barrier over the first `threads` threads of the block (id 1..15). */
+__device__ __forceinline__ void lfm_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+/* ------------------------------------------------------------------------
+ * Q4_K x Q8_K: 8 weight rows per warp
+ * ------------------------------------------------------------------------ */
+
+struct RowDebug {
+    int32_t *sub_dots;  /* [8 rows][nb][8] or NULL */
+    int32_t *acc;       /* [8 rows][nb] */
+    int32_t *mins;      /* [8 rows][nb] */
+};
+
+/*
+ * Dots of 8 consecutive Q4_K weight rows (row r at w + r*rstride; generic
+ * pointer: shared or global memory) -- and, for kMats == 2, of the 8 rows at
+ * w1 -- with nt (<= 8) Q8_K activation rows act[rows[t]].
+ *
+ * Lane 4*r + g owns weight row r and the 32 nibble bytes of group g (sub-blocks
+ * 2g and 2g+1) of every super-block.  For each super-block b in order and each
+ * token: sub-block dots with __dp4a, the exact integer super-block sums
+ *   acc = sum_j sc_j * dot_j,   mins = sum_j m_j * (bsum_{2j} + bsum_{2j+1})
+ * (reduced over the row's 4 lanes; integer, so any order), then the fp32 update
+ * of the reference's 4-row AVX-VNNI kernel (tools/lfm2_cpuid_quants.c:1189-1257):
+ *   sum = fma(d8*d, acc, fma(-(d8*dmin), mins, sum)),  skipped when d8 == 0.
+ * The running sums stay in registers; every lane of a row ends with the row's
+ * results s0[t] (and s1[t]).  Activations are read through the read-only
+ * cache: all 8 rows of the warp read the same bytes, so each load is one
+ * broadcast.
+ */
+template <int kMats, bool kDebug>
+__device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *w1, uint32_t rstride, uint32_t nb,
+                                              const Q8Rows &act, const int (&rows)[LFM_GEMV_CHUNK], int nt,
+                                              float (&s0)[LFM_GEMV_CHUNK], float (&s1)[LFM_GEMV_CHUNK],
+                                              RowDebug dbg) {
+    const int lane = threadIdx.x & 31;
+    const int r = lane >> 2, g = lane & 3;
+    const uint8_t *row0 = w0 + (size_t)r * rstride;
+    const uint8_t *row1 = kMats == 2 ? w1 + (size_t)r * rstride : nullptr;
+#pragma unroll
+    for (int t = 0; t < LFM_GEMV_CHUNK; ++t) { s0[t] = 0.0f; s1[t] = 0.0f; }
+    for (uint32_t b = 0; b < nb; ++b) {
+        int sc0l, m0l, sc0h, m0h, sc1l = 0, m1l = 0, sc1h = 0, m1h = 0;
+        uint32_t wl0[8], wh0[8], wl1[8], wh1[8];
+        float d0, dm0, d1 = 0.0f, dm1 = 0.0f;
+        {
+            const uint8_t *blk = row0 + (size_t)b * LFM_Q4K_BYTES;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+            const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+            const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+            lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc0l, m0l, sc0h, m0h);
+            d0 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
+            dm0 = lfm_h2f((uint16_t)(hdr.x >> 16));
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { wl0[i] = w[i] & 0x0F0F0F0Fu; wh0[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
+        }
+        if (kMats == 2) {
+            const uint8_t *blk = row1 + (size_t)b * LFM_Q4K_BYTES;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+            const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+            const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+            lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc1l, m1l, sc1h, m1h);
+            d1 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
+            dm1 = lfm_h2f((uint16_t)(hdr.x >> 16));
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { wl1[i] = w[i] & 0x0F0F0F0Fu; wh1[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
+        }
+#pragma unroll
+        for (int t = 0; t < LFM_GEMV_CHUNK; ++t) {
+            if (t < nt) {
+                const size_t ar = (size_t)rows[t];
+                const uint4 *xp = reinterpret_cast<const uint4 *>(act.qs + ar * act.cols + 256 * b + 64 * g);
+                const uint4 x0 = __ldg(xp), x1 = __ldg(xp + 1), x2 = __ldg(xp + 2), x3 = __ldg(xp + 3);
+                const uint2 bw = __ldg(reinterpret_cast<const uint2 *>(act.bs + (ar * nb + b) * 16 + 4 * g));
+                const float d8 = __ldg(act.d + ar * nb + b);
+                const int xl[8] = {(int)x0.x, (int)x0.y, (int)x0.z, (int)x0.w, (int)x1.x, (int)x1.y, (int)x1.z, (int)x1.w};
+                const int xh[8] = {(int)x2.x, (int)x2.y, (int)x2.z, (int)x2.w, (int)x3.x, (int)x3.y, (int)x3.z, (int)x3.w};
+                const int bp0 = (int)(int16_t)(bw.x & 0xFFFFu) + (int)(int16_t)(bw.x >> 16);
+                const int bp1 = (int)(int16_t)(bw.y & 0xFFFFu) + (int)(int16_t)(bw.y >> 16);
+                /* four independent 2-deep chains per sum (exact integers: any order) */
+                int pl0[4], ph0[4], pl1[4], ph1[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    pl0[i] = __dp4a((int)wl0[i + 4], xl[i + 4], __dp4a((int)wl0[i], xl[i], 0));
+                    ph0[i] = __dp4a((int)wh0[i + 4], xh[i + 4], __dp4a((int)wh0[i], xh[i], 0));
+                    if (kMats == 2) {
+                        pl1[i] = __dp4a((int)wl1[i + 4], xl[i + 4], __dp4a((int)wl1[i], xl[i], 0));
+                        ph1[i] = __dp4a((int)wh1[i + 4], xh[i + 4], __dp4a((int)wh1[i], xh[i], 0));
+                    }
+                }
+                const int dl0 = (pl0[0] + pl0[1]) + (pl0[2] + pl0[3]);
+                const int dh0 = (ph0[0] + ph0[1]) + (ph0[2] + ph0[3]);
+                const int dl1 = kMats == 2 ? (pl1[0] + pl1[1]) + (pl1[2] + pl1[3]) : 0;
+                const int dh1 = kMats == 2 ? (ph1[0] + ph1[1]) + (ph1[2] + ph1[3]) : 0;
+                if (kDebug && dbg.sub_dots) {
+                    dbg.sub_dots[((size_t)r * nb + b) * 8 + 2 * g] = dl0;
+                    dbg.sub_dots[((size_t)r * nb + b) * 8 + 2 * g + 1] = dh0;
+                }
+                int a0 = sc0l * dl0 + sc0h * dh0, n0 = m0l * bp0 + m0h * bp1;
+                int a1 = sc1l * dl1 + sc1h * dh1, n1 = m1l * bp0 + m1h * bp1;
+                a0 += __shfl_xor_sync(LFM_FULL_MASK, a0, 1);
+                n0 += __shfl_xor_sync(LFM_FULL_MASK, n0, 1);
+                if (kMats == 2) {
+                    a1 += __shfl_xor_sync(LFM_FULL_MASK, a1, 1);
+                    n1 += __shfl_xor_sync(LFM_FULL_MASK, n1, 1);
+                }
+                a0 += __shfl_xor_sync(LFM_FULL_MASK, a0, 2);
+                n0 += __shfl_xor_sync(LFM_FULL_MASK, n0, 2);
+                if (kMats == 2) {
+                    a1 += __shfl_xor_sync(LFM_FULL_MASK, a1, 2);
+                    n1 += __shfl_xor_sync(LFM_FULL_MASK, n1, 2);
+                }
+                if (kDebug && dbg.acc && g == 0) {
+                    dbg.acc[(size_t)r * nb + b] = a0;
+                    dbg.mins[(size_t)r * nb + b] = n0;
+                }
+                if (d8 != 0.0f) {
+                    s0[t] = __fmaf_rn(__fmul_rn(d8, d0), (float)a0, __fmaf_rn(-__fmul_rn(d8, dm0), (float)n0, s0[t]));
+                    if (kMats == 2)
+                        s1[t] = __fmaf_rn(__fmul_rn(d8, d1), (float)a1, __fmaf_rn(-__fmul_rn(d8, dm1), (float)n1, s1[t]));
+                }
+            }
+        }
+    }
+}
+
+/* Shared-memory row stride for 8 staged weight rows of row_bytes each: padded
+ * by 16 bytes when row_bytes/16 is even, so the two rows a quarter-warp reads
+ * fall in different 16-byte bank groups. */
+__host__ __device__ inline uint32_t lfm_stage_stride(uint32_t row_bytes) {
+    return ((row_bytes / 16) & 1u) ? row_bytes : row_bytes + 16u;
+}
+
+/* Q8_K of one 256-value block held 8 per lane (values v[], elements 8*lane..):
+ * d = max/127, q = RNE(x*(127/max)), bsums of the unsaturated codes
+ * (tools/lfm2_cpuid_quants.c:584-631).  Writes into Q8 row `r`, block `b`. */
+__device__ __forceinline__ void lfm_quant_block_warp(const float v[8], Q8Rows dst, size_t r, uint32_t b) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t nb = dst.cols / 256;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = lfm_warp_max(amax);
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int part = 0;
+    if (amax != 0.0f) {
+        const float s = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { q[i] = __float2int_rn(__fmul_rn(v[i], s)); part += q[i]; }
+    }
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[i])) << (8 * i);
+        hi |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[4 + i])) << (8 * i);
+    }
+    *reinterpret_cast<uint2 *>(dst.qs + r * dst.cols + 256 * b + 8 * lane) = make_uint2(lo, hi);
+    const int pair = part + __shfl_xor_sync(LFM_FULL_MASK, part, 1);
+    if ((lane & 1) == 0) dst.bs[(r * nb + b) * 16 + (lane >> 1)] = (int16_t)pair;
+    if (lane == 0) dst.d[r * nb + b] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
 }
 
 #endif /* LFM_MOE_DEVICE_CUH */

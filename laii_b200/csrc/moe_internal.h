@@ -8,20 +8,24 @@
  *   router   fp32 [E][D], bias fp32 [E], ffn_norm fp32 [D]
  * Activations are kept as split Q8_K rows (qs int8 [rows][cols], d fp32
  * [rows][cols/256], bsums int16 [rows][cols/256][16]): same numbers as
- * block_q8_K, but 16-byte aligned rows for vector loads.
+ * block_q8_K, but 16-byte aligned rows for vector and bulk loads.
  */
 #ifndef LFM_MOE_INTERNAL_H
 #define LFM_MOE_INTERNAL_H
 
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #include "lfm_formats.h"
 
 #define LFM_GPU_MAX_TOPK_DEV 8
 #define LFM_GPU_MAX_EXPERTS_DEV 256
+#define LFM_GPU_MAX_D 8192      /* router stages 5*D fp32 in shared memory     */
+#define LFM_GEMV_CHUNK 8        /* tokens per staged activation chunk (GEMV)   */
+#define LFM_GEMV_ROWS 8         /* weight rows per pipeline stage (one per consumer warp) */
 
-/* Device error word bits (read by lfm_gpu_moe_sync). */
+/* Device error word bits (read by lfm_gpu_moe_sync and the host-buffer forward). */
 #define LFM_DEVERR_EXPERT_ID 0x1u   /* routing produced an expert id >= E     */
 #define LFM_DEVERR_SEGMENT 0x2u     /* dispatch segment out of range           */
 #define LFM_DEVERR_TIMEOUT 0x4u     /* a bounded device wait ran out           */
@@ -33,20 +37,22 @@ struct Q8Rows {
     uint32_t cols;
 };
 
-/* Routing / dispatch tables for one forward. */
+/* Routing / dispatch tables for one forward (all device pointers). */
 struct RouteTables {
-    int32_t *idx;        /* [T*K] expert id of assignment a = t*K + k           */
-    float *w;            /* [T*K] combine weight                                */
-    int32_t *counts;     /* [E]   assignments per expert                         */
-    int32_t *offsets;    /* [E+1] exclusive prefix of counts                     */
-    int32_t *perm;       /* [T*K] slot -> assignment (grouped by expert)        */
-    int32_t *inv;        /* [T*K] assignment -> slot                             */
-    int32_t *cursor;     /* [E]   scatter cursors (scratch)                      */
-    int32_t *summary;    /* [4]   unique experts, max segment, -, -             */
-    uint32_t *tok_count; /* [T]   per-token arrival counters (kept at zero)      */
-    float *logits;       /* [T*E] router logits                                  */
-    uint32_t *err;       /* device error word                                    */
-    unsigned long long *loads; /* [2] running sum of unique experts, layer runs  */
+    int32_t *idx;        /* [T*K] expert id of assignment a = t*K + k                   */
+    float *w;            /* [T*K] combine weight                                        */
+    int32_t *counts;     /* [E]   assignments per expert                                 */
+    int32_t *offsets;    /* [E+1] exclusive prefix of counts (first slot of expert e)     */
+    int32_t *perm;       /* [T*K] slot -> assignment (slots grouped by expert)           */
+    int32_t *inv;        /* [T*K] assignment -> slot                                     */
+    int32_t *act;        /* [E]   expert id of active expert u (experts with tokens)     */
+    int2 *pairs;         /* [E + T*K/8] (u, chunk) work pairs, u-major                   */
+    int32_t *summary;    /* [4]   active experts U, max segment, slots, pairs            */
+    uint32_t *tok_count; /* [T]   per-token router-block arrival counters (kept at 0)     */
+    uint32_t *done;      /* [1]   routed-token counter (kept at 0)                        */
+    float *logits;       /* [T*E] router logits                                          */
+    uint32_t *err;       /* device error word                                            */
+    unsigned long long *loads; /* [2] running sum of unique experts, MoE layer runs      */
 };
 
 struct MoeLayerDev {
@@ -61,21 +67,27 @@ struct MoeLayerDev {
     const uint8_t *down;
 };
 
+/* Expert-side geometry of a layer (dense layers are one expert, top-1). */
+__host__ __device__ inline uint32_t lfm_layer_E(const MoeLayerDev &L) { return L.dense ? 1u : L.E; }
+__host__ __device__ inline uint32_t lfm_layer_K(const MoeLayerDev &L) { return L.dense ? 1u : L.K; }
+
+/* Raise a kernel's dynamic shared-memory limit once per device (cache16: 16 slots). */
+cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16);
+
 /* k_route.cu */
-cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
-                             const RouteTables &rt, cudaStream_t s);
-cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
-/* dense layer: every token to "expert 0" with weight 1 (x + down exactly) */
-cudaError_t lfm_launch_dense_tables(uint32_t T, const RouteTables &rt, cudaStream_t s);
+size_t lfm_route_smem(uint32_t D);
+cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
+                             cudaStream_t s, bool pdl);
 
 /* k_expert.cu */
-cudaError_t lfm_launch_gateup(const MoeLayerDev &L, uint32_t T, Q8Rows xq, const RouteTables &rt, float *h,
-                              cudaStream_t s);
-cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s);
-cudaError_t lfm_launch_down(const MoeLayerDev &L, uint32_t T, Q8Rows hq, const RouteTables &rt, float *y,
-                            cudaStream_t s);
-cudaError_t lfm_launch_combine(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt,
-                               const float *y, cudaStream_t s);
+size_t lfm_gemv_smem(uint32_t cols, uint32_t mats);
+cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables &rt, float *h, int grid,
+                              cudaStream_t s, bool pdl);
+cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s, bool pdl);
+cudaError_t lfm_launch_down(const MoeLayerDev &L, Q8Rows hq, const RouteTables &rt, float *y, int grid,
+                            cudaStream_t s, bool pdl);
+cudaError_t lfm_launch_combine(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, const float *y,
+                               cudaStream_t s, bool pdl);
 cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_t n_cols, Q8Rows xq,
                                       uint32_t n_vec, int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                       float *rows_out, cudaStream_t s);

@@ -140,6 +140,15 @@ class GpuMoE:
                                                          _ptr(sub), _ptr(acc), _ptr(mins), _ptr(out)))
         return sub, acc, mins, out
 
+    TENSORS = ("ffn_norm", "router_w", "exp_probs_b", "gate", "up", "down")
+
+    def read_layer(self, layer: int, which: str, nbytes: int) -> np.ndarray:
+        """Bytes of one device tensor of an uploaded layer (see TENSORS)."""
+        out = np.zeros(nbytes, np.uint8)
+        self._check(self._lib.lfm_gpu_moe_debug_read_layer(self._h, layer, self.TENSORS.index(which), _ptr(out),
+                                                           nbytes))
+        return out
+
     def profile(self, enable: bool = True):
         self._check(self._lib.lfm_gpu_moe_profile(self._h, int(enable)))
 

@@ -306,3 +306,21 @@ ORC_EXPORT int orc_dense_ffn_forward(int order, float *x, uint32_t T, uint32_t D
     free(xb); free(h); free(dn); free(xq);
     return 0;
 }
+
+/* Known-answer inputs of the reference's own tests, rebuilt exactly (same
+ * float expressions) so the golden fixtures can pin the oracle to them:
+ *  - router test, tests/test_moe_checkpoint.c:146-159 (xb, router weights,
+ *    exp_probs_b with experts 9 and 25 forced to win);
+ *  - Q8_K test, tests/test_cpuid_quants.c:80-82. */
+ORC_EXPORT void orc_kat_router_inputs(float *xb, float *gate_inp, float *bias, uint32_t D, uint32_t E) {
+    for (uint32_t i = 0; i < D; ++i) xb[i] = cosf((float)i * 0.013f);
+    for (uint32_t e = 0; e < E; ++e) {
+        bias[e] = (float)(e % 5) * 0.15f - 0.2f;
+        for (uint32_t i = 0; i < D; ++i) gate_inp[(size_t)e * D + i] = sinf((float)(e * 17 + i) * 0.007f) * 0.04f;
+    }
+    if (E > 25) { bias[9] = 2.5f; bias[25] = 3.0f; }
+}
+
+ORC_EXPORT void orc_kat_q8k_inputs(float *x, uint32_t n) {
+    for (uint32_t i = 0; i < n; ++i) x[i] = sinf((float)i * 0.031f) * ((i % 2 == 0) ? 2.5f : -1.8f);
+}

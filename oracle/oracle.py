@@ -52,6 +52,8 @@ class Oracle:
         lib.orc_moe_forward.restype = _int
         lib.orc_moe_forward.argtypes = [_int, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _vp, _vp, _vp, _vp, _vp,
                                         _vp, _int, _f32, _vp, _vp, _vp, _vp]
+        lib.orc_kat_router_inputs.argtypes = [_vp, _vp, _vp, _u32, _u32]
+        lib.orc_kat_q8k_inputs.argtypes = [_vp, _u32]
         lib.orc_dense_ffn_forward.restype = _int
         lib.orc_dense_ffn_forward.argtypes = [_int, _vp, _u32, _u32, _u32, _f32, _vp, _vp, _vp, _vp]
         self.lib = lib
@@ -61,6 +63,20 @@ class Oracle:
         out = np.zeros(x.size // 256 * 292, np.uint8)
         self.lib.orc_quantize_q8k(_p(x), _p(out), x.size)
         return out
+
+    def kat_router_inputs(self, D=2048, E=32):
+        """Inputs of the reference's router known-answer test (tests/test_moe_checkpoint.c:138-218)."""
+        xb = np.zeros(D, np.float32)
+        w = np.zeros((E, D), np.float32)
+        b = np.zeros(E, np.float32)
+        self.lib.orc_kat_router_inputs(_p(xb), _p(w), _p(b), D, E)
+        return xb, w, b
+
+    def kat_q8k_inputs(self, n=2048):
+        """Input of the reference's Q8_K parity test (tests/test_cpuid_quants.c:69-111)."""
+        x = np.zeros(n, np.float32)
+        self.lib.orc_kat_q8k_inputs(_p(x), n)
+        return x
 
     def rmsnorm_q8k(self, x: np.ndarray, norm_w: Optional[np.ndarray], eps: float):
         x = np.ascontiguousarray(x, np.float32)

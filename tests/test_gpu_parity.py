@@ -174,7 +174,7 @@ def test_prefill_zipf_subset(oracle, gpu):
 
 
 def test_device_synth_matches_host(gpu):
-    """A layer generated on the device equals the host-generated one: same forward bits."""
+    """A layer generated on the device equals the host-generated one, byte for byte."""
     from laii_b200 import synth
     D, E, K, I = 512, 8, 2, 512
     L = cached_layer(D, E, K, I, layer=5)
@@ -182,6 +182,14 @@ def test_device_synth_matches_host(gpu):
                                                synth.SEED_BIAS)]
     gpu.upload_layer(4, L)
     gpu.synth_layer(5, D, E, K, I, seeds)
+    host = {"ffn_norm": L.ffn_norm, "router_w": L.router_w, "exp_probs_b": L.bias, "gate": L.gate, "up": L.up,
+            "down": L.down}
+    for name, arr in host.items():
+        b = np.ascontiguousarray(arr).view(np.uint8).ravel()
+        d = gpu.read_layer(5, name, b.size)
+        bad = np.nonzero(d != b)[0]
+        assert bad.size == 0, f"{name}: {bad.size} bytes differ, first at {bad[:8]}"
+        assert np.array_equal(gpu.read_layer(4, name, b.size), b), f"upload of {name} altered bytes"
     x = synth.make_hidden(6, D, seed_offset=5)
     a = gpu.forward(4, np.array(x, copy=True))
     b = gpu.forward(5, np.array(x, copy=True))
