@@ -144,7 +144,8 @@ lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void *w, uin
 
 /* Copy tensor `which` of an uploaded layer back to host memory, for checking
  * uploads and the device generator: 0 ffn_norm, 1 router_w, 2 exp_probs_b,
- * 3 gate, 4 up, 5 down (`bytes` must equal the tensor's size).  Synchronous.
+ * 3 gate, 4 up, 5 down; the first `bytes` bytes (at most the tensor's size;
+ * exp_probs_b is stored padded to a multiple of 4 floats).  Synchronous.
  * No counterpart in the reference. */
 lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
                                               size_t bytes);

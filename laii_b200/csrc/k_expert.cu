@@ -33,6 +33,7 @@ template <int kMats> struct GemvShape {
     static constexpr int kConsumers = kMats == 2 ? 16 : 12;  /* consumer warps */
     static constexpr int kPerItem = kMats;                    /* warps sharing one item */
     static constexpr int kThreads = (kConsumers + 1) * 32;
+    static constexpr int kActSlots = kMats == 2 ? 2 : 3;      /* (expert, chunk) pairs staged per phase */
 };
 constexpr int kRows = LFM_GEMV_ROWS; /* rows per item (8) */
 constexpr int kCh = LFM_GEMV_CHUNK;
@@ -53,9 +54,14 @@ struct GemvArgs {
     Q8Rows act;        /* activation rows: xq (token-indexed) or hq (slot-indexed) */
     RouteTables rt;
     float *out;        /* h [slots][I] or y [slots][D] */
-    uint32_t stages;   /* stages in use = lanes_of_work * depth */
+    uint32_t stages;   /* stages in use = groups * depth */
     uint32_t groups;   /* active consumer groups (warp pairs for gate|up, warps for down) */
+    uint32_t slots;    /* activation slots (pairs staged per phase), 1..kActSlots */
+    int next_down;     /* gate|up: prefetch the down rows of the next kernel into L2 */
 };
+
+/* Dynamic shared memory: [stages][kMats][8 rows][row stride] weights, then
+ * kActSlots activation slots. */
 
 template <int kMats>
 __global__ void __launch_bounds__(GemvShape<kMats>::kThreads, 1) k_gemv(GemvArgs A) {
@@ -123,15 +129,30 @@ __global__ void __launch_bounds__(GemvShape<kMats>::kThreads, 1) k_gemv(GemvArgs
                 const size_t row0 = (size_t)e * rows_total + (size_t)(i % gpp) * kRows;
                 uint8_t *dst = dsm + (size_t)s * stage_bytes;
                 lfm_mbar_arrive_tx(&sh.full[s], kMats * kRows * row_bytes);
-                for (int m = 0; m < kMats; ++m) {
-                    const uint8_t *src = (m == 0 ? W0 : W1) + row0 * row_bytes;
-                    uint8_t *d = dst + (size_t)m * kRows * rs;
-                    if (rs == row_bytes) {
-                        lfm_bulk_g2s(d, src, kRows * row_bytes, &sh.full[s], policy);
-                    } else {
-                        for (int r = 0; r < kRows; ++r)
-                            lfm_bulk_g2s(d + (size_t)r * rs, src + (size_t)r * row_bytes, row_bytes, &sh.full[s], policy);
-                    }
+                for (int m = 0; m < kMats; ++m)
+                    lfm_bulk_g2s(dst + (size_t)m * kRows * rs, (m == 0 ? W0 : W1) + row0 * row_bytes,
+                                 kRows * row_bytes, &sh.full[s], policy);
+                /* the item that refills this stage next round: start its HBM read now */
+                const uint64_t ia = i + (uint64_t)G * depth;
+                if (ia < i1) {
+                    const uint64_t pa = ia / gpp;
+                    const int ea = pa == pj ? e : __ldcg(A.rt.act + __ldcg(A.rt.pairs + pa).x);
+                    const size_t rowa = (size_t)ea * rows_total + (size_t)(ia % gpp) * kRows;
+                    for (int m = 0; m < kMats; ++m)
+                        lfm_prefetch_l2((m == 0 ? W0 : W1) + rowa * row_bytes, kRows * row_bytes);
+                }
+            }
+            if (kMats == 2 && A.next_down) {
+                /* warm L2 with the rows this block will stream in the down kernel
+                 * (same pair list and block partition there) */
+                const uint32_t nbd = L.I / 256, dbytes = nbd * LFM_Q4K_BYTES;
+                const uint64_t gd = L.D / kRows, nd = (uint64_t)__ldcg(A.rt.summary + 3) * gd;
+                const uint64_t d0 = nd * blockIdx.x / gridDim.x, d1 = nd * (blockIdx.x + 1) / gridDim.x;
+                uint64_t pd = ~0ull;
+                int ed = 0;
+                for (uint64_t q = d0; q < d1; ++q) {
+                    if (q / gd != pd) { pd = q / gd; ed = __ldcg(A.rt.act + __ldcg(A.rt.pairs + pd).x); }
+                    lfm_prefetch_l2(L.down + ((size_t)ed * L.D + (size_t)(q % gd) * kRows) * dbytes, kRows * dbytes);
                 }
             }
             /* leave no copy in flight into this block's shared memory: the last
@@ -151,67 +172,94 @@ __global__ void __launch_bounds__(GemvShape<kMats>::kThreads, 1) k_gemv(GemvArgs
     const int mat = warp % Sh::kPerItem;                  /* gate|up: 0 gate, 1 up */
     if (grp >= G) return;
     const int r = lane >> 2, g = lane & 3;
-    int64_t cur_pair = -1;
-    int rows[kCh];
-    int nt = 0, slot0 = 0;
-    for (uint64_t k = grp, i = i0 + grp; i < i1; k += G, i += G) {
-        const int64_t j = (int64_t)(i / gpp);
-        if (j != cur_pair) {
-            const int2 pr = __ldcg(A.rt.pairs + j);
-            const uint32_t e = (uint32_t)__ldcg(A.rt.act + pr.x);
-            const uint32_t n_e = (uint32_t)__ldcg(A.rt.counts + e);
-            const uint32_t off_e = (uint32_t)__ldcg(A.rt.offsets + e);
-            slot0 = (int)off_e + pr.y * kCh;
-            nt = min(kCh, (int)n_e - pr.y * kCh);
-#pragma unroll
-            for (int t = 0; t < kCh; ++t)
-                rows[t] = t < nt ? (kMats == 2 ? __ldcg(A.rt.perm + slot0 + t) / (int)K : slot0 + t) : 0;
-            cur_pair = j;
-        }
-        uint32_t ph;
-        const uint32_t s = stage_of(k, ph);
-        bool ok = !ld_volatile(&sh.abort) && lfm_mbar_wait(&sh.full[s], ph & 1u, A.rt.err);
-        ok = __all_sync(LFM_FULL_MASK, ok); /* the row dots shuffle across the whole warp */
-        if (kMats == 2) {
-            /* both warps of the pair decide together from slots only they write,
-             * so they always take the same number of pair barriers */
-            if (lane == 0) sh.pair_ok[grp][mat] = ok ? 1 : 0;
-            lfm_bar_sync(1 + (int)grp, 64);
-            ok = sh.pair_ok[grp][0] && sh.pair_ok[grp][1];
-            lfm_bar_sync(1 + (int)grp, 64); /* both read the slots before either rewrites them */
-        }
-        if (!ok) {
-            if (lane == 0) atomicExch(&sh.abort, 1);
-            break;
-        }
-        const uint8_t *st = dsm + (size_t)s * stage_bytes + (size_t)mat * kRows * rs;
-        const uint32_t row0 = (uint32_t)(i % gpp) * kRows;
-        float s0[kCh], s1[kCh];
-        lfm_q4k_rows8<1, false>(st, nullptr, rs, nb, A.act, rows, nt, s0, s1, RowDebug{});
-        if (kMats == 2) {
-            if (mat == 0) {
-#pragma unroll
-                for (int t = 0; t < kCh; ++t)
-                    if ((t & 3) == g && t < nt) sh.gx[grp][r][t] = s0[t];
+    const int n_cons = (int)G * Sh::kPerItem * 32;        /* threads in the consumer barrier */
+    const int ctid = threadIdx.x;
+    uint8_t *act_base = dsm + (size_t)A.stages * stage_bytes;
+    const size_t slot_bytes = lfm_act_slot_bytes(cols);
+    __shared__ int s_rows[Sh::kActSlots][kCh]; /* A.slots <= kActSlots */
+    __shared__ int s_nt[Sh::kActSlots], s_slot0[Sh::kActSlots];
+    bool stop = false;
+    if (i0 < i1) {
+        const uint64_t j_first = i0 / gpp, j_last = (i1 - 1) / gpp;
+        for (uint64_t jp = j_first; jp <= j_last; jp += A.slots) {
+            const uint32_t np = (uint32_t)min((uint64_t)A.slots, j_last - jp + 1);
+            /* stage this phase's pairs */
+            lfm_bar_sync(15, n_cons); /* previous phase fully consumed */
+            if (ctid < (int)np) {
+                const int2 pr = __ldcg(A.rt.pairs + jp + ctid);
+                const uint32_t e = (uint32_t)__ldcg(A.rt.act + pr.x);
+                const int n_e = __ldcg(A.rt.counts + e);
+                const int off_e = __ldcg(A.rt.offsets + e);
+                s_slot0[ctid] = off_e + pr.y * kCh;
+                s_nt[ctid] = min(kCh, n_e - pr.y * kCh);
             }
-            lfm_bar_sync(1 + (int)grp, 64); /* gate results visible; both warps done reading the stage */
-            if (mat == 1) {
-                if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
+            lfm_bar_sync(15, n_cons);
+            if (ctid < (int)np * kCh) {
+                const int q = ctid / kCh, t = ctid % kCh;
+                s_rows[q][t] = t < s_nt[q] ? (kMats == 2 ? __ldcg(A.rt.perm + s_slot0[q] + t) / (int)K : s_slot0[q] + t) : 0;
+            }
+            lfm_bar_sync(15, n_cons);
+            for (uint32_t q = 0; q < np; ++q)
+                lfm_stage_act(A.act, s_rows[q], s_nt[q], act_base + q * slot_bytes, ctid, n_cons);
+            lfm_bar_sync(15, n_cons);
+
+            /* this phase's items, round-robin over groups (k = local item index) */
+            const uint64_t ia = max(i0, jp * gpp), ib = min(i1, (jp + np) * gpp);
+            uint64_t k = ia - i0;
+            k += (grp + G - (uint32_t)(k % G)) % G;
+            for (; i0 + k < ib; k += G) {
+                const uint64_t i = i0 + k;
+                const uint32_t q = (uint32_t)(i / gpp - jp);
+                const int nt = s_nt[q], slot0 = s_slot0[q];
+                uint32_t ph;
+                const uint32_t s = stage_of(k, ph);
+                bool ok = !stop && !ld_volatile(&sh.abort) && lfm_mbar_wait(&sh.full[s], ph & 1u, A.rt.err);
+                ok = __all_sync(LFM_FULL_MASK, ok); /* the row dots shuffle across the whole warp */
+                if (kMats == 2) {
+                    /* both warps of the pair decide together from slots only they write,
+                     * so they always take the same number of pair barriers */
+                    if (lane == 0) sh.pair_ok[grp][mat] = ok ? 1 : 0;
+                    lfm_bar_sync(1 + (int)grp, 64);
+                    ok = sh.pair_ok[grp][0] && sh.pair_ok[grp][1];
+                    lfm_bar_sync(1 + (int)grp, 64); /* both read the slots before either rewrites them */
+                }
+                if (!ok) {
+                    /* keep walking the phase (barriers stay balanced) but do no more work */
+                    if (lane == 0) atomicExch(&sh.abort, 1);
+                    stop = true;
+                    continue;
+                }
+                const uint8_t *st = dsm + (size_t)s * stage_bytes + (size_t)mat * kRows * rs;
+                const uint32_t row0 = (uint32_t)(i % gpp) * kRows;
+                const ActSmem av = lfm_act_slot(act_base + q * slot_bytes, cols);
+                float s0[kCh], s1[kCh];
+                lfm_q4k_rows8<1, false>(st, nullptr, rs, av, nt, s0, s1, RowDebug{});
+                if (kMats == 2) {
+                    if (mat == 0) {
 #pragma unroll
-                for (int t = 0; t < kCh; ++t) {
-                    if ((t & 3) == g && t < nt) {
-                        const float gv = sh.gx[grp][r][t];
-                        const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, lfm_expf(-gv)));
-                        A.out[(size_t)(slot0 + t) * L.I + row0 + r] = __fmul_rn(silu, s0[t]);
+                        for (int t = 0; t < kCh; ++t)
+                            if ((t & 3) == g && t < nt) sh.gx[grp][r][t] = s0[t];
                     }
+                    lfm_bar_sync(1 + (int)grp, 64); /* gate results visible; both warps done with the stage */
+                    if (mat == 1) {
+                        if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
+#pragma unroll
+                        for (int t = 0; t < kCh; ++t) {
+                            if ((t & 3) == g && t < nt) {
+                                const float gv = sh.gx[grp][r][t];
+                                const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, lfm_expf(-gv)));
+                                A.out[(size_t)(slot0 + t) * L.I + row0 + r] = __fmul_rn(silu, s0[t]);
+                            }
+                        }
+                    }
+                } else {
+                    __syncwarp();
+                    if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
+#pragma unroll
+                    for (int t = 0; t < kCh; ++t)
+                        if ((t & 3) == g && t < nt) A.out[(size_t)(slot0 + t) * L.D + row0 + r] = s0[t];
                 }
             }
-        } else {
-            __syncwarp();
-            if (lane == 0) lfm_mbar_arrive(&sh.empty[s]);
-#pragma unroll
-            for (int t = 0; t < kCh; ++t)
-                if ((t & 3) == g && t < nt) A.out[(size_t)(slot0 + t) * L.D + row0 + r] = s0[t];
         }
     }
 }
@@ -271,18 +319,22 @@ __global__ void __launch_bounds__(128) k_combine(float *__restrict__ x, uint32_t
 __global__ void __launch_bounds__(256) k_debug_rows(const uint8_t *__restrict__ w, uint32_t n_rows, uint32_t n_cols,
                                                     Q8Rows xq, int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                                     float *rows_out) {
+    extern __shared__ __align__(128) uint8_t slot[];
+    __shared__ int vrow[kCh];
     const uint32_t nb = n_cols / 256;
     const uint32_t v = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t row_bytes = (size_t)nb * LFM_Q4K_BYTES;
-    int rows[kCh];
-#pragma unroll
-    for (int t = 0; t < kCh; ++t) rows[t] = (int)v;
+    if (threadIdx.x < kCh) vrow[threadIdx.x] = (int)v;
+    __syncthreads();
+    lfm_stage_act(xq, vrow, 1, slot, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const ActSmem av = lfm_act_slot(slot, n_cols);
     for (uint32_t rb = (blockIdx.y * 8 + warp) * kRows; rb < n_rows; rb += gridDim.y * 8 * kRows) {
         const size_t o = (size_t)v * n_rows + rb;
         RowDebug dbg{sub_dots + o * nb * 8, acc + o * nb, mins + o * nb};
         float s0[kCh], s1[kCh];
-        lfm_q4k_rows8<1, true>(w + rb * row_bytes, nullptr, (uint32_t)row_bytes, nb, xq, rows, 1, s0, s1, dbg);
+        lfm_q4k_rows8<1, true, false>(w + rb * row_bytes, nullptr, (uint32_t)row_bytes, av, 1, s0, s1, dbg);
         if ((lane & 3) == 0) rows_out[o + (lane >> 2)] = s0[0];
     }
 }
@@ -342,11 +394,21 @@ constexpr size_t kSmemBudget = 220 * 1024;
 
 /* Consumer groups and stages: as many groups as stages allow (at most the
  * kernel's), then a whole number of private stages per group. */
-void gemv_plan(uint32_t cols, uint32_t mats, uint32_t &groups, uint32_t &stages) {
+/* Activation slots, consumer groups and stages: the most slots that still
+ * leave stages for at least 4 groups (else one slot), as many groups as the
+ * remaining stages allow (at most the kernel's), then a whole number of
+ * private stages per group. */
+void gemv_plan(uint32_t cols, uint32_t mats, uint32_t &slots, uint32_t &groups, uint32_t &stages) {
     const size_t stage = (size_t)mats * kRows * lfm_stage_stride(cols / 256 * LFM_Q4K_BYTES);
-    size_t n = (kSmemBudget - sizeof(GemvShared) - 1024) / stage;
-    if (n > kMaxStages) n = kMaxStages;
     const uint32_t gmax = mats == 2 ? (uint32_t)GemvShape<2>::kConsumers / 2 : (uint32_t)GemvShape<1>::kConsumers;
+    const uint32_t smax = mats == 2 ? (uint32_t)GemvShape<2>::kActSlots : (uint32_t)GemvShape<1>::kActSlots;
+    size_t n = 0;
+    for (slots = smax; slots >= 1; --slots) {
+        const size_t fixed = sizeof(GemvShared) + 2048 + (size_t)slots * lfm_act_slot_bytes(cols);
+        n = fixed < kSmemBudget ? (kSmemBudget - fixed) / stage : 0;
+        if (n >= 4 || slots == 1) break;
+    }
+    if (n > kMaxStages) n = kMaxStages;
     groups = (uint32_t)(n < gmax ? n : gmax);
     stages = groups ? (uint32_t)(n / groups * groups) : 0;
 }
@@ -366,16 +428,17 @@ cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16) {
 }
 
 size_t lfm_gemv_smem(uint32_t cols, uint32_t mats) {
-    uint32_t groups, stages;
-    gemv_plan(cols, mats, groups, stages);
-    return (size_t)stages * mats * kRows * lfm_stage_stride(cols / 256 * LFM_Q4K_BYTES);
+    uint32_t slots, groups, stages;
+    gemv_plan(cols, mats, slots, groups, stages);
+    return (size_t)stages * mats * kRows * lfm_stage_stride(cols / 256 * LFM_Q4K_BYTES) +
+           (size_t)slots * lfm_act_slot_bytes(cols);
 }
 
 static cudaError_t launch_gemv(const void *fn, uint32_t cols, uint32_t mats, GemvArgs &a, int grid, cudaStream_t s,
                                bool pdl) {
     static size_t cache[2][16];
-    gemv_plan(cols, mats, a.groups, a.stages);
-    if (a.groups == 0) return cudaErrorInvalidValue;
+    gemv_plan(cols, mats, a.slots, a.groups, a.stages);
+    if (a.groups == 0 || a.slots == 0) return cudaErrorInvalidValue;
     const size_t smem = lfm_gemv_smem(cols, mats);
     cudaError_t e = lfm_smem_attr(fn, smem, cache[mats - 1]);
     if (e != cudaSuccess) return e;
@@ -386,13 +449,13 @@ static cudaError_t launch_gemv(const void *fn, uint32_t cols, uint32_t mats, Gem
 
 cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables &rt, float *h, int grid,
                               cudaStream_t s, bool pdl) {
-    GemvArgs a{L, xq, rt, h, 0, 0};
+    GemvArgs a{L, xq, rt, h, 0, 0, 0, 1};
     return launch_gemv((const void *)k_gemv<2>, L.D, 2, a, grid, s, pdl);
 }
 
 cudaError_t lfm_launch_down(const MoeLayerDev &L, Q8Rows hq, const RouteTables &rt, float *y, int grid,
                             cudaStream_t s, bool pdl) {
-    GemvArgs a{L, hq, rt, y, 0, 0};
+    GemvArgs a{L, hq, rt, y, 0, 0, 0, 0};
     return launch_gemv((const void *)k_gemv<1>, L.I, 1, a, grid, s, pdl);
 }
 
@@ -416,8 +479,12 @@ cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_
                                       uint32_t n_vec, int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                       float *rows_out, cudaStream_t s) {
     if (n_rows % kRows) return cudaErrorInvalidValue;
+    static size_t cache[16];
+    const size_t smem = lfm_act_slot_bytes(n_cols);
+    cudaError_t e = lfm_smem_attr((const void *)k_debug_rows, smem, cache);
+    if (e != cudaSuccess) return e;
     const uint32_t gy = min(64u, (n_rows / kRows + 7) / 8);
-    k_debug_rows<<<dim3(n_vec, gy), 256, 0, s>>>(w, n_rows, n_cols, xq, sub_dots, acc, mins, rows_out);
+    k_debug_rows<<<dim3(n_vec, gy), 256, smem, s>>>(w, n_rows, n_cols, xq, sub_dots, acc, mins, rows_out);
     return cudaGetLastError();
 }
 

@@ -331,7 +331,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
-    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * E,
+    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * ((E + 3) / 4 * 4),
                           (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
                           (size_t)E * D * nbi * LFM_Q4K_BYTES};
     const void *src[6] = {ffn_norm, router_w, exp_probs_b, gate_exps, up_exps, down_exps};
@@ -339,7 +339,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
         if (i == 0 && !ffn_norm) continue;
         if (i == 2 && !exp_probs_b) continue;
         cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
-        if (e == cudaSuccess) e = cudaMemcpy(S.bufs[i], src[i], sz[i], cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && i == 2) e = cudaMemset(S.bufs[i], 0, sz[i]); /* bias padded to 16 bytes */
+        if (e == cudaSuccess)
+            e = cudaMemcpy(S.bufs[i], src[i], i == 2 ? sizeof(float) * E : sz[i], cudaMemcpyHostToDevice);
         if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "layer upload"); }
         S.sizes[i] = sz[i];
     }
@@ -394,7 +396,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t laye
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
-    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * E,
+    const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * ((E + 3) / 4 * 4),
                           (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
                           (size_t)E * D * nbi * LFM_Q4K_BYTES};
     for (int i = 0; i < 6; ++i) {
@@ -406,8 +408,11 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t laye
     cudaError_t e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[0]), D, 0, 1.0f, 0.0f, s);
     if (e == cudaSuccess) e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[1]), (uint64_t)E * D, seeds[3], 0.0f, router_std, s);
     if (e == cudaSuccess) {
-        if (exp_probs_b) e = cudaMemcpyAsync(S.bufs[2], exp_probs_b, sizeof(float) * E, cudaMemcpyHostToDevice, s);
-        else e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[2]), E, seeds[4], 0.0f, bias_std, s);
+        e = cudaMemsetAsync(S.bufs[2], 0, sz[2], s);
+        if (e == cudaSuccess && exp_probs_b)
+            e = cudaMemcpyAsync(S.bufs[2], exp_probs_b, sizeof(float) * E, cudaMemcpyHostToDevice, s);
+        else if (e == cudaSuccess)
+            e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[2]), E, seeds[4], 0.0f, bias_std, s);
     }
     if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[3]), (uint64_t)E * I * nbd, seeds[0], w_std, s);
     if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[4]), (uint64_t)E * I * nbd, seeds[1], w_std, s);
@@ -605,8 +610,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t
         return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
     const LayerSlot &S = h->layers[layer];
     if (!S.bufs[which]) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u has no tensor %u", layer, which);
-    if (bytes != S.sizes[which])
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "tensor %u is %zu bytes, not %zu", which, S.sizes[which], bytes);
+    if (bytes == 0 || bytes > S.sizes[which])
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "tensor %u holds %zu bytes, asked for %zu", which, S.sizes[which], bytes);
     DeviceGuard g(h->device);
     LFM_CUDA(h, cudaStreamSynchronize(h->stream));
     LFM_CUDA(h, cudaMemcpy(out, S.bufs[which], bytes, cudaMemcpyDeviceToHost));

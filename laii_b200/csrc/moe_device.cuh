@@ -152,6 +152,11 @@ __device__ __forceinline__ void lfm_bulk_g2s_plain(void *dst, const void *src, u
                  : "memory");
 }
 
+/* Bulk prefetch of global memory into L2 (bytes % 16 == 0, 16-byte aligned). */
+__device__ __forceinline__ void lfm_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 /* Programmatic dependent launch: wait for the preceding kernel's results /
  * let the next kernel start its prologue. */
 __device__ __forceinline__ void lfm_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -174,10 +179,72 @@ struct RowDebug {
     int32_t *mins;      /* [8 rows][nb] */
 };
 
+/* Q8_K activation rows staged in shared memory for one (expert, chunk) pair:
+ *   qs  [nt][cols]   within each 256-byte super-block, the 16-byte chunk
+ *                    (group g, part k) -- bytes 64g+16k.. -- is stored at
+ *                    chunk 4k+g, so the 4 lane groups of a warp reading part k
+ *                    hit 4 distinct bank groups (and the 8 rows broadcast);
+ *   bs  [nt][nb][16] bsums;   d [nt][nb] scales. */
+struct ActSmem {
+    const uint8_t *qs;
+    const int16_t *bs;
+    const float *d;
+    uint32_t cols, nb;
+};
+
+__host__ __device__ constexpr size_t lfm_act_slot_bytes(uint32_t cols) {
+    return (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * (cols / 256) * 36;
+}
+
+__device__ __forceinline__ ActSmem lfm_act_slot(const uint8_t *base, uint32_t cols) {
+    const uint32_t nb = cols / 256;
+    return ActSmem{base, reinterpret_cast<const int16_t *>(base + (size_t)LFM_GEMV_CHUNK * cols),
+                   reinterpret_cast<const float *>(base + (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * nb * 32),
+                   cols, nb};
+}
+
+/* Copy nt Q8 rows (global row ids rows[t]) into a slot; threads tid of nthr. */
+__device__ __forceinline__ void lfm_stage_act(const Q8Rows &src, const int *rows, int nt, uint8_t *slot, int tid,
+                                              int nthr) {
+    const uint32_t cols = src.cols, nb = cols / 256, qv = cols / 16;
+    uint8_t *qs = slot;
+    int16_t *bs = reinterpret_cast<int16_t *>(slot + (size_t)LFM_GEMV_CHUNK * cols);
+    float *dd = reinterpret_cast<float *>(slot + (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * nb * 32);
+    for (uint32_t q = tid; q < (uint32_t)nt * qv; q += nthr) {
+        const uint32_t t = q / qv, c = q % qv;
+        const uint32_t sb = c >> 4, gk = c & 15;             /* logical chunk 4g+k of super-block sb */
+        const uint32_t phys = sb * 16 + (gk & 3) * 4 + (gk >> 2);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src.qs + (size_t)rows[t] * cols) + c);
+        reinterpret_cast<uint4 *>(qs + (size_t)t * cols)[phys] = v;
+    }
+    for (uint32_t q = tid; q < (uint32_t)nt * nb * 2; q += nthr) {
+        const uint32_t t = q / (nb * 2), c = q % (nb * 2);
+        reinterpret_cast<uint4 *>(bs + (size_t)t * nb * 16)[c] =
+            __ldcg(reinterpret_cast<const uint4 *>(src.bs + (size_t)rows[t] * nb * 16) + c);
+    }
+    for (uint32_t q = tid; q < (uint32_t)nt * nb; q += nthr) {
+        const uint32_t t = q / nb, c = q % nb;
+        dd[(size_t)t * nb + c] = __ldcg(src.d + (size_t)rows[t] * nb + c);
+    }
+}
+
+/* 16-byte load from shared memory (kShared) or through a generic pointer. */
+template <bool kShared>
+__device__ __forceinline__ uint4 lfm_ld16(const uint8_t *p) {
+    if (kShared) {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(lfm_smem_u32(p)));
+        return v;
+    }
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
 /*
- * Dots of 8 consecutive Q4_K weight rows (row r at w + r*rstride; generic
- * pointer: shared or global memory) -- and, for kMats == 2, of the 8 rows at
- * w1 -- with nt (<= 8) Q8_K activation rows act[rows[t]].
+ * Dots of 8 consecutive Q4_K weight rows (row r at w + r*rstride, shared memory
+ * when kSharedW) -- and, for kMats == 2, of the 8 rows at w1 -- with nt (<= 8)
+ * staged Q8_K activation rows.
  *
  * Lane 4*r + g owns weight row r and the 32 nibble bytes of group g (sub-blocks
  * 2g and 2g+1) of every super-block.  For each super-block b in order and each
@@ -187,17 +254,15 @@ struct RowDebug {
  * of the reference's 4-row AVX-VNNI kernel (tools/lfm2_cpuid_quants.c:1189-1257):
  *   sum = fma(d8*d, acc, fma(-(d8*dmin), mins, sum)),  skipped when d8 == 0.
  * The running sums stay in registers; every lane of a row ends with the row's
- * results s0[t] (and s1[t]).  Activations are read through the read-only
- * cache: all 8 rows of the warp read the same bytes, so each load is one
- * broadcast.
+ * results s0[t] (and s1[t]).
  */
-template <int kMats, bool kDebug>
-__device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *w1, uint32_t rstride, uint32_t nb,
-                                              const Q8Rows &act, const int (&rows)[LFM_GEMV_CHUNK], int nt,
-                                              float (&s0)[LFM_GEMV_CHUNK], float (&s1)[LFM_GEMV_CHUNK],
-                                              RowDebug dbg) {
+template <int kMats, bool kDebug, bool kSharedW = true>
+__device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *w1, uint32_t rstride,
+                                              const ActSmem &act, int nt, float (&s0)[LFM_GEMV_CHUNK],
+                                              float (&s1)[LFM_GEMV_CHUNK], RowDebug dbg) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2, g = lane & 3;
+    const uint32_t nb = act.nb;
     const uint8_t *row0 = w0 + (size_t)r * rstride;
     const uint8_t *row1 = kMats == 2 ? w1 + (size_t)r * rstride : nullptr;
 #pragma unroll
@@ -208,9 +273,9 @@ __device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *
         float d0, dm0, d1 = 0.0f, dm1 = 0.0f;
         {
             const uint8_t *blk = row0 + (size_t)b * LFM_Q4K_BYTES;
-            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-            const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
-            const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+            const uint4 hdr = lfm_ld16<kSharedW>(blk);
+            const uint4 qa = lfm_ld16<kSharedW>(blk + 16 + 32 * g);
+            const uint4 qb = lfm_ld16<kSharedW>(blk + 32 + 32 * g);
             lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc0l, m0l, sc0h, m0h);
             d0 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
             dm0 = lfm_h2f((uint16_t)(hdr.x >> 16));
@@ -220,9 +285,9 @@ __device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *
         }
         if (kMats == 2) {
             const uint8_t *blk = row1 + (size_t)b * LFM_Q4K_BYTES;
-            const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-            const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
-            const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+            const uint4 hdr = lfm_ld16<kSharedW>(blk);
+            const uint4 qa = lfm_ld16<kSharedW>(blk + 16 + 32 * g);
+            const uint4 qb = lfm_ld16<kSharedW>(blk + 32 + 32 * g);
             lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc1l, m1l, sc1h, m1h);
             d1 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
             dm1 = lfm_h2f((uint16_t)(hdr.x >> 16));
@@ -233,11 +298,16 @@ __device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *
 #pragma unroll
         for (int t = 0; t < LFM_GEMV_CHUNK; ++t) {
             if (t < nt) {
-                const size_t ar = (size_t)rows[t];
-                const uint4 *xp = reinterpret_cast<const uint4 *>(act.qs + ar * act.cols + 256 * b + 64 * g);
-                const uint4 x0 = __ldg(xp), x1 = __ldg(xp + 1), x2 = __ldg(xp + 2), x3 = __ldg(xp + 3);
-                const uint2 bw = __ldg(reinterpret_cast<const uint2 *>(act.bs + (ar * nb + b) * 16 + 4 * g));
-                const float d8 = __ldg(act.d + ar * nb + b);
+                /* this lane's 64 activation bytes: parts k = 0..3 of group g, at chunks 4k+g */
+                const uint8_t *xb = act.qs + (size_t)t * act.cols + 256 * b + 16 * g;
+                const uint4 x0 = lfm_ld16<true>(xb), x1 = lfm_ld16<true>(xb + 64);
+                const uint4 x2 = lfm_ld16<true>(xb + 128), x3 = lfm_ld16<true>(xb + 192);
+                uint2 bw;
+                float d8;
+                asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
+                             : "=r"(bw.x), "=r"(bw.y)
+                             : "r"(lfm_smem_u32(act.bs + ((size_t)t * nb + b) * 16 + 4 * g)));
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(d8) : "r"(lfm_smem_u32(act.d + (size_t)t * nb + b)));
                 const int xl[8] = {(int)x0.x, (int)x0.y, (int)x0.z, (int)x0.w, (int)x1.x, (int)x1.y, (int)x1.z, (int)x1.w};
                 const int xh[8] = {(int)x2.x, (int)x2.y, (int)x2.z, (int)x2.w, (int)x3.x, (int)x3.y, (int)x3.z, (int)x3.w};
                 const int bp0 = (int)(int16_t)(bw.x & 0xFFFFu) + (int)(int16_t)(bw.x >> 16);
@@ -289,12 +359,11 @@ __device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *
     }
 }
 
-/* Shared-memory row stride for 8 staged weight rows of row_bytes each: padded
- * by 16 bytes when row_bytes/16 is even, so the two rows a quarter-warp reads
- * fall in different 16-byte bank groups. */
-__host__ __device__ inline uint32_t lfm_stage_stride(uint32_t row_bytes) {
-    return ((row_bytes / 16) & 1u) ? row_bytes : row_bytes + 16u;
-}
+/* Shared-memory row stride of staged weight rows: rows stay contiguous so an
+ * item is one bulk copy per matrix (the two rows a quarter-warp reads may share
+ * a bank group: a 2-way conflict on 3 loads per super-block, cheaper than 8
+ * copies per matrix). */
+__host__ __device__ inline uint32_t lfm_stage_stride(uint32_t row_bytes) { return row_bytes; }
 
 /* Q8_K of one 256-value block held 8 per lane (values v[], elements 8*lane..):
  * d = max/127, q = RNE(x*(127/max)), bsums of the unsaturated codes
