@@ -121,6 +121,27 @@ lfm_gpu_status_t lfm_gpu_moe_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x,
 lfm_gpu_status_t lfm_gpu_moe_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x,
                                            uint32_t T, int x_on_device, void *stream);
 
+/* Size of the fixed scratch that lfm_gpu_moe_forward_noalloc uses (per device). */
+#define LFM_GPU_MOE_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* lfm_gpu_moe_forward for device-resident x on `stream` (NULL = the CUDA
+ * default stream) that allocates nothing: no cudaMalloc/cudaFree, no growth of
+ * the handle's scratch.  It exists for callers that must not allocate while a
+ * step runs (an engine that plans all device memory at load time, or code that
+ * cannot afford the device-wide synchronisation an allocation may cause).  Its
+ * scratch is one fixed array of LFM_GPU_MOE_NOALLOC_SCRATCH_BYTES per device in
+ * the library's static device memory; a (T, layer shape) whose scratch does not
+ * fit is rejected with LFM_GPU_ERR_UNSUPPORTED before anything is launched
+ * (the decode shape D=2048, E=32, K=4, I=1792 fits up to T=58 tokens).
+ * The first call on a device looks the array up (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  Calls that can overlap on one
+ * device -- on different streams, threads or handles -- race on the shared
+ * scratch: serialise them.  Asynchronous; device-side errors are reported by
+ * the next lfm_gpu_moe_sync.  Does not touch the handle's statistics or
+ * profiling records.  No counterpart in the reference. */
+lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                             void *stream);
+
 /* Routing only, for parity checks: RMSNorm + Q8_K + router + top-K of host
  * x[T][D] -> expert ids [T][K], weights [T][K] and, if q8_out != NULL, the
  * Q8_K blocks of the normalised input [T][D/256] (292-byte GGUF layout).

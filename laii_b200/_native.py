@@ -42,6 +42,7 @@ GPU_API = [
     ("lfm_gpu_moe_reserve", c_int, [c_vp, c_u32]),
     ("lfm_gpu_moe_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_int, c_vp]),
     ("lfm_gpu_moe_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_int, c_vp]),
+    ("lfm_gpu_moe_forward_noalloc", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp]),
     ("lfm_gpu_moe_debug_route", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_debug_q4k_rows", c_int, [c_vp, c_vp, c_u32, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_debug_read_layer", c_int, [c_vp, c_u32, c_u32, c_vp, ctypes.c_size_t]),

@@ -13,6 +13,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <vector>
 
 #include "lfm_gpu_moe.h"
@@ -681,5 +682,112 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_profile_read(lfm_gpu_moe_t *h, lfm_gpu_moe_
         ++n;
     }
     *n_out = n;
+    return LFM_GPU_OK;
+}
+
+/* ---- forward without allocation -------------------------------------------
+ * The regular forward grows the handle's scratch on demand, which calls
+ * cudaMalloc after a device-wide synchronisation.  A caller that must not
+ * allocate mid-step (a serving engine with a memory plan fixed at load time, or
+ * one that cannot stall every stream of the device for an allocation) uses
+ * lfm_gpu_moe_forward_noalloc instead: its scratch is the file-scope array
+ * below, whose address is looked up once per device. */
+namespace {
+constexpr size_t kNoAllocBytes = LFM_GPU_MOE_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_base[kNoAllocMaxDevices] = {nullptr};
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+/* Carve the scratch of one layer call (T tokens) out of `b` (nullptr: only
+ * size it).  Returns the bytes used; *counters_end = the leading bytes that
+ * must be zero when the route kernel starts. */
+static size_t noalloc_layout(uint32_t T, const MoeLayerDev &L, uint8_t *b, Workspace *w, size_t *counters_end) {
+    const size_t E = L.E ? L.E : 1, K = lfm_layer_K(L) ? lfm_layer_K(L) : 1;
+    const size_t TK = (size_t)T * K, D = L.D, I = L.I;
+    const size_t n_pairs = E + (TK + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK + 1;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t o_tc = take(sizeof(uint32_t) * T), o_done = take(sizeof(uint32_t));
+    if (counters_end) *counters_end = off;
+    const size_t o_xq = take((size_t)T * D), o_xd = take(sizeof(float) * T * (D / 256)),
+                 o_xb = take(sizeof(int16_t) * T * (D / 256) * 16);
+    const size_t o_idx = take(sizeof(int32_t) * TK), o_w = take(sizeof(float) * TK),
+                 o_cnt = take(sizeof(int32_t) * E), o_off = take(sizeof(int32_t) * (E + 1)),
+                 o_perm = take(sizeof(int32_t) * TK), o_inv = take(sizeof(int32_t) * TK),
+                 o_act = take(sizeof(int32_t) * E), o_pairs = take(sizeof(int2) * n_pairs),
+                 o_sum = take(sizeof(int32_t) * 4), o_log = take(sizeof(float) * T * E);
+    const size_t o_h = take(sizeof(float) * TK * I), o_hq = take(TK * I), o_hd = take(sizeof(float) * TK * (I / 256)),
+                 o_hb = take(sizeof(int16_t) * TK * (I / 256) * 16), o_y = take(sizeof(float) * TK * D);
+    if (!b) return off;
+    w->T = T; w->D = L.D; w->E = (uint32_t)E; w->K = (uint32_t)K; w->I = L.I;
+    w->base = b; w->bytes = off; w->counters_bytes = o_xq;
+    w->x = nullptr;
+    w->xq = Q8Rows{reinterpret_cast<int8_t *>(b + o_xq), reinterpret_cast<float *>(b + o_xd),
+                   reinterpret_cast<int16_t *>(b + o_xb), L.D};
+    w->rt.idx = reinterpret_cast<int32_t *>(b + o_idx);
+    w->rt.w = reinterpret_cast<float *>(b + o_w);
+    w->rt.counts = reinterpret_cast<int32_t *>(b + o_cnt);
+    w->rt.offsets = reinterpret_cast<int32_t *>(b + o_off);
+    w->rt.perm = reinterpret_cast<int32_t *>(b + o_perm);
+    w->rt.inv = reinterpret_cast<int32_t *>(b + o_inv);
+    w->rt.act = reinterpret_cast<int32_t *>(b + o_act);
+    w->rt.pairs = reinterpret_cast<int2 *>(b + o_pairs);
+    w->rt.summary = reinterpret_cast<int32_t *>(b + o_sum);
+    w->rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
+    w->rt.done = reinterpret_cast<uint32_t *>(b + o_done);
+    w->rt.logits = reinterpret_cast<float *>(b + o_log);
+    w->h = reinterpret_cast<float *>(b + o_h);
+    w->hq = Q8Rows{reinterpret_cast<int8_t *>(b + o_hq), reinterpret_cast<float *>(b + o_hd),
+                   reinterpret_cast<int16_t *>(b + o_hb), L.I};
+    w->y = reinterpret_cast<float *>(b + o_y);
+    return off;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                                     void *stream) {
+    if (!h || !x) return LFM_GPU_ERR_INVALID_ARG;
+    if (T == 0) return LFM_GPU_OK;
+    if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
+        return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
+    const MoeLayerDev &L = h->layers[layer].dev;
+    const size_t need = noalloc_layout(T, L, nullptr, nullptr, nullptr);
+    if (T > 65535 || need > kNoAllocBytes)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED,
+                    "forward_noalloc: T=%u on layer %u needs %zu bytes of scratch, above its fixed %zu bytes",
+                    T, layer, need, kNoAllocBytes);
+    if (h->device >= kNoAllocMaxDevices)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "forward_noalloc: device %d above %d", h->device, kNoAllocMaxDevices);
+    DeviceGuard g(h->device);
+    uint8_t *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_base[h->device]) {
+            void *p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || !p) return cuda_fail(h, e, "cudaGetSymbolAddress(noalloc scratch)");
+            g_noalloc_base[h->device] = p;
+        }
+        base = static_cast<uint8_t *>(g_noalloc_base[h->device]);
+    }
+    Workspace w;
+    size_t counters_end = 0;
+    noalloc_layout(T, L, base, &w, &counters_end);
+    w.rt.err = h->dev_err;
+    w.rt.loads = h->loads;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int grid = h->sm_count;
+    const uint32_t K = lfm_layer_K(L);
+    /* the completion counters start every layer at zero (an earlier call that
+     * was abandoned on a device error may have left them part-way) */
+    cudaError_t e = cudaMemsetAsync(base, 0, counters_end, s);
+    if (e == cudaSuccess) e = lfm_launch_route(L, x, T, w.xq, w.rt, s, false);
+    if (e == cudaSuccess) e = lfm_launch_gateup(L, w.xq, w.rt, w.h, grid, s, true);
+    if (e == cudaSuccess) e = lfm_launch_quant_rows(w.h, T * K, L.I, w.hq, s, true);
+    if (e == cudaSuccess) e = lfm_launch_down(L, w.hq, w.rt, w.y, grid, s, true);
+    if (e == cudaSuccess) e = lfm_launch_combine(L, x, T, w.rt, w.y, s, true);
+    if (e != cudaSuccess) return cuda_fail(h, e, "forward_noalloc launch");
     return LFM_GPU_OK;
 }
