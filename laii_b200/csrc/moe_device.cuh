@@ -49,29 +49,6 @@ __device__ __forceinline__ float lfm_warp_max(float v) {
     return v;
 }
 
-/* 6-bit scale and min of sub-blocks 2g and 2g+1 from the 12 scale bytes
- * (three little-endian words s0 = bytes 0-3, s1 = 4-7, s2 = 8-11), without
- * branching on g.  Sub-block j < 4 keeps scale/min in the low 6 bits of byte j
- * and byte j+4; j >= 4 keeps the low nibbles in byte j+4 and the top 2 bits in
- * bits 6-7 of bytes j-4 (scale) and j (min) -- the layout lfm_q4k_scale_min
- * reads.  sh = 16*(g&1) selects the byte pair for both halves. */
-__device__ __forceinline__ void lfm_q4k_pair_scales(uint32_t s0, uint32_t s1, uint32_t s2, int g, int &sc_lo,
-                                                    int &m_lo, int &sc_hi, int &m_hi) {
-    const uint32_t sh = 16u * (uint32_t)(g & 1);
-    const uint32_t a0 = s0 >> sh, a1 = s1 >> sh, a2 = s2 >> sh;
-    if (g < 2) {  /* uniform per quarter-warp group of 4 lanes; both sides are a handful of ops */
-        sc_lo = (int)(a0 & 63u);
-        sc_hi = (int)((a0 >> 8) & 63u);
-        m_lo = (int)(a1 & 63u);
-        m_hi = (int)((a1 >> 8) & 63u);
-    } else {
-        sc_lo = (int)((a2 & 15u) | (((a0 >> 6) & 3u) << 4));
-        sc_hi = (int)(((a2 >> 8) & 15u) | (((a0 >> 14) & 3u) << 4));
-        m_lo = (int)(((a2 >> 4) & 15u) | (((a1 >> 6) & 3u) << 4));
-        m_hi = (int)(((a2 >> 12) & 15u) | (((a1 >> 14) & 3u) << 4));
-    }
-}
-
 /* ------------------------------------------------------------------------
  * mbarrier + bulk-copy (TMA, non-tensor) + programmatic dependent launch
  * ------------------------------------------------------------------------ */
@@ -170,63 +147,8 @@ __device__ __forceinline__ void lfm_bar_sync(int id, int threads) {
 }
 
 /* ------------------------------------------------------------------------
- * Q4_K x Q8_K: 8 weight rows per warp
+ * Q4_K x Q8_K: one super-block per lane
  * ------------------------------------------------------------------------ */
-
-struct RowDebug {
-    int32_t *sub_dots;  /* [8 rows][nb][8] or NULL */
-    int32_t *acc;       /* [8 rows][nb] */
-    int32_t *mins;      /* [8 rows][nb] */
-};
-
-/* Q8_K activation rows staged in shared memory for one (expert, chunk) pair:
- *   qs  [nt][cols]   within each 256-byte super-block, the 16-byte chunk
- *                    (group g, part k) -- bytes 64g+16k.. -- is stored at
- *                    chunk 4k+g, so the 4 lane groups of a warp reading part k
- *                    hit 4 distinct bank groups (and the 8 rows broadcast);
- *   bs  [nt][nb][16] bsums;   d [nt][nb] scales. */
-struct ActSmem {
-    const uint8_t *qs;
-    const int16_t *bs;
-    const float *d;
-    uint32_t cols, nb;
-};
-
-__host__ __device__ constexpr size_t lfm_act_slot_bytes(uint32_t cols) {
-    return (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * (cols / 256) * 36;
-}
-
-__device__ __forceinline__ ActSmem lfm_act_slot(const uint8_t *base, uint32_t cols) {
-    const uint32_t nb = cols / 256;
-    return ActSmem{base, reinterpret_cast<const int16_t *>(base + (size_t)LFM_GEMV_CHUNK * cols),
-                   reinterpret_cast<const float *>(base + (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * nb * 32),
-                   cols, nb};
-}
-
-/* Copy nt Q8 rows (global row ids rows[t]) into a slot; threads tid of nthr. */
-__device__ __forceinline__ void lfm_stage_act(const Q8Rows &src, const int *rows, int nt, uint8_t *slot, int tid,
-                                              int nthr) {
-    const uint32_t cols = src.cols, nb = cols / 256, qv = cols / 16;
-    uint8_t *qs = slot;
-    int16_t *bs = reinterpret_cast<int16_t *>(slot + (size_t)LFM_GEMV_CHUNK * cols);
-    float *dd = reinterpret_cast<float *>(slot + (size_t)LFM_GEMV_CHUNK * cols + (size_t)LFM_GEMV_CHUNK * nb * 32);
-    for (uint32_t q = tid; q < (uint32_t)nt * qv; q += nthr) {
-        const uint32_t t = q / qv, c = q % qv;
-        const uint32_t sb = c >> 4, gk = c & 15;             /* logical chunk 4g+k of super-block sb */
-        const uint32_t phys = sb * 16 + (gk & 3) * 4 + (gk >> 2);
-        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src.qs + (size_t)rows[t] * cols) + c);
-        reinterpret_cast<uint4 *>(qs + (size_t)t * cols)[phys] = v;
-    }
-    for (uint32_t q = tid; q < (uint32_t)nt * nb * 2; q += nthr) {
-        const uint32_t t = q / (nb * 2), c = q % (nb * 2);
-        reinterpret_cast<uint4 *>(bs + (size_t)t * nb * 16)[c] =
-            __ldcg(reinterpret_cast<const uint4 *>(src.bs + (size_t)rows[t] * nb * 16) + c);
-    }
-    for (uint32_t q = tid; q < (uint32_t)nt * nb; q += nthr) {
-        const uint32_t t = q / nb, c = q % nb;
-        dd[(size_t)t * nb + c] = __ldcg(src.d + (size_t)rows[t] * nb + c);
-    }
-}
 
 /* 16-byte load from shared memory (kShared) or through a generic pointer. */
 template <bool kShared>
@@ -241,129 +163,172 @@ __device__ __forceinline__ uint4 lfm_ld16(const uint8_t *p) {
     return *reinterpret_cast<const uint4 *>(p);
 }
 
-/*
- * Dots of 8 consecutive Q4_K weight rows (row r at w + r*rstride, shared memory
- * when kSharedW) -- and, for kMats == 2, of the 8 rows at w1 -- with nt (<= 8)
- * staged Q8_K activation rows.
- *
- * Lane 4*r + g owns weight row r and the 32 nibble bytes of group g (sub-blocks
- * 2g and 2g+1) of every super-block.  For each super-block b in order and each
- * token: sub-block dots with __dp4a, the exact integer super-block sums
- *   acc = sum_j sc_j * dot_j,   mins = sum_j m_j * (bsum_{2j} + bsum_{2j+1})
- * (reduced over the row's 4 lanes; integer, so any order), then the fp32 update
- * of the reference's 4-row AVX-VNNI kernel (tools/lfm2_cpuid_quants.c:1189-1257):
- *   sum = fma(d8*d, acc, fma(-(d8*dmin), mins, sum)),  skipped when d8 == 0.
- * The running sums stay in registers; every lane of a row ends with the row's
- * results s0[t] (and s1[t]).
- */
-template <int kMats, bool kDebug, bool kSharedW = true>
-__device__ __forceinline__ void lfm_q4k_rows8(const uint8_t *w0, const uint8_t *w1, uint32_t rstride,
-                                              const ActSmem &act, int nt, float (&s0)[LFM_GEMV_CHUNK],
-                                              float (&s1)[LFM_GEMV_CHUNK], RowDebug dbg) {
-    const int lane = threadIdx.x & 31;
-    const int r = lane >> 2, g = lane & 3;
-    const uint32_t nb = act.nb;
-    const uint8_t *row0 = w0 + (size_t)r * rstride;
-    const uint8_t *row1 = kMats == 2 ? w1 + (size_t)r * rstride : nullptr;
-#pragma unroll
-    for (int t = 0; t < LFM_GEMV_CHUNK; ++t) { s0[t] = 0.0f; s1[t] = 0.0f; }
-    for (uint32_t b = 0; b < nb; ++b) {
-        int sc0l, m0l, sc0h, m0h, sc1l = 0, m1l = 0, sc1h = 0, m1h = 0;
-        uint32_t wl0[8], wh0[8], wl1[8], wh1[8];
-        float d0, dm0, d1 = 0.0f, dm1 = 0.0f;
-        {
-            const uint8_t *blk = row0 + (size_t)b * LFM_Q4K_BYTES;
-            const uint4 hdr = lfm_ld16<kSharedW>(blk);
-            const uint4 qa = lfm_ld16<kSharedW>(blk + 16 + 32 * g);
-            const uint4 qb = lfm_ld16<kSharedW>(blk + 32 + 32 * g);
-            lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc0l, m0l, sc0h, m0h);
-            d0 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
-            dm0 = lfm_h2f((uint16_t)(hdr.x >> 16));
-            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { wl0[i] = w[i] & 0x0F0F0F0Fu; wh0[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
-        }
-        if (kMats == 2) {
-            const uint8_t *blk = row1 + (size_t)b * LFM_Q4K_BYTES;
-            const uint4 hdr = lfm_ld16<kSharedW>(blk);
-            const uint4 qa = lfm_ld16<kSharedW>(blk + 16 + 32 * g);
-            const uint4 qb = lfm_ld16<kSharedW>(blk + 32 + 32 * g);
-            lfm_q4k_pair_scales(hdr.y, hdr.z, hdr.w, g, sc1l, m1l, sc1h, m1h);
-            d1 = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu));
-            dm1 = lfm_h2f((uint16_t)(hdr.x >> 16));
-            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { wl1[i] = w[i] & 0x0F0F0F0Fu; wh1[i] = (w[i] >> 4) & 0x0F0F0F0Fu; }
-        }
-#pragma unroll
-        for (int t = 0; t < LFM_GEMV_CHUNK; ++t) {
-            if (t < nt) {
-                /* this lane's 64 activation bytes: parts k = 0..3 of group g, at chunks 4k+g */
-                const uint8_t *xb = act.qs + (size_t)t * act.cols + 256 * b + 16 * g;
-                const uint4 x0 = lfm_ld16<true>(xb), x1 = lfm_ld16<true>(xb + 64);
-                const uint4 x2 = lfm_ld16<true>(xb + 128), x3 = lfm_ld16<true>(xb + 192);
-                uint2 bw;
-                float d8;
-                asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                             : "=r"(bw.x), "=r"(bw.y)
-                             : "r"(lfm_smem_u32(act.bs + ((size_t)t * nb + b) * 16 + 4 * g)));
-                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(d8) : "r"(lfm_smem_u32(act.d + (size_t)t * nb + b)));
-                const int xl[8] = {(int)x0.x, (int)x0.y, (int)x0.z, (int)x0.w, (int)x1.x, (int)x1.y, (int)x1.z, (int)x1.w};
-                const int xh[8] = {(int)x2.x, (int)x2.y, (int)x2.z, (int)x2.w, (int)x3.x, (int)x3.y, (int)x3.z, (int)x3.w};
-                const int bp0 = (int)(int16_t)(bw.x & 0xFFFFu) + (int)(int16_t)(bw.x >> 16);
-                const int bp1 = (int)(int16_t)(bw.y & 0xFFFFu) + (int)(int16_t)(bw.y >> 16);
-                /* four independent 2-deep chains per sum (exact integers: any order) */
-                int pl0[4], ph0[4], pl1[4], ph1[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    pl0[i] = __dp4a((int)wl0[i + 4], xl[i + 4], __dp4a((int)wl0[i], xl[i], 0));
-                    ph0[i] = __dp4a((int)wh0[i + 4], xh[i + 4], __dp4a((int)wh0[i], xh[i], 0));
-                    if (kMats == 2) {
-                        pl1[i] = __dp4a((int)wl1[i + 4], xl[i + 4], __dp4a((int)wl1[i], xl[i], 0));
-                        ph1[i] = __dp4a((int)wh1[i + 4], xh[i + 4], __dp4a((int)wh1[i], xh[i], 0));
-                    }
-                }
-                const int dl0 = (pl0[0] + pl0[1]) + (pl0[2] + pl0[3]);
-                const int dh0 = (ph0[0] + ph0[1]) + (ph0[2] + ph0[3]);
-                const int dl1 = kMats == 2 ? (pl1[0] + pl1[1]) + (pl1[2] + pl1[3]) : 0;
-                const int dh1 = kMats == 2 ? (ph1[0] + ph1[1]) + (ph1[2] + ph1[3]) : 0;
-                if (kDebug && dbg.sub_dots) {
-                    dbg.sub_dots[((size_t)r * nb + b) * 8 + 2 * g] = dl0;
-                    dbg.sub_dots[((size_t)r * nb + b) * 8 + 2 * g + 1] = dh0;
-                }
-                int a0 = sc0l * dl0 + sc0h * dh0, n0 = m0l * bp0 + m0h * bp1;
-                int a1 = sc1l * dl1 + sc1h * dh1, n1 = m1l * bp0 + m1h * bp1;
-                a0 += __shfl_xor_sync(LFM_FULL_MASK, a0, 1);
-                n0 += __shfl_xor_sync(LFM_FULL_MASK, n0, 1);
-                if (kMats == 2) {
-                    a1 += __shfl_xor_sync(LFM_FULL_MASK, a1, 1);
-                    n1 += __shfl_xor_sync(LFM_FULL_MASK, n1, 1);
-                }
-                a0 += __shfl_xor_sync(LFM_FULL_MASK, a0, 2);
-                n0 += __shfl_xor_sync(LFM_FULL_MASK, n0, 2);
-                if (kMats == 2) {
-                    a1 += __shfl_xor_sync(LFM_FULL_MASK, a1, 2);
-                    n1 += __shfl_xor_sync(LFM_FULL_MASK, n1, 2);
-                }
-                if (kDebug && dbg.acc && g == 0) {
-                    dbg.acc[(size_t)r * nb + b] = a0;
-                    dbg.mins[(size_t)r * nb + b] = n0;
-                }
-                if (d8 != 0.0f) {
-                    s0[t] = __fmaf_rn(__fmul_rn(d8, d0), (float)a0, __fmaf_rn(-__fmul_rn(d8, dm0), (float)n0, s0[t]));
-                    if (kMats == 2)
-                        s1[t] = __fmaf_rn(__fmul_rn(d8, d1), (float)a1, __fmaf_rn(-__fmul_rn(d8, dm1), (float)n1, s1[t]));
-                }
-            }
+/* Q8_K activation rows staged in shared memory, one 304-byte record per
+ * (row, super-block):  [0,256) codes, [256,288) the 16 bsums, [288,292) d.
+ * Records of a row are consecutive (row stride nb*304), so lane h of a row
+ * group reading super-block 8p+h hits bank group (3h + j) mod 8 for 16-byte
+ * chunk j: the 8 super-block lanes of a warp never conflict, every offset
+ * inside a record is an immediate, and the 4 row groups read the same
+ * addresses (broadcast). */
+#define LFM_ACT_REC 304u
+
+struct ActSlot {
+    const uint8_t *rec;  /* row 0, super-block 0 */
+    uint32_t nb;
+};
+
+__host__ __device__ constexpr size_t lfm_act_slot_bytes(uint32_t cols, uint32_t rows_cap = LFM_GEMV_CHUNK) {
+    return (size_t)rows_cap * (cols / 256) * LFM_ACT_REC;
+}
+
+__device__ __forceinline__ ActSlot lfm_act_slot(const uint8_t *base, uint32_t cols) { return ActSlot{base, cols / 256}; }
+
+/* Copy nt Q8 rows (global row ids rows[t]) into a slot; threads tid of nthr. */
+__device__ __forceinline__ void lfm_stage_act(const Q8Rows &src, const int *rows, int nt, uint8_t *slot, int tid,
+                                              int nthr) {
+    const uint32_t cols = src.cols, nb = cols / 256;
+    /* 19 16-byte pieces per record: 16 of codes, 2 of bsums, then d (4 bytes) */
+    const uint32_t per_row = nb * 19;
+    for (uint32_t q = tid; q < (uint32_t)nt * per_row; q += nthr) {
+        const uint32_t t = q / per_row, r = q % per_row, b = r / 19, j = r % 19;
+        const size_t row = (size_t)rows[t];
+        uint8_t *dst = slot + ((size_t)t * nb + b) * LFM_ACT_REC + 16 * j;
+        if (j < 16) {
+            *reinterpret_cast<uint4 *>(dst) = __ldcg(reinterpret_cast<const uint4 *>(src.qs + row * cols + 256 * b) + j);
+        } else if (j < 18) {
+            *reinterpret_cast<uint4 *>(dst) =
+                __ldcg(reinterpret_cast<const uint4 *>(src.bs + (row * nb + b) * 16) + (j - 16));
+        } else {
+            *reinterpret_cast<float *>(dst) = __ldcg(src.d + row * nb + b);
         }
     }
 }
 
-/* Shared-memory row stride of staged weight rows: rows stay contiguous so an
- * item is one bulk copy per matrix (the two rows a quarter-warp reads may share
- * a bank group: a 2-way conflict on 3 loads per super-block, cheaper than 8
- * copies per matrix). */
-__host__ __device__ inline uint32_t lfm_stage_stride(uint32_t row_bytes) { return row_bytes; }
+/* 32-bit load from shared memory. */
+__device__ __forceinline__ uint32_t lfm_lds32(const uint8_t *p) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(lfm_smem_u32(p)));
+    return v;
+}
+
+/* sum of 4 products of unsigned bytes of a with signed bytes of b, plus c */
+__device__ __forceinline__ int lfm_dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+/*
+ * One Q4_K super-block (the 144 bytes at w) against super-block b of kNt staged
+ * Q8_K rows (records rec, rec + tstride, ...), as the reference's Q4_K x Q8_K
+ * row kernels form it (tools/lfm2_cpuid_quants.c:421-457, :1189-1257):
+ *   dot_j   = sum_{l<32} q4[32j+l] * q8[32j+l]          (sub-block j = 0..7)
+ *   acc     = sum_j sc_j * dot_j
+ *   mins    = sum_j m_j * (bsum[2j] + bsum[2j+1])
+ * and the operands of its fp32 update  sum = fma(d8*d, acc, fma(-(d8*dmin), mins, sum)):
+ *   out[t] = (d8*d, (float)acc, d8*dmin, (float)mins),
+ * or (-0, 0, 0, 0) -- an exact identity of that update -- when d8 == 0 (the
+ * reference skips such blocks).  Nibble layout: byte l of 32-byte group c
+ * holds element l of sub-block 2c (low nibble) and of 2c+1 (high nibble); the
+ * high nibbles are used in place (w & 0xF0F0F0F0 = 16 * nibble, unsigned) and
+ * the exact dot divided by 16 afterwards.  Integers: the order is free.
+ * kDebug: dbg[0..7] = token 0's sub-block dots, dbg[8] = acc, dbg[9] = mins.
+ */
+template <int kNt, bool kSharedW, bool kDebug>
+__device__ __forceinline__ void lfm_q4k_sb(const uint8_t *w, const uint8_t *rec, uint32_t tstride, float4 (&out)[kNt],
+                                           int32_t *dbg) {
+    const uint4 hdr = lfm_ld16<kSharedW>(w);
+    const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+    /* 6-bit scales and mins of sub-blocks 0-3 (low 6 bits of bytes 0-3 / 4-7)
+     * and 4-7 (low / high nibble of bytes 8-11, top 2 bits from bytes 0-3 / 4-7) */
+    const uint32_t scA = s0 & 0x3F3F3F3Fu;
+    const uint32_t scB = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+    const uint32_t mA = s1 & 0x3F3F3F3Fu;
+    const uint32_t mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+    /* m_j duplicated into the byte pair __dp2a multiplies bsum 2j and 2j+1 by */
+    const int mm0 = (int)__byte_perm(mA, 0, 0x1100), mm1 = (int)__byte_perm(mA, 0, 0x3322);
+    const int mm2 = (int)__byte_perm(mB, 0, 0x1100), mm3 = (int)__byte_perm(mB, 0, 0x3322);
+    int acc[kNt];
+#pragma unroll
+    for (int t = 0; t < kNt; ++t) acc[t] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 qa = lfm_ld16<kSharedW>(w + 16 + 32 * c), qb = lfm_ld16<kSharedW>(w + 32 + 32 * c);
+        const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        int lo[8];
+        uint32_t hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo[i] = (int)(q[i] & 0x0F0F0F0Fu);
+            hi[i] = q[i] & 0xF0F0F0F0u;
+        }
+        const int sc_lo = (int)(((c < 2 ? scA : scB) >> (16 * (c & 1))) & 0xFFu);
+        const int sc_hi = (int)(((c < 2 ? scA : scB) >> (16 * (c & 1) + 8)) & 0xFFu);
+#pragma unroll
+        for (int t = 0; t < kNt; ++t) {
+            const uint8_t *xr = rec + (size_t)t * tstride + 64 * c;
+            const uint4 x0 = lfm_ld16<true>(xr), x1 = lfm_ld16<true>(xr + 16);
+            const uint4 x2 = lfm_ld16<true>(xr + 32), x3 = lfm_ld16<true>(xr + 48);
+            int dl = __dp4a(lo[0], (int)x0.x, 0);
+            dl = __dp4a(lo[1], (int)x0.y, dl);
+            dl = __dp4a(lo[2], (int)x0.z, dl);
+            dl = __dp4a(lo[3], (int)x0.w, dl);
+            dl = __dp4a(lo[4], (int)x1.x, dl);
+            dl = __dp4a(lo[5], (int)x1.y, dl);
+            dl = __dp4a(lo[6], (int)x1.z, dl);
+            dl = __dp4a(lo[7], (int)x1.w, dl);
+            int dh = lfm_dp4a_us(hi[0], (int)x2.x, 0);
+            dh = lfm_dp4a_us(hi[1], (int)x2.y, dh);
+            dh = lfm_dp4a_us(hi[2], (int)x2.z, dh);
+            dh = lfm_dp4a_us(hi[3], (int)x2.w, dh);
+            dh = lfm_dp4a_us(hi[4], (int)x3.x, dh);
+            dh = lfm_dp4a_us(hi[5], (int)x3.y, dh);
+            dh = lfm_dp4a_us(hi[6], (int)x3.z, dh);
+            dh = lfm_dp4a_us(hi[7], (int)x3.w, dh);
+            dh >>= 4; /* exact: a multiple of 16 */
+            acc[t] += sc_lo * dl + sc_hi * dh;
+            if (kDebug && t == 0) {
+                dbg[2 * c] = dl;
+                dbg[2 * c + 1] = dh;
+            }
+        }
+    }
+    const float d = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu)), dmin = lfm_h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+    for (int t = 0; t < kNt; ++t) {
+        const uint8_t *xr = rec + (size_t)t * tstride;
+        const uint4 p0 = lfm_ld16<true>(xr + 256), p1 = lfm_ld16<true>(xr + 272);
+        const float d8 = __uint_as_float(lfm_lds32(xr + 288));
+        int mins = __dp2a_lo((int)p0.x, mm0, 0);
+        mins = __dp2a_hi((int)p0.y, mm0, mins);
+        mins = __dp2a_lo((int)p0.z, mm1, mins);
+        mins = __dp2a_hi((int)p0.w, mm1, mins);
+        mins = __dp2a_lo((int)p1.x, mm2, mins);
+        mins = __dp2a_hi((int)p1.y, mm2, mins);
+        mins = __dp2a_lo((int)p1.z, mm3, mins);
+        mins = __dp2a_hi((int)p1.w, mm3, mins);
+        if (kDebug && t == 0) {
+            dbg[8] = acc[0];
+            dbg[9] = mins;
+        }
+        out[t] = d8 != 0.0f ? make_float4(__fmul_rn(d8, d), (float)acc[t], __fmul_rn(d8, dmin), (float)mins)
+                            : make_float4(-0.0f, 0.0f, 0.0f, 0.0f);
+    }
+}
+
+/* The reference's fp32 update over n super-blocks in order, from the operands
+ * lfm_q4k_sb produced: e = (d8*d, acc, d8*dmin, mins) at e0, e0 + estride, ... */
+__device__ __forceinline__ float lfm_q4k_chain(float sum, const uint8_t *e0, uint32_t estride, uint32_t n) {
+#pragma unroll
+    for (uint32_t h = 0; h < 8; ++h) {
+        if (h < n) {
+            const uint4 v = lfm_ld16<true>(e0 + (size_t)h * estride);
+            sum = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y),
+                            __fmaf_rn(-__uint_as_float(v.z), __uint_as_float(v.w), sum));
+        }
+    }
+    return sum;
+}
 
 /* Q8_K of one 256-value block held 8 per lane (values v[], elements 8*lane..):
  * d = max/127, q = RNE(x*(127/max)), bsums of the unsaturated codes

@@ -23,7 +23,6 @@
 #define LFM_GPU_MAX_EXPERTS_DEV 256
 #define LFM_GPU_MAX_D 8192      /* router stages 5*D fp32 in shared memory     */
 #define LFM_GEMV_CHUNK 8        /* tokens per staged activation chunk (GEMV)   */
-#define LFM_GEMV_ROWS 8         /* weight rows per pipeline stage (one per consumer warp) */
 
 /* Device error word bits (read by lfm_gpu_moe_sync and the host-buffer forward). */
 #define LFM_DEVERR_EXPERT_ID 0x1u   /* routing produced an expert id >= E     */
