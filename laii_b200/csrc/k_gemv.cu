@@ -111,7 +111,10 @@ template <int kNt>
 __device__ __forceinline__ void unit_ints(const uint8_t *wsb, const uint8_t *rec, uint32_t tstride, bool act,
                                           uint8_t *st, int g, int h) {
     float4 o[kNt];
-    if (act) lfm_q4k_sb<kNt, true, false>(wsb, rec, tstride, o, nullptr);
+    uint32_t toff[kNt];
+#pragma unroll
+    for (int t = 0; t < kNt; ++t) toff[t] = (uint32_t)t * tstride;
+    if (act) lfm_q4k_sb<kNt, true, false>(wsb, rec, toff, o, nullptr);
     __syncwarp();
     if (act) {
 #pragma unroll
@@ -307,8 +310,9 @@ __global__ void __launch_bounds__(256) k_debug_rows(const uint8_t *__restrict__ 
             if ((uint32_t)h < nsb) {
                 int32_t dbg[10];
                 float4 e[1];
+                const uint32_t toff[1] = {0};
                 lfm_q4k_sb<1, false, true>(w + row * row_bytes + (size_t)b * LFM_Q4K_BYTES, slot + (size_t)b * LFM_ACT_REC,
-                                           0, e, dbg);
+                                           toff, e, dbg);
                 for (int j = 0; j < 8; ++j) sub_dots[(o * nb + b) * 8 + j] = dbg[j];
                 acc_out[o * nb + b] = dbg[8];
                 mins_out[o * nb + b] = dbg[9];

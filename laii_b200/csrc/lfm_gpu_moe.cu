@@ -41,13 +41,14 @@ struct Workspace {
     float *h = nullptr;       /* [T*K][I]                              */
     Q8Rows hq{};              /* [T*K] x I                             */
     float *y = nullptr;       /* [T*K][D]                              */
+    unsigned *gbar = nullptr; /* [2] grid barrier of the fused layer (counter region) */
 };
 
 }  // namespace
 
 namespace {
-enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_COUNT };
-const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine"};
+enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_COUNT };
+const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -75,6 +76,7 @@ struct lfm_gpu_moe {
     bool prof = false;
     std::vector<ProfRec> recs;
     bool use_graphs = true;
+    bool use_fused = true;   /* fused decode layer for T <= LFM_FUSED_MAX_T */
     std::vector<GraphEntry> graphs;
 };
 
@@ -149,6 +151,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     /* counters first: one memset covers them */
     const size_t o_tc = take(sizeof(uint32_t) * T);
     const size_t o_done = take(sizeof(uint32_t));
+    const size_t o_gbar = take(sizeof(uint32_t) * 2);
     const size_t counters_end = off;
     const size_t o_x = take(sizeof(float) * T * D);
     const size_t o_xq = take((size_t)T * D);
@@ -203,6 +206,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.hq = Q8Rows{reinterpret_cast<int8_t *>(b + o_hq), reinterpret_cast<float *>(b + o_hd),
                   reinterpret_cast<int16_t *>(b + o_hb), 0};
     w.y = reinterpret_cast<float *>(b + o_y);
+    w.gbar = reinterpret_cast<unsigned *>(b + o_gbar);
     return LFM_GPU_OK;
 }
 
@@ -243,7 +247,8 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
 }
 
 /* One layer forward on device x; `stream` already resolved.
- *   route(+dispatch) -> gate|up(+SwiGLU) -> h->Q8_K -> down -> combine
+ * T <= LFM_FUSED_MAX_T: one cooperative launch of the fused layer (k_layer.cu).
+ * Otherwise route(+dispatch) -> gate|up(+SwiGLU) -> h->Q8_K -> down -> combine
  * chained with programmatic dependent launch.
  * Profiling brackets each launch with events, which breaks the PDL overlap,
  * so it is turned off while profiling. */
@@ -255,6 +260,10 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
     const bool pdl = !h->prof;
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
+    if (h->use_fused && lfm_fused_ok(L, T, grid)) {
+        LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, grid, s); }));
+        return LFM_GPU_OK;
+    }
     LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
     LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, xq, w.rt, w.h, grid, s, pdl); }));
     LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * K, L.I, hq, s, pdl); }));
@@ -284,6 +293,10 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
     lfm_gpu_moe_t *h = new (std::nothrow) lfm_gpu_moe_t();
     if (!h) return LFM_GPU_ERR_OOM;
     h->device = device_id;
+    {
+        const char *nf = getenv("LFM_GPU_MOE_NO_FUSED"); /* force the separate-kernel path (A/B runs) */
+        h->use_fused = !(nf && nf[0] && nf[0] != '0');
+    }
     DeviceGuard g(device_id);
     if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess ||
         h->sm_count <= 0)
@@ -489,6 +502,8 @@ static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_
     if (!h || !x) return LFM_GPU_ERR_INVALID_ARG;
     if (T == 0) return LFM_GPU_OK;
     if (T > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "T=%u above 65535 tokens per call", T);
+    if (x_on_device && (reinterpret_cast<uintptr_t>(x) & 15u))
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "device x must be 16-byte aligned (bulk copies read it)");
     if (n == 0 || first >= LFM_GPU_MOE_MAX_LAYERS || n > LFM_GPU_MOE_MAX_LAYERS - first)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer range [%u, %u+%u) invalid", first, first, n);
     uint32_t D = 0, E = 1, K = 1, I = 0;
@@ -750,6 +765,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t 
                                                      void *stream) {
     if (!h || !x) return LFM_GPU_ERR_INVALID_ARG;
     if (T == 0) return LFM_GPU_OK;
+    if (reinterpret_cast<uintptr_t>(x) & 15u)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "device x must be 16-byte aligned (bulk copies read it)");
     if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
         return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
     const MoeLayerDev &L = h->layers[layer].dev;

@@ -220,7 +220,7 @@ __device__ __forceinline__ int lfm_dp4a_us(uint32_t a, int b, int c) {
 
 /*
  * One Q4_K super-block (the 144 bytes at w) against super-block b of kNt staged
- * Q8_K rows (records rec, rec + tstride, ...), as the reference's Q4_K x Q8_K
+ * Q8_K rows (records rec + toff[t]), as the reference's Q4_K x Q8_K
  * row kernels form it (tools/lfm2_cpuid_quants.c:421-457, :1189-1257):
  *   dot_j   = sum_{l<32} q4[32j+l] * q8[32j+l]          (sub-block j = 0..7)
  *   acc     = sum_j sc_j * dot_j
@@ -235,8 +235,8 @@ __device__ __forceinline__ int lfm_dp4a_us(uint32_t a, int b, int c) {
  * kDebug: dbg[0..7] = token 0's sub-block dots, dbg[8] = acc, dbg[9] = mins.
  */
 template <int kNt, bool kSharedW, bool kDebug>
-__device__ __forceinline__ void lfm_q4k_sb(const uint8_t *w, const uint8_t *rec, uint32_t tstride, float4 (&out)[kNt],
-                                           int32_t *dbg) {
+__device__ __forceinline__ void lfm_q4k_sb(const uint8_t *w, const uint8_t *rec, const uint32_t (&toff)[kNt],
+                                           float4 (&out)[kNt], int32_t *dbg) {
     const uint4 hdr = lfm_ld16<kSharedW>(w);
     const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
     /* 6-bit scales and mins of sub-blocks 0-3 (low 6 bits of bytes 0-3 / 4-7)
@@ -266,7 +266,7 @@ __device__ __forceinline__ void lfm_q4k_sb(const uint8_t *w, const uint8_t *rec,
         const int sc_hi = (int)(((c < 2 ? scA : scB) >> (16 * (c & 1) + 8)) & 0xFFu);
 #pragma unroll
         for (int t = 0; t < kNt; ++t) {
-            const uint8_t *xr = rec + (size_t)t * tstride + 64 * c;
+            const uint8_t *xr = rec + toff[t] + 64 * c;
             const uint4 x0 = lfm_ld16<true>(xr), x1 = lfm_ld16<true>(xr + 16);
             const uint4 x2 = lfm_ld16<true>(xr + 32), x3 = lfm_ld16<true>(xr + 48);
             int dl = __dp4a(lo[0], (int)x0.x, 0);
@@ -296,7 +296,7 @@ __device__ __forceinline__ void lfm_q4k_sb(const uint8_t *w, const uint8_t *rec,
     const float d = lfm_h2f((uint16_t)(hdr.x & 0xFFFFu)), dmin = lfm_h2f((uint16_t)(hdr.x >> 16));
 #pragma unroll
     for (int t = 0; t < kNt; ++t) {
-        const uint8_t *xr = rec + (size_t)t * tstride;
+        const uint8_t *xr = rec + toff[t];
         const uint4 p0 = lfm_ld16<true>(xr + 256), p1 = lfm_ld16<true>(xr + 272);
         const float d8 = __uint_as_float(lfm_lds32(xr + 288));
         int mins = __dp2a_lo((int)p0.x, mm0, 0);
@@ -328,6 +328,35 @@ __device__ __forceinline__ float lfm_q4k_chain(float sum, const uint8_t *e0, uin
         }
     }
     return sum;
+}
+
+/* Q8_K of one 256-value block held 8 per lane (elements 8*lane..8*lane+7),
+ * written as a 304-byte activation record in shared memory: d = max/127,
+ * q = RNE(x*(127/max)) saturated to int8, bsums of the unsaturated codes
+ * (tools/lfm2_cpuid_quants.c:584-631). */
+__device__ __forceinline__ void lfm_quant_block_rec(const float v[8], uint8_t *rec) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = lfm_warp_max(amax);
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int part = 0;
+    if (amax != 0.0f) {
+        const float sc = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { q[i] = __float2int_rn(__fmul_rn(v[i], sc)); part += q[i]; }
+    }
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[i])) << (8 * i);
+        hi |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[4 + i])) << (8 * i);
+    }
+    *reinterpret_cast<uint2 *>(rec + 8 * lane) = make_uint2(lo, hi);
+    const int pair = part + __shfl_xor_sync(LFM_FULL_MASK, part, 1);
+    if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(rec + 256 + lane) = (int16_t)pair;
+    if (lane == 0) *reinterpret_cast<float *>(rec + 288) = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
 }
 
 /* Q8_K of one 256-value block held 8 per lane (values v[], elements 8*lane..):

@@ -23,6 +23,7 @@
 #define LFM_GPU_MAX_EXPERTS_DEV 256
 #define LFM_GPU_MAX_D 8192      /* router stages 5*D fp32 in shared memory     */
 #define LFM_GEMV_CHUNK 8        /* tokens per staged activation chunk (GEMV)   */
+#define LFM_FUSED_MAX_T 16      /* largest T the fused decode layer handles    */
 
 /* Device error word bits (read by lfm_gpu_moe_sync and the host-buffer forward). */
 #define LFM_DEVERR_EXPERT_ID 0x1u   /* routing produced an expert id >= E     */
@@ -80,6 +81,12 @@ cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q
 
 /* k_expert.cu */
 size_t lfm_gemv_smem(uint32_t cols, uint32_t mats);
+
+/* Fused decode layer (k_layer.cu): whether (layer, T) fits it, and its
+ * cooperative launch on `grid` CTAs (one per SM). gbar: 2 zeroed words. */
+bool lfm_fused_ok(const MoeLayerDev &L, uint32_t T, int grid);
+cudaError_t lfm_launch_layer_fused(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, float *h,
+                                   float *y, unsigned *gbar, int grid, cudaStream_t s);
 cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables &rt, float *h, int grid,
                               cudaStream_t s, bool pdl);
 cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s, bool pdl);
