@@ -9,12 +9,13 @@
  * barriers (arrival counter + generation word in global memory, bounded
  * waits) and every CTA keeps the routing tables in its own shared memory:
  *
- *  1. router logits, distributed: CTA c scores (token, expert) pairs
- *     [c*T*E/G, (c+1)*T*E/G), one half-warp per pair, RMSNorm and dot in the
- *     reference's 16-lane order (tools/lfm2_decode_1x4.c:98-133,
- *     include/lfm2_simd_avx2.h:676-687); logits to global; grid barrier.
- *     While waiting, every CTA builds the Q8_K records of all T normalised
- *     rows in shared memory (tools/lfm2_decode_1x4.c:150-186).
+ *  1. x, ffn_norm and the CTA's router rows are bulk-copied into shared
+ *     memory; RMSNorm in the reference's 16-lane order, xb = (x*inv)*w
+ *     (tools/lfm2_decode_1x4.c:98-133); router logits distributed: CTA c
+ *     scores dots [c*T*E/G, (c+1)*T*E/G) (expert-major, one half-warp each,
+ *     include/lfm2_simd_avx2.h:676-687) and quantises its share of the T*D/256
+ *     Q8_K records (tools/lfm2_decode_1x4.c:150-186); both go to global
+ *     memory; grid barrier; every CTA bulk-copies all records back.
  *  2. every CTA reads the T*E logits and computes, identically, the biased
  *     top-K and weights (tools/lfm2_moe_checkpoint.c:183-239) and the dispatch
  *     tables: per-expert counts, offsets, a slot order that is a pure function
@@ -29,8 +30,8 @@
  *     4-row) items; y to global; grid barrier.
  *  5. combine: x[t][r] = fma(w_k, y[slot(t,k)][r], x[t][r]) for k in order
  *     (tools/lfm2_moe_checkpoint.c:266-269), the CTA's slice of T*D.
- * Dense layers skip 1-2: every token goes to expert 0 with weight 1, so the
- * combine is x + down exactly (tools/lfm2_decode_1x4.c:1086-1103).
+ * Dense layers skip the router: every token goes to expert 0 with weight 1,
+ * so the combine is x + down exactly (tools/lfm2_decode_1x4.c:1086-1103).
  *
  * Co-residency of all CTAs is guaranteed by the cooperative launch.  Every
  * wait (mbarrier or grid barrier) is bounded; after a timeout the CTA stops
@@ -77,6 +78,7 @@ struct LayerArgs {
     float *h;        /* [T*K][I] */
     float *y;        /* [T*K][D] */
     unsigned *gbar;  /* [2]: arrival count, generation */
+    uint8_t *xrec;   /* [T][D/256] Q8_K records of the normalised rows (exchange) */
     uint32_t S;      /* stages per warp */
     uint32_t dslots; /* down pairs staged per phase */
 };
@@ -92,32 +94,37 @@ __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-/* Grid barrier, split so a CTA can work between arriving and waiting.
- * Arrive: the CTA's global writes so far are published (bar.sync, then a
- * gpu-scope fence by thread 0 before its arrival); the last CTA to arrive
- * resets the count and bumps the generation. */
-__device__ void grid_arrive(unsigned *gb, LayerShared &sh) {
+__device__ __forceinline__ unsigned atom_add_release_gpu(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+/* Grid barriers of one launch, numbered k = 1..nbar.  gb[0] counts arrivals
+ * (k*G after barrier k; reset to 0 by the last arrival of the last barrier),
+ * gb[1] is a generation word read once at kernel start (sh.gen0): barrier k
+ * is complete when it has advanced by k.  Arrival is one release atomic by
+ * thread 0 after bar.sync, so the CTA's global writes are published; the last
+ * arrival publishes the new generation. */
+__device__ void grid_arrive(unsigned *gb, LayerShared &sh, uint32_t k, uint32_t nbar) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned g0 = ld_acquire_gpu(gb + 1);
-        sh.gen0 = g0;
-        if (atomicAdd(gb, 1u) == gridDim.x - 1) {
-            atomicExch(gb, 0u);
-            __threadfence();
-            st_release_gpu(gb + 1, g0 + 1);
+        const unsigned target = k * gridDim.x;
+        if (atom_add_release_gpu(gb, 1u) == target - 1) {
+            if (k == nbar) gb[0] = 0u; /* nobody reads the count again in this launch */
+            st_release_gpu(gb + 1, sh.gen0 + k);
         }
     }
 }
 
-/* Wait for the generation to move past the one seen at arrival (bounded). */
-__device__ bool grid_wait(unsigned *gb, LayerShared &sh, uint32_t *err) {
+/* Wait until barrier k is complete (bounded). */
+__device__ bool grid_wait(unsigned *gb, LayerShared &sh, uint32_t k, uint32_t *err) {
     if (threadIdx.x == 0) {
         bool ok = true;
         const unsigned g0 = sh.gen0;
-        if (ld_acquire_gpu(gb + 1) == g0) {
+        if ((int)(ld_acquire_gpu(gb + 1) - g0) < (int)k) {
             const uint64_t t0 = lfm_globaltimer();
-            while (ld_acquire_gpu(gb + 1) == g0) {
+            while ((int)(ld_acquire_gpu(gb + 1) - g0) < (int)k) {
                 if (lfm_globaltimer() - t0 > LFM_WAIT_LIMIT_NS) {
                     atomicOr(err, LFM_DEVERR_TIMEOUT);
                     ok = false;
@@ -125,7 +132,6 @@ __device__ bool grid_wait(unsigned *gb, LayerShared &sh, uint32_t *err) {
                 }
             }
         }
-        __threadfence();
         sh.ok = ok ? 1 : 0;
     }
     __syncthreads();
@@ -158,6 +164,7 @@ __device__ __forceinline__ void unit_dispatch(int nt, const uint8_t *wsb, const 
                                               const uint32_t (&toff)[kCh], bool act, uint8_t *st, int g, int h) {
     if (nt <= 1) unit_ints<1>(wsb, rec, toff, act, st, g, h);
     else if (nt <= 2) unit_ints<2>(wsb, rec, toff, act, st, g, h);
+    else if (nt <= 3) unit_ints<3>(wsb, rec, toff, act, st, g, h);
     else if (nt <= 4) unit_ints<4>(wsb, rec, toff, act, st, g, h);
     else unit_ints<8>(wsb, rec, toff, act, st, g, h);
 }
@@ -221,16 +228,15 @@ __device__ void layer_topk(const MoeLayerDev &L, uint32_t t, const float *sg, co
  * whose cost interval starts below target (monotone, so consecutive CTAs'
  * ranges tile the item list). */
 constexpr uint32_t kUnitCost = 3;
-__device__ uint32_t split_count(const LayerShared &sh, uint32_t P, uint32_t gpp, uint64_t target) {
-    uint64_t cum = 0;
-    uint32_t n = 0;
+__device__ uint32_t split_count(const LayerShared &sh, uint32_t P, uint32_t gpp, uint32_t target) {
+    uint32_t cum = 0, n = 0;
     for (uint32_t j = 0; j < P; ++j) {
-        const uint64_t w = kUnitCost + (uint32_t)sh.pnt[j];
-        const uint64_t span = w * gpp;
+        const uint32_t w = kUnitCost + (uint32_t)sh.pnt[j];
+        const uint32_t span = w * gpp;
         if (target >= cum + span) {
             n += gpp;
         } else {
-            if (target > cum) n += (uint32_t)((target - cum + w - 1) / w);
+            if (target > cum) n += (target - cum + w - 1) / w;
             break;
         }
         cum += span;
@@ -286,7 +292,12 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         if (warp == 0) lfm_mbar_init(&sh.bar_in, 1);
         lfm_fence_mbar_init();
     }
-    if (threadIdx.x == 0) sh.abort = 0;
+    if (threadIdx.x == 0) {
+        sh.abort = 0;
+        sh.gen0 = ld_acquire_gpu(gb + 1); /* no barrier of this launch can complete before every CTA has started */
+    }
+    const uint32_t nbar = 3; /* records exchange, after gate|up, after down */
+    uint32_t bar_k = 0;
     __syncthreads();
     if (threadIdx.x == 0) {
         const uint32_t bytes = (T * D + (L.ffn_norm ? D : 0u) + nrows * D) * 4u;
@@ -297,7 +308,8 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
     }
     bool alive = lfm_mbar_wait(&sh.bar_in, 0, err);
 
-    /* ---- 1. RMSNorm, router logits (distributed), Q8_K records of all rows ---- */
+    /* ---- 1. RMSNorm; xb = (x*inv)*w in place; router logits and this CTA's
+     *         share of the Q8_K records, both exchanged through global memory ---- */
     for (uint32_t t0 = 2u * warp; t0 < T; t0 += 2u * W) { /* warp-uniform: half-warp per token */
         const uint32_t t = t0 + (uint32_t)(lane >> 4);
         const bool valid = t < T && alive;
@@ -311,6 +323,12 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         if (l16 == 0 && t < T) sh.inv_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
     }
     __syncthreads();
+    for (uint32_t q = threadIdx.x; q < T * D; q += blockDim.x) {
+        const uint32_t t = q / D, i = q - t * D;
+        const float n = __fmul_rn(xs[q], sh.inv_rms[t]);
+        xs[q] = L.ffn_norm ? __fmul_rn(n, nw[i]) : n;
+    }
+    __syncthreads();
     if (!L.dense) {
         for (uint32_t base = d0 + 2u * warp; base < d1; base += 2u * W) { /* warp-uniform trip count */
             const uint32_t p = base + (uint32_t)(lane >> 4);
@@ -319,35 +337,38 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
             float acc = 0.0f;
             if (valid) {
                 const float *xt = xs + (size_t)t * D, *wr = wsr + (size_t)(e - e_lo) * D;
-                const float inv = sh.inv_rms[t];
 #pragma unroll 16
-                for (uint32_t i = 0; i < D; i += 16) {
-                    const float n = __fmul_rn(xt[i + l16], inv);
-                    const float xb = L.ffn_norm ? __fmul_rn(n, nw[i + l16]) : n;
-                    acc = __fmaf_rn(wr[i + l16], xb, acc);
-                }
+                for (uint32_t i = 0; i < D; i += 16) acc = __fmaf_rn(wr[i + l16], xt[i + l16], acc);
             }
             const float z = lfm_hsum16_ref(acc);
             if (l16 == 0 && valid) A.rt.logits[(size_t)t * E + e] = z;
         }
-        grid_arrive(gb, sh);
     }
-    for (uint32_t q = warp; q < T * nbD; q += W) {
-        const uint32_t t = q / nbD, b = q - t * nbD;
-        const float inv = sh.inv_rms[t];
-        const float *xp = xs + (size_t)t * D + 256 * b + 8 * lane;
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float n = __fmul_rn(xp[i], inv);
-            v[i] = L.ffn_norm ? __fmul_rn(n, nw[256 * b + 8 * lane + i]) : n;
+    {
+        const uint32_t nq = T * nbD;
+        const uint32_t q0 = nq * blockIdx.x / gridDim.x, q1 = nq * (blockIdx.x + 1) / gridDim.x;
+        for (uint32_t q = q0 + warp; q < q1; q += W) {
+            const uint32_t t = q / nbD, b = q - t * nbD;
+            const float *xp = xs + (size_t)t * D + 256 * b + 8 * lane;
+            const float v[8] = {xp[0], xp[1], xp[2], xp[3], xp[4], xp[5], xp[6], xp[7]};
+            lfm_quant_block_rec(v, act + (size_t)q * LFM_ACT_REC); /* build in shared, then publish */
+            __syncwarp();
+            const uint4 *src = reinterpret_cast<const uint4 *>(act + (size_t)q * LFM_ACT_REC);
+            uint4 *dst = reinterpret_cast<uint4 *>(A.xrec + (size_t)q * LFM_ACT_REC);
+            for (uint32_t c = lane; c < LFM_ACT_REC / 16; c += 32) dst[c] = src[c];
         }
-        lfm_quant_block_rec(v, act + ((size_t)t * nbD + b) * LFM_ACT_REC);
+    }
+    grid_arrive(gb, sh, ++bar_k, nbar);
+    alive = grid_wait(gb, sh, bar_k, err) && alive; /* also: every warp is done with xs */
+    if (threadIdx.x == 0 && alive) { /* every row's records, from global into shared */
+        asm volatile("fence.proxy.async.global;" ::: "memory"); /* generic-proxy writes, read by the bulk copy */
+        const uint32_t bytes = T * nbD * LFM_ACT_REC;
+        lfm_mbar_arrive_tx(&sh.bar_in, bytes);
+        lfm_bulk_g2s_plain(act, A.xrec, bytes, &sh.bar_in);
     }
 
     /* ---- 2. routing and dispatch tables (identical in every CTA) ---- */
     if (!L.dense) {
-        alive = grid_wait(gb, sh, err) && alive; /* also: every warp is done with xs */
         float *sg = reinterpret_cast<float *>(dsm), *sl = sg + (size_t)T * E;
         for (uint32_t q = threadIdx.x; q < T * E; q += blockDim.x) {
             const uint32_t e = q % E;
@@ -439,18 +460,20 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
     __syncthreads();
     const uint32_t P = (uint32_t)sh.npairs;
     const uint32_t gpp_gu = I / 2, gpp_dn = D / 4;
-    if (threadIdx.x < 4) { /* this CTA's cost-weighted item ranges */
+    if (threadIdx.x < 4) { /* this CTA's cost-weighted item ranges (totals < 2^32: P*gpp*11) */
         const uint32_t gpp = threadIdx.x < 2 ? gpp_gu : gpp_dn;
-        uint64_t tot = 0;
-        for (uint32_t j = 0; j < P; ++j) tot += (uint64_t)(kUnitCost + (uint32_t)sh.pnt[j]) * gpp;
+        uint32_t tot = 0;
+        for (uint32_t j = 0; j < P; ++j) tot += (kUnitCost + (uint32_t)sh.pnt[j]) * gpp;
         const uint32_t bb = blockIdx.x + (threadIdx.x & 1);
-        const uint32_t n = split_count(sh, P, gpp, tot * bb / gridDim.x);
+        const uint32_t n = split_count(sh, P, gpp, (uint32_t)((uint64_t)tot * bb / gridDim.x));
         if (threadIdx.x == 0) sh.gu_lo = n;
         else if (threadIdx.x == 1) sh.gu_hi = n;
         else if (threadIdx.x == 2) sh.dn_lo = n;
         else sh.dn_hi = n;
     }
     __syncthreads();
+
+    if (alive) alive = lfm_mbar_wait(&sh.bar_in, 1, err); /* the records copied after barrier 1 */
 
     /* ---- 3. per-warp unit streams: gate|up units, then down units ---- */
     const uint32_t np_gu = (nbD + kUnitSb - 1) / kUnitSb, np_dn = (nbI + kUnitSb - 1) / kUnitSb;
@@ -541,8 +564,8 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
             cc.next(W, gpp_gu);
         }
     }
-    grid_arrive(gb, sh);
-    alive = grid_wait(gb, sh, err) && alive;
+    grid_arrive(gb, sh, ++bar_k, nbar);
+    alive = grid_wait(gb, sh, bar_k, err) && alive;
     if (!alive) stop = true;
 
     /* ---- 4. down: h rows of the CTA's pairs as Q8_K records, then the items ---- */
@@ -579,8 +602,8 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
             }
         }
     }
-    grid_arrive(gb, sh);
-    alive = grid_wait(gb, sh, err) && alive;
+    grid_arrive(gb, sh, ++bar_k, nbar);
+    alive = grid_wait(gb, sh, bar_k, err) && alive;
 
     /* ---- 5. combine: this CTA's slice of x ---- */
     if (alive) {
@@ -642,13 +665,13 @@ FusedPlan fused_plan(const MoeLayerDev &L, uint32_t T, uint32_t grid) {
 bool lfm_fused_ok(const MoeLayerDev &L, uint32_t T, int grid) { return fused_plan(L, T, (uint32_t)grid).warps != 0; }
 
 cudaError_t lfm_launch_layer_fused(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, float *h,
-                                   float *y, unsigned *gbar, int grid, cudaStream_t s) {
+                                   float *y, unsigned *gbar, uint8_t *xrec, int grid, cudaStream_t s) {
     const FusedPlan pl = fused_plan(L, T, (uint32_t)grid);
     if (pl.warps == 0) return cudaErrorInvalidValue;
     static size_t cache[16];
     cudaError_t e = lfm_smem_attr((const void *)k_moe_layer, pl.smem, cache);
     if (e != cudaSuccess) return e;
-    LayerArgs a{L, x, T, rt, h, y, gbar, pl.stages, pl.dslots};
+    LayerArgs a{L, x, T, rt, h, y, gbar, xrec, pl.stages, pl.dslots};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(pl.warps * 32);
