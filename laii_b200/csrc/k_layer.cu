@@ -138,6 +138,17 @@ __device__ bool grid_wait(unsigned *gb, LayerShared &sh, uint32_t k, uint32_t *e
     return sh.ok != 0;
 }
 
+/* Operand entry (super-block lane h, token t, row group g) of a unit, written
+ * over the consumed stage: 16 bytes at ((h*8 + (t^h))*4 + g)*16.  The XOR
+ * skew makes both the integer lanes' stores (fixed t) and the chain lanes'
+ * loads (fixed h) touch 8 distinct 16-byte bank groups per 8 lanes. */
+__device__ __forceinline__ uint32_t opnd_off(int h, int t, int g) { return (uint32_t)(((h * 8 + (t ^ h)) * 4 + g) * 16); }
+
+__device__ __forceinline__ void st_opnd(uint8_t *st, int h, int t, int g, const float4 &o) {
+    const uint32_t a = lfm_smem_u32(st + opnd_off(h, t, g));
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(o.x), "f"(o.y), "f"(o.z), "f"(o.w) : "memory");
+}
+
 /* Integer phase of one unit (see k_gemv): operands written over the stage. */
 template <int kNt>
 __device__ __forceinline__ void unit_ints(const uint8_t *wsb, const uint8_t *rec, const uint32_t (&toff8)[kCh],
@@ -150,14 +161,23 @@ __device__ __forceinline__ void unit_ints(const uint8_t *wsb, const uint8_t *rec
     __syncwarp();
     if (act) {
 #pragma unroll
-        for (int t = 0; t < kNt; ++t) {
-            const uint32_t a = lfm_smem_u32(st + (size_t)((h * 8 + t) * 4 + g) * 16);
-            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(o[t].x), "f"(o[t].y), "f"(o[t].z),
-                         "f"(o[t].w)
-                         : "memory");
-        }
+        for (int t = 0; t < kNt; ++t) st_opnd(st, h, t, g, o[t]);
     }
     __syncwarp();
+}
+
+/* fp32 update chain of row group g, token t over the unit's n super-blocks
+ * in order, from the operand entries (see lfm_q4k_chain). */
+__device__ __forceinline__ float chain_swz(float sum, const uint8_t *st, int t, int g, uint32_t n) {
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+        if ((uint32_t)h < n) {
+            const uint4 v = lfm_ld16<true>(st + opnd_off(h, t, g));
+            sum = __fmaf_rn(__uint_as_float(v.x), __uint_as_float(v.y),
+                            __fmaf_rn(-__uint_as_float(v.z), __uint_as_float(v.w), sum));
+        }
+    }
+    return sum;
 }
 
 __device__ __forceinline__ void unit_dispatch(int nt, const uint8_t *wsb, const uint8_t *rec,
@@ -286,7 +306,9 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
     const uint32_t e_lo = d0 < d1 ? d0 / T : 0u, nrows = d0 < d1 ? (d1 - 1) / T - e_lo + 1 : 0u;
     float *xs = reinterpret_cast<float *>(dsm);
     float *nw = xs + (size_t)T * D;
-    float *wsr = nw + D;
+    float *bs = nw + D;                                  /* exp_probs_b, padded to 4 */
+    const uint32_t nbias = L.dense || !L.bias ? 0u : (L.E + 3u) & ~3u;
+    float *wsr = bs + nbias;
     if (lane == 0) {
         for (uint32_t s = 0; s < S; ++s) lfm_mbar_init(&sh.full[warp][s], 1);
         if (warp == 0) lfm_mbar_init(&sh.bar_in, 1);
@@ -300,10 +322,11 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
     uint32_t bar_k = 0;
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t bytes = (T * D + (L.ffn_norm ? D : 0u) + nrows * D) * 4u;
+        const uint32_t bytes = (T * D + (L.ffn_norm ? D : 0u) + nbias + nrows * D) * 4u;
         lfm_mbar_arrive_tx(&sh.bar_in, bytes);
         lfm_bulk_g2s_plain(xs, A.x, T * D * 4u, &sh.bar_in);
         if (L.ffn_norm) lfm_bulk_g2s_plain(nw, L.ffn_norm, D * 4u, &sh.bar_in);
+        if (nbias) lfm_bulk_g2s_plain(bs, L.bias, nbias * 4u, &sh.bar_in);
         if (nrows) lfm_bulk_g2s_plain(wsr, L.router_w + (size_t)e_lo * D, nrows * D * 4u, &sh.bar_in);
     }
     bool alive = lfm_mbar_wait(&sh.bar_in, 0, err);
@@ -323,10 +346,13 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         if (l16 == 0 && t < T) sh.inv_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
     }
     __syncthreads();
-    for (uint32_t q = threadIdx.x; q < T * D; q += blockDim.x) {
-        const uint32_t t = q / D, i = q - t * D;
-        const float n = __fmul_rn(xs[q], sh.inv_rms[t]);
-        xs[q] = L.ffn_norm ? __fmul_rn(n, nw[i]) : n;
+    for (uint32_t t = 0; t < T; ++t) {
+        const float inv = sh.inv_rms[t];
+        float *xt = xs + (size_t)t * D;
+        for (uint32_t i = threadIdx.x; i < D; i += blockDim.x) {
+            const float n = __fmul_rn(xt[i], inv);
+            xt[i] = L.ffn_norm ? __fmul_rn(n, nw[i]) : n;
+        }
     }
     __syncthreads();
     if (!L.dense) {
@@ -369,13 +395,14 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
 
     /* ---- 2. routing and dispatch tables (identical in every CTA) ---- */
     if (!L.dense) {
-        float *sg = reinterpret_cast<float *>(dsm), *sl = sg + (size_t)T * E;
+        /* scores go after the staged x/norm/bias, which are no longer needed but the bias */
+        float *sg = wsr, *sl = sg + (size_t)T * E;
         for (uint32_t q = threadIdx.x; q < T * E; q += blockDim.x) {
-            const uint32_t e = q % E;
+            const uint32_t t = q / E, e = q - t * E;
             const float z = __ldcg(A.rt.logits + q);
             const float sgm = __fdiv_rn(1.0f, __fadd_rn(1.0f, lfm_expf(-z)));
             sg[q] = sgm;
-            sl[q] = L.bias ? __fadd_rn(sgm, L.bias[e]) : sgm;
+            sl[q] = nbias ? __fadd_rn(sgm, bs[e]) : sgm;
         }
         __syncthreads();
         for (uint32_t t = warp; t < T; t += W) layer_topk(L, t, sg + (size_t)t * E, sl + (size_t)t * E, sh);
@@ -532,7 +559,7 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         const uint32_t nsb = min(kUnitSb, nb - kUnitSb * p);
         unit_dispatch(nt, st + (size_t)g * rs + (size_t)h * LFM_Q4K_BYTES,
                       rec_base + (size_t)(kUnitSb * p + h) * LFM_ACT_REC, toff, (uint32_t)h < nsb, st, g, h);
-        if (h < nt) run = lfm_q4k_chain(run, st + (size_t)(h * 4 + g) * 16, 512, nsb);
+        if (h < nt) run = chain_swz(run, st, h, g, nsb);
         __syncwarp(); /* stage free again */
         if (++c_stage == S) { c_stage = 0; c_par ^= 1u; }
         if (lane == 0) {
@@ -649,10 +676,11 @@ FusedPlan fused_plan(const MoeLayerDev &L, uint32_t T, uint32_t grid) {
                 if (s > kMaxS) s = kMaxS;
                 if (s < want) continue;
                 const size_t ring = (size_t)w * s * stage;
-                /* the ring memory first holds x, ffn_norm and the CTA's router rows, then 2*T*E scores */
+                /* the ring memory first holds x, ffn_norm, bias and the CTA's router rows, then the scores */
                 const uint32_t dots = L.dense ? 0u : T * L.E;
                 const uint32_t rows = dots ? (dots + grid - 1) / grid / T + 2 : 0u;
-                if (ring < ((size_t)T * L.D + L.D + (size_t)rows * L.D) * 4 || ring < (size_t)2 * T * L.E * 4) continue;
+                const size_t head = ((size_t)T * L.D + L.D + ((L.E + 3) & ~3u)) * 4; /* x, ffn_norm, bias */
+                if (ring < head + (size_t)rows * L.D * 4 || ring < head + (size_t)2 * T * L.E * 4) continue;
                 return FusedPlan{w, s, dslots, ring + act};
             }
         }
