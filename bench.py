@@ -272,8 +272,11 @@ def run_ours(args, cfg):
     n_launch, tot_ms = prof[dom]
     gu_bytes = 2 * I * (D // 256) * Q4K
     dn_bytes = D * (I // 256) * Q4K
+    # algorithmic bytes per launch: the active experts' Q4_K bytes (each read once) plus, for the
+    # fused layer, the router rows and x in/out; Q8_K activations at 292/256 bytes per value
     per_launch_bytes = {"gateup": ploads * gu_bytes / n_launch + T * D * 1.140625,
-                        "down": ploads * dn_bytes / n_launch + T * K * I * 1.140625 + T * K * D * 4}
+                        "down": ploads * dn_bytes / n_launch + T * K * I * 1.140625 + T * K * D * 4,
+                        "moe_layer": ploads * (gu_bytes + dn_bytes) / n_launch + E * D * 4 + 2 * T * D * 4}
     ach = per_launch_bytes.get(dom, 0.0) / (tot_ms / n_launch / 1e3) / 1e9
     total_prof = sum(v[1] for v in prof.values())
     traffic = None
