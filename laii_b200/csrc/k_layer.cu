@@ -79,6 +79,7 @@ struct LayerArgs {
     float *y;        /* [T*K][D] */
     unsigned *gbar;  /* [2]: arrival count, generation */
     uint8_t *xrec;   /* [T][D/256] Q8_K records of the normalised rows (exchange) */
+    float *scores;   /* [T*E][2]: sigmoid and biased selection score (exchange) */
     uint32_t S;      /* stages per warp */
     uint32_t dslots; /* down pairs staged per phase */
 };
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         sh.abort = 0;
         sh.gen0 = ld_acquire_gpu(gb + 1); /* no barrier of this launch can complete before every CTA has started */
     }
-    const uint32_t nbar = 3; /* records exchange, after gate|up, after down */
+    const uint32_t nbar = 3; /* records/scores exchange; all h written; all y written */
     uint32_t bar_k = 0;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -367,7 +368,12 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
                 for (uint32_t i = 0; i < D; i += 16) acc = __fmaf_rn(wr[i + l16], xt[i + l16], acc);
             }
             const float z = lfm_hsum16_ref(acc);
-            if (l16 == 0 && valid) A.rt.logits[(size_t)t * E + e] = z;
+            if (l16 == 0 && valid) {
+                const float sgm = __fdiv_rn(1.0f, __fadd_rn(1.0f, lfm_expf(-z)));
+                A.rt.logits[(size_t)t * E + e] = z;
+                reinterpret_cast<float2 *>(A.scores)[(size_t)t * E + e] =
+                    make_float2(sgm, nbias ? __fadd_rn(sgm, bs[e]) : sgm);
+            }
         }
     }
     {
@@ -395,31 +401,37 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
 
     /* ---- 2. routing and dispatch tables (identical in every CTA) ---- */
     if (!L.dense) {
-        /* scores go after the staged x/norm/bias, which are no longer needed but the bias */
-        float *sg = wsr, *sl = sg + (size_t)T * E;
+        float *sg = wsr, *sl = sg + (size_t)T * E; /* x / norm / router rows are no longer needed */
         for (uint32_t q = threadIdx.x; q < T * E; q += blockDim.x) {
-            const uint32_t t = q / E, e = q - t * E;
-            const float z = __ldcg(A.rt.logits + q);
-            const float sgm = __fdiv_rn(1.0f, __fadd_rn(1.0f, lfm_expf(-z)));
-            sg[q] = sgm;
-            sl[q] = nbias ? __fadd_rn(sgm, bs[e]) : sgm;
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(A.scores) + q);
+            sg[q] = v.x;
+            sl[q] = v.y;
         }
         __syncthreads();
         for (uint32_t t = warp; t < T; t += W) layer_topk(L, t, sg + (size_t)t * E, sl + (size_t)t * E, sh);
     } else {
         for (uint32_t t = threadIdx.x; t < T; t += blockDim.x) { sh.idx[t] = 0; sh.wk[t] = 1.0f; }
     }
+    __syncthreads();
     const uint32_t n_as = T * K;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) sh.cnt[e] = 0;
-    __syncthreads();
-    for (uint32_t a = threadIdx.x; a < n_as; a += blockDim.x) {
-        const int e = sh.idx[a];
-        if ((unsigned)e < E) atomicAdd(&sh.cnt[e], 1);
-        else atomicOr(err, LFM_DEVERR_EXPERT_ID);
-    }
-    __syncthreads();
+    const uint32_t gpp_gu = I / 2, gpp_dn = D / 4;
     if (warp == 0) {
-        /* lane l owns experts 8l .. 8l+7: counts and pair counts, then warp scans */
+        /* counts and, in assignment order, each assignment's rank within its expert */
+        for (uint32_t e = lane; e < E; e += 32) sh.cnt[e] = 0;
+        __syncwarp();
+        for (uint32_t base = 0; base < n_as; base += 32) {
+            const uint32_t a = base + lane;
+            int e = a < n_as ? sh.idx[a] : -1;
+            if (a < n_as && (unsigned)e >= E) { atomicOr(err, LFM_DEVERR_EXPERT_ID); e = -1; }
+            const int key = e >= 0 ? e : -2 - lane; /* unmatched for invalid slots */
+            const unsigned m = __match_any_sync(LFM_FULL_MASK, key);
+            const int r = __popc(m & ((1u << lane) - 1u));
+            if (e >= 0) sh.inv[a] = sh.cnt[e] + r; /* rank, turned into the slot below */
+            __syncwarp();
+            if (e >= 0 && 31 - __clz(m) == lane) sh.cnt[e] += __popc(m);
+            __syncwarp();
+        }
+        /* lane l owns experts 8l .. 8l+7: offsets and pair list by warp scans */
         int c[8], csum = 0, psum = 0, mx = 0, uq = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -433,8 +445,8 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         int cex = csum, pex = psum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int a = __shfl_up_sync(LFM_FULL_MASK, cex, o), b = __shfl_up_sync(LFM_FULL_MASK, pex, o);
-            if (lane >= o) { cex += a; pex += b; }
+            const int x1 = __shfl_up_sync(LFM_FULL_MASK, cex, o), x2 = __shfl_up_sync(LFM_FULL_MASK, pex, o);
+            if (lane >= o) { cex += x1; pex += x2; }
         }
         cex -= csum; /* exclusive */
         pex -= psum;
@@ -455,6 +467,7 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
             mx = max(mx, __shfl_xor_sync(LFM_FULL_MASK, mx, o));
             uq += __shfl_xor_sync(LFM_FULL_MASK, uq, o);
         }
+        const int np_all = __shfl_sync(LFM_FULL_MASK, pex, 31), total = __shfl_sync(LFM_FULL_MASK, cex, 31);
         if (lane == 31) {
             sh.off[E] = cex;
             sh.npairs = pex;
@@ -466,39 +479,37 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
                 if (A.rt.loads && !L.dense) { A.rt.loads[0] += (unsigned long long)uq; A.rt.loads[1] += 1ull; }
             }
         }
-    }
-    __syncthreads();
-    for (uint32_t a = threadIdx.x; a < n_as; a += blockDim.x) {
-        const int e = sh.idx[a];
-        int pos = -1;
-        if ((unsigned)e < E) {
-            int r = 0;
-            for (uint32_t b = 0; b < a; ++b) r += sh.idx[b] == e;
-            pos = sh.off[e] + r;
-            sh.perm[pos] = (int)a;
-            sh.tok[pos] = (int)(a / K);
+        __syncwarp();
+        for (uint32_t a = lane; a < n_as; a += 32) {
+            const int e = sh.idx[a];
+            int pos = -1;
+            if ((unsigned)e < E) {
+                pos = sh.off[e] + sh.inv[a];
+                sh.perm[pos] = (int)a;
+                sh.tok[pos] = (int)(a / K);
+            }
+            sh.inv[a] = pos;
+            if (blockIdx.x == 0) {
+                A.rt.idx[a] = e;
+                A.rt.w[a] = sh.wk[a];
+            }
         }
-        sh.inv[a] = pos;
-        if (blockIdx.x == 0) {
-            A.rt.idx[a] = e;
-            A.rt.w[a] = sh.wk[a];
+        (void)total;
+        if (lane < 4) { /* this CTA's cost-weighted item ranges (totals < 2^32: P*gpp*11) */
+            const uint32_t P = (uint32_t)np_all;
+            const uint32_t gpp = lane < 2 ? gpp_gu : gpp_dn;
+            uint32_t tot = 0;
+            for (uint32_t j = 0; j < P; ++j) tot += (kUnitCost + (uint32_t)sh.pnt[j]) * gpp;
+            const uint32_t bb = blockIdx.x + (lane & 1);
+            const uint32_t n = split_count(sh, P, gpp, (uint32_t)((uint64_t)tot * bb / gridDim.x));
+            if (lane == 0) sh.gu_lo = n;
+            else if (lane == 1) sh.gu_hi = n;
+            else if (lane == 2) sh.dn_lo = n;
+            else sh.dn_hi = n;
         }
     }
     __syncthreads();
     const uint32_t P = (uint32_t)sh.npairs;
-    const uint32_t gpp_gu = I / 2, gpp_dn = D / 4;
-    if (threadIdx.x < 4) { /* this CTA's cost-weighted item ranges (totals < 2^32: P*gpp*11) */
-        const uint32_t gpp = threadIdx.x < 2 ? gpp_gu : gpp_dn;
-        uint32_t tot = 0;
-        for (uint32_t j = 0; j < P; ++j) tot += (kUnitCost + (uint32_t)sh.pnt[j]) * gpp;
-        const uint32_t bb = blockIdx.x + (threadIdx.x & 1);
-        const uint32_t n = split_count(sh, P, gpp, (uint32_t)((uint64_t)tot * bb / gridDim.x));
-        if (threadIdx.x == 0) sh.gu_lo = n;
-        else if (threadIdx.x == 1) sh.gu_hi = n;
-        else if (threadIdx.x == 2) sh.dn_lo = n;
-        else sh.dn_hi = n;
-    }
-    __syncthreads();
 
     if (alive) alive = lfm_mbar_wait(&sh.bar_in, 1, err); /* the records copied after barrier 1 */
 
@@ -693,13 +704,13 @@ FusedPlan fused_plan(const MoeLayerDev &L, uint32_t T, uint32_t grid) {
 bool lfm_fused_ok(const MoeLayerDev &L, uint32_t T, int grid) { return fused_plan(L, T, (uint32_t)grid).warps != 0; }
 
 cudaError_t lfm_launch_layer_fused(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, float *h,
-                                   float *y, unsigned *gbar, uint8_t *xrec, int grid, cudaStream_t s) {
+                                   float *y, unsigned *gbar, uint8_t *xrec, float *scores, int grid, cudaStream_t s) {
     const FusedPlan pl = fused_plan(L, T, (uint32_t)grid);
     if (pl.warps == 0) return cudaErrorInvalidValue;
     static size_t cache[16];
     cudaError_t e = lfm_smem_attr((const void *)k_moe_layer, pl.smem, cache);
     if (e != cudaSuccess) return e;
-    LayerArgs a{L, x, T, rt, h, y, gbar, xrec, pl.stages, pl.dslots};
+    LayerArgs a{L, x, T, rt, h, y, gbar, xrec, scores, pl.stages, pl.dslots};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(pl.warps * 32);

@@ -43,6 +43,7 @@ struct Workspace {
     float *y = nullptr;       /* [T*K][D]                              */
     unsigned *gbar = nullptr; /* [2] grid barrier of the fused layer (counter region) */
     uint8_t *xrec = nullptr;  /* [T][D/256] Q8_K records exchanged by the fused layer */
+    float *scores = nullptr;  /* [T*E][2] router scores exchanged by the fused layer */
 };
 
 }  // namespace
@@ -174,6 +175,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_hb = take(sizeof(int16_t) * TK * (I / 256) * 16);
     const size_t o_y = take(sizeof(float) * TK * D);
     const size_t o_xrec = take((size_t)T * (D / 256) * 304);
+    const size_t o_scores = take(sizeof(float) * 2 * T * E);
     void *base = nullptr;
     /* the old workspace may still be read by queued work on any stream */
     cudaError_t e = cudaDeviceSynchronize();
@@ -210,6 +212,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.y = reinterpret_cast<float *>(b + o_y);
     w.gbar = reinterpret_cast<unsigned *>(b + o_gbar);
     w.xrec = b + o_xrec;
+    w.scores = reinterpret_cast<float *>(b + o_scores);
     return LFM_GPU_OK;
 }
 
@@ -264,7 +267,7 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
     if (h->use_fused && lfm_fused_ok(L, T, grid)) {
-        LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, grid, s); }));
+        LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
         return LFM_GPU_OK;
     }
     LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));

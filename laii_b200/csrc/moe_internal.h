@@ -86,7 +86,7 @@ size_t lfm_gemv_smem(uint32_t cols, uint32_t mats);
  * cooperative launch on `grid` CTAs (one per SM). gbar: 2 zeroed words. */
 bool lfm_fused_ok(const MoeLayerDev &L, uint32_t T, int grid);
 cudaError_t lfm_launch_layer_fused(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, float *h,
-                                   float *y, unsigned *gbar, uint8_t *xrec, int grid, cudaStream_t s);
+                                   float *y, unsigned *gbar, uint8_t *xrec, float *scores, int grid, cudaStream_t s);
 cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables &rt, float *h, int grid,
                               cudaStream_t s, bool pdl);
 cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s, bool pdl);
