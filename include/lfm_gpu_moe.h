@@ -105,6 +105,51 @@ lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t layer, uint3
                                          float w_std, float router_std, float bias_std,
                                          const float *exp_probs_b);
 
+/* Expert parallelism (one process per GPU, experts sharded across ranks): a
+ * layer holding the full router (exp_probs_b, ffn_norm) but only experts
+ * [expert_first, expert_first + n_local) of E.  gate/up/down_local are those
+ * experts' slices of the GGUF tensors ([n_local][rows][cols/256] Q4_K), i.e.
+ * lfm2_slice_expert_tensor_2d of each (tools/lfm2_moe_checkpoint.c:110-127).
+ * A shard layer runs only through the lfm_gpu_moe_ep_* calls below. */
+lfm_gpu_status_t lfm_gpu_moe_upload_layer_shard(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                const float *router_w, const float *exp_probs_b,
+                                                const void *gate_local, const void *up_local,
+                                                const void *down_local, uint32_t w_type, int norm_topk_prob,
+                                                float routed_scale, uint32_t expert_first, uint32_t n_local);
+
+/* The seeded synthetic layer restricted to an expert shard: byte-identical to
+ * the same experts of lfm_gpu_moe_synth_layer.  No counterpart in the reference. */
+lfm_gpu_status_t lfm_gpu_moe_synth_layer_shard(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                               uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
+                                               float w_std, float router_std, float bias_std,
+                                               const float *exp_probs_b, uint32_t expert_first,
+                                               uint32_t n_local);
+
+/* EP step 1 (home rank): RMSNorm + Q8_K + router + top-K of device x[T][D]
+ * (lfm2_rmsnorm_quantize_q8_K_simd + lfm2_moe_route_sigmoid_topk,
+ * tools/lfm2_moe_checkpoint.c:328-333).  Device outputs: idx[T][K] global
+ * expert ids, w[T][K] combine weights, q8[T][D/256] 292-byte block_q8_K.
+ * Asynchronous on `stream`. */
+lfm_gpu_status_t lfm_gpu_moe_ep_route(lfm_gpu_moe_t *h, uint32_t layer, const float *x, uint32_t T,
+                                      int32_t *idx_out, float *w_out, void *q8_out, void *stream);
+
+/* EP step 2 (expert rank): rows received from any rank -- row a is one
+ * (token, k) assignment as q8_in[a][D/256] block_q8_K routed to global expert
+ * expert_ids[a], which must lie in this rank's shard -- through gate/up,
+ * SwiGLU, Q8_K(h) and down (tools/lfm2_moe_checkpoint.c:338-363 without the
+ * weighting): y_out[a][D] fp32, unweighted.  n_rows <= 65535 per call.
+ * Asynchronous on `stream`; a foreign expert id sets LFM_GPU_ERR_DEVICE_CHECK
+ * at the next lfm_gpu_moe_sync. */
+lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer, const void *q8_in, uint32_t n_rows,
+                                        const int32_t *expert_ids, float *y_out, void *stream);
+
+/* EP step 3 (home rank): x[t] = fma(w[t][k], y[t*K + k], x[t]) for k = 0..K-1
+ * in order (tools/lfm2_moe_checkpoint.c:266-269), y[T*K][D] in (t, k) order.
+ * Asynchronous on `stream`. */
+lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T, const float *w,
+                                        const float *y, void *stream);
+
 /* Reserve scratch for up to max_tokens tokens per forward (forward grows it on
  * demand; reserve first when the forward is to be captured in a CUDA graph). */
 lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens);

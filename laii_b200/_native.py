@@ -39,6 +39,13 @@ GPU_API = [
     ("lfm_gpu_moe_upload_dense", c_int, [c_vp, c_u32, c_u32, c_u32, c_f32, c_vp, c_vp, c_vp, c_vp, c_u32]),
     ("lfm_gpu_moe_synth_layer", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32, ctypes.POINTER(c_u64),
                                         c_f32, c_f32, c_f32, c_vp]),
+    ("lfm_gpu_moe_upload_layer_shard", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32, c_vp, c_vp, c_vp,
+                                               c_vp, c_vp, c_vp, c_u32, c_int, c_f32, c_u32, c_u32]),
+    ("lfm_gpu_moe_synth_layer_shard", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32,
+                                              ctypes.POINTER(c_u64), c_f32, c_f32, c_f32, c_vp, c_u32, c_u32]),
+    ("lfm_gpu_moe_ep_route", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp, c_vp]),
+    ("lfm_gpu_moe_ep_experts", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
+    ("lfm_gpu_moe_ep_combine", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_reserve", c_int, [c_vp, c_u32]),
     ("lfm_gpu_moe_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_int, c_vp]),
     ("lfm_gpu_moe_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_int, c_vp]),

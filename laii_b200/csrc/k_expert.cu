@@ -62,6 +62,32 @@ __global__ void __launch_bounds__(128) k_combine(float *__restrict__ x, uint32_t
     *reinterpret_cast<float4 *>(x + (size_t)t * D + r) = v;
 }
 
+/* Expert parallelism, received rows: row a goes to local expert
+ * expert_ids[a] - first with weight 1 (out-of-shard ids are flagged and dropped). */
+__global__ void k_ep_prepare(const int32_t *__restrict__ ids, uint32_t n, uint32_t first, uint32_t count,
+                             RouteTables rt) {
+    for (uint32_t a = blockIdx.x * blockDim.x + threadIdx.x; a < n; a += gridDim.x * blockDim.x) {
+        const int32_t e = ids[a] - (int32_t)first;
+        const bool ok = e >= 0 && (uint32_t)e < count;
+        if (!ok) atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
+        rt.idx[a] = ok ? e : -1;
+        rt.w[a] = 1.0f;
+    }
+}
+
+/* x[t][r] = fma(w[t][k], y[t*K+k][r], x[t][r]) for k = 0..K-1 in order
+ * (tools/lfm2_moe_checkpoint.c:266-269), y already in (t, k) order. */
+__global__ void __launch_bounds__(256) k_ep_combine(float *__restrict__ x, uint32_t T, uint32_t D, uint32_t K,
+                                                    const float *__restrict__ w, const float *__restrict__ y) {
+    const uint64_t n = (uint64_t)T * D;
+    for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n; q += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t t = q / D, r = q - t * D;
+        float acc = x[q];
+        for (uint32_t k = 0; k < K; ++k) acc = __fmaf_rn(w[t * K + k], y[(t * K + k) * D + r], acc);
+        x[q] = acc;
+    }
+}
+
 /* Internal Q8 rows <-> 292-byte GGUF block_q8_K. */
 __global__ void k_q8_to_gguf(Q8Rows q, uint32_t rows, uint8_t *out) {
     const uint32_t nb = q.cols / 256;
@@ -154,5 +180,21 @@ cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cu
     const uint32_t n = rows * (q.cols / 256);
     if (n == 0) return cudaSuccess;
     k_gguf_to_q8<<<n, 128, 0, s>>>(in, rows, q);
+    return cudaGetLastError();
+}
+
+cudaError_t lfm_launch_ep_prepare(const int32_t *expert_ids, uint32_t n, uint32_t first, uint32_t count,
+                                  const RouteTables &rt, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    k_ep_prepare<<<min(1184u, (n + 255) / 256), 256, 0, s>>>(expert_ids, n, first, count, rt);
+    return cudaGetLastError();
+}
+
+cudaError_t lfm_launch_ep_combine(float *x, uint32_t T, uint32_t D, uint32_t K, const float *w, const float *y,
+                                  cudaStream_t s) {
+    const uint64_t n = (uint64_t)T * D;
+    if (n == 0) return cudaSuccess;
+    const uint64_t blocks = (n + 255) / 256;
+    k_ep_combine<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(x, T, D, K, w, y);
     return cudaGetLastError();
 }

@@ -367,7 +367,19 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
     route_dispatch(L, T, rt, s);
 }
 
+/* Dispatch tables alone, for rows whose experts are given (expert parallelism). */
+__global__ void __launch_bounds__(256) k_dispatch_only(MoeLayerDev L, uint32_t T, RouteTables rt) {
+    __shared__ RouteSmem s;
+    route_dispatch(L, T, rt, s);
+}
+
 }  // namespace
+
+cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    k_dispatch_only<<<1, 256, 0, s>>>(L, T, rt);
+    return cudaGetLastError();
+}
 
 size_t lfm_route_smem(uint32_t D) { return sizeof(float) * D * (2 + kExpertsPerBlock); }
 

@@ -26,6 +26,7 @@ namespace {
 struct LayerSlot {
     bool present = false;
     MoeLayerDev dev{};
+    uint32_t ep_first = 0, ep_count = 0; /* expert shard [first, first+count); count 0 = all experts */
     void *bufs[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     size_t sizes[7] = {0, 0, 0, 0, 0, 0, 0};
 };
@@ -124,6 +125,7 @@ void free_layer(LayerSlot &L) {
     }
     for (size_t &z : L.sizes) z = 0;
     L.present = false;
+    L.ep_first = L.ep_count = 0;
     L.dev = MoeLayerDev{};
 }
 
@@ -335,15 +337,17 @@ LFM_API void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h) {
 
 LFM_API const char *lfm_gpu_moe_last_error(const lfm_gpu_moe_t *h) { return h ? h->err : "null handle"; }
 
-LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
-                                                  uint32_t K, uint32_t I, float eps, const float *ffn_norm,
-                                                  const float *router_w, const float *exp_probs_b,
-                                                  const void *gate_exps, const void *up_exps,
-                                                  const void *down_exps, uint32_t w_type, int norm_topk_prob,
-                                                  float routed_scale) {
+/* Upload of a layer with experts [first, first + n) of E (all of them when n == E). */
+static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E, uint32_t K,
+                                          uint32_t I, float eps, const float *ffn_norm, const float *router_w,
+                                          const float *exp_probs_b, const void *gate_exps, const void *up_exps,
+                                          const void *down_exps, uint32_t w_type, int norm_topk_prob,
+                                          float routed_scale, uint32_t first, uint32_t n) {
     if (!h) return LFM_GPU_ERR_INVALID_ARG;
     lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
     if (st != LFM_GPU_OK) return st;
+    if (n == 0 || first >= E || n > E - first)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "expert shard [%u, %u+%u) not inside 0..%u", first, first, n, E);
     if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "expert weight type %u (only Q4_K=12)", w_type);
     if (!router_w || !gate_exps || !up_exps || !down_exps) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
     DeviceGuard g(h->device);
@@ -352,8 +356,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
     const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * ((E + 3) / 4 * 4),
-                          (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
-                          (size_t)E * D * nbi * LFM_Q4K_BYTES};
+                          (size_t)n * I * nbd * LFM_Q4K_BYTES, (size_t)n * I * nbd * LFM_Q4K_BYTES,
+                          (size_t)n * D * nbi * LFM_Q4K_BYTES};
     const void *src[6] = {ffn_norm, router_w, exp_probs_b, gate_exps, up_exps, down_exps};
     for (int i = 0; i < 6; ++i) {
         if (i == 0 && !ffn_norm) continue;
@@ -369,8 +373,31 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
                         static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
                         static_cast<float *>(S.bufs[2]), static_cast<const uint8_t *>(S.bufs[3]),
                         static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5])};
+    S.ep_first = first;
+    S.ep_count = n;
     S.present = true;
     return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                  uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                  const float *router_w, const float *exp_probs_b,
+                                                  const void *gate_exps, const void *up_exps,
+                                                  const void *down_exps, uint32_t w_type, int norm_topk_prob,
+                                                  float routed_scale) {
+    return upload_layer_impl(h, layer, D, E, K, I, eps, ffn_norm, router_w, exp_probs_b, gate_exps, up_exps,
+                             down_exps, w_type, norm_topk_prob, routed_scale, 0, E);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer_shard(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                        uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                        const float *router_w, const float *exp_probs_b,
+                                                        const void *gate_local, const void *up_local,
+                                                        const void *down_local, uint32_t w_type,
+                                                        int norm_topk_prob, float routed_scale,
+                                                        uint32_t expert_first, uint32_t n_local) {
+    return upload_layer_impl(h, layer, D, E, K, I, eps, ffn_norm, router_w, exp_probs_b, gate_local, up_local,
+                             down_local, w_type, norm_topk_prob, routed_scale, expert_first, n_local);
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t I,
@@ -404,21 +431,23 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t lay
     return LFM_GPU_OK;
 }
 
-LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
-                                                 uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
-                                                 float w_std, float router_std, float bias_std,
-                                                 const float *exp_probs_b) {
+static lfm_gpu_status_t synth_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E, uint32_t K,
+                                         uint32_t I, float eps, const uint64_t seeds[5], float w_std,
+                                         float router_std, float bias_std, const float *exp_probs_b,
+                                         uint32_t first, uint32_t n) {
     if (!h || !seeds) return LFM_GPU_ERR_INVALID_ARG;
     lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
     if (st != LFM_GPU_OK) return st;
+    if (n == 0 || first >= E || n > E - first)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "expert shard [%u, %u+%u) not inside 0..%u", first, first, n, E);
     DeviceGuard g(h->device);
     drop_graphs(h);
     LayerSlot &S = h->layers[layer];
     free_layer(S);
     const size_t nbd = D / 256, nbi = I / 256;
     const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * ((E + 3) / 4 * 4),
-                          (size_t)E * I * nbd * LFM_Q4K_BYTES, (size_t)E * I * nbd * LFM_Q4K_BYTES,
-                          (size_t)E * D * nbi * LFM_Q4K_BYTES};
+                          (size_t)n * I * nbd * LFM_Q4K_BYTES, (size_t)n * I * nbd * LFM_Q4K_BYTES,
+                          (size_t)n * D * nbi * LFM_Q4K_BYTES};
     for (int i = 0; i < 6; ++i) {
         cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
         if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "synth layer cudaMalloc"); }
@@ -434,16 +463,41 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t laye
         else if (e == cudaSuccess)
             e = lfm_launch_synth_f32(static_cast<float *>(S.bufs[2]), E, seeds[4], 0.0f, bias_std, s);
     }
-    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[3]), (uint64_t)E * I * nbd, seeds[0], w_std, s);
-    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[4]), (uint64_t)E * I * nbd, seeds[1], w_std, s);
-    if (e == cudaSuccess) e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[5]), (uint64_t)E * D * nbi, seeds[2], w_std, s);
+    /* the shard's blocks are blocks [first*rows*nb, ...) of the full tensors */
+    if (e == cudaSuccess)
+        e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[3]), (uint64_t)n * I * nbd, seeds[0], w_std, s,
+                                 (uint64_t)first * I * nbd);
+    if (e == cudaSuccess)
+        e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[4]), (uint64_t)n * I * nbd, seeds[1], w_std, s,
+                                 (uint64_t)first * I * nbd);
+    if (e == cudaSuccess)
+        e = lfm_launch_synth_q4k(static_cast<uint8_t *>(S.bufs[5]), (uint64_t)n * D * nbi, seeds[2], w_std, s,
+                                 (uint64_t)first * D * nbi);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) { free_layer(S); return cuda_fail(h, e, "synth layer"); }
     S.dev = MoeLayerDev{D, E, K, I, 0, eps, 1.0f, 1, static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
                         static_cast<float *>(S.bufs[2]), static_cast<const uint8_t *>(S.bufs[3]),
                         static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5])};
+    S.ep_first = first;
+    S.ep_count = n;
     S.present = true;
     return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                 uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
+                                                 float w_std, float router_std, float bias_std,
+                                                 const float *exp_probs_b) {
+    return synth_layer_impl(h, layer, D, E, K, I, eps, seeds, w_std, router_std, bias_std, exp_probs_b, 0, E);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_synth_layer_shard(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                       uint32_t K, uint32_t I, float eps, const uint64_t seeds[5],
+                                                       float w_std, float router_std, float bias_std,
+                                                       const float *exp_probs_b, uint32_t expert_first,
+                                                       uint32_t n_local) {
+    return synth_layer_impl(h, layer, D, E, K, I, eps, seeds, w_std, router_std, bias_std, exp_probs_b,
+                            expert_first, n_local);
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens) {
@@ -516,6 +570,8 @@ static lfm_gpu_status_t forward_common(lfm_gpu_moe_t *h, uint32_t first, uint32_
     for (uint32_t l = first; l < first + n; ++l) {
         const LayerSlot &S = h->layers[l];
         if (!S.present) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", l);
+        if (S.ep_count && S.ep_count != S.dev.E)
+            return fail(h, LFM_GPU_ERR_UNSUPPORTED, "layer %u holds an expert shard: use the lfm_gpu_moe_ep_* calls", l);
         if (D && S.dev.D != D) return fail(h, LFM_GPU_ERR_INVALID_ARG, "layers disagree on D");
         D = S.dev.D;
         E = S.dev.E > E ? S.dev.E : E;
@@ -812,5 +868,90 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t 
     if (e == cudaSuccess) e = lfm_launch_down(L, w.hq, w.rt, w.y, grid, s, true);
     if (e == cudaSuccess) e = lfm_launch_combine(L, x, T, w.rt, w.y, s, true);
     if (e != cudaSuccess) return cuda_fail(h, e, "forward_noalloc launch");
+    return LFM_GPU_OK;
+}
+
+/* ---- expert parallelism ---------------------------------------------------
+ * One process per GPU; each holds the full router and an expert shard.  The
+ * caller exchanges rows between ranks (e.g. NCCL all-to-all): route locally,
+ * send each (token, k) row to the rank owning its expert, run the local
+ * experts on the rows received, send the outputs back, combine at home. */
+
+static lfm_gpu_status_t ep_layer(lfm_gpu_moe_t *h, uint32_t layer, const LayerSlot **out) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present || h->layers[layer].dev.dense)
+        return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u is not an uploaded MoE layer", layer);
+    *out = &h->layers[layer];
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_route(lfm_gpu_moe_t *h, uint32_t layer, const float *x, uint32_t T,
+                                              int32_t *idx_out, float *w_out, void *q8_out, void *stream) {
+    const LayerSlot *S = nullptr;
+    lfm_gpu_status_t st = ep_layer(h, layer, &S);
+    if (st != LFM_GPU_OK) return st;
+    if (!x || !idx_out || !w_out || !q8_out) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null buffer");
+    if (T == 0) return LFM_GPU_OK;
+    if (T > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "T=%u above 65535", T);
+    if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(h, LFM_GPU_ERR_INVALID_ARG, "device x must be 16-byte aligned");
+    const MoeLayerDev &L = S->dev;
+    DeviceGuard g(h->device);
+    st = ensure_workspace(h, T, L.D, L.E, L.K, L.I);
+    if (st != LFM_GPU_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace &w = h->ws;
+    Q8Rows xq = w.xq; xq.cols = L.D;
+    LFM_CUDA(h, lfm_launch_route(L, x, T, xq, w.rt, s, false));
+    LFM_CUDA(h, cudaMemcpyAsync(idx_out, w.rt.idx, sizeof(int32_t) * T * L.K, cudaMemcpyDeviceToDevice, s));
+    LFM_CUDA(h, cudaMemcpyAsync(w_out, w.rt.w, sizeof(float) * T * L.K, cudaMemcpyDeviceToDevice, s));
+    LFM_CUDA(h, lfm_launch_q8_to_gguf(xq, T, static_cast<uint8_t *>(q8_out), s));
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer, const void *q8_in, uint32_t n_rows,
+                                                const int32_t *expert_ids, float *y_out, void *stream) {
+    const LayerSlot *S = nullptr;
+    lfm_gpu_status_t st = ep_layer(h, layer, &S);
+    if (st != LFM_GPU_OK) return st;
+    if (n_rows == 0) return LFM_GPU_OK;
+    if (!q8_in || !expert_ids || !y_out) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null buffer");
+    if (n_rows > 65535) return fail(h, LFM_GPU_ERR_INVALID_ARG, "n_rows=%u above 65535 per call", n_rows);
+    const uint32_t first = S->ep_first, count = S->ep_count ? S->ep_count : S->dev.E;
+    /* the shard as a layer of its own: local experts 0..count-1, top-1, weight 1 */
+    MoeLayerDev Lx = S->dev;
+    Lx.E = count;
+    Lx.K = 1;
+    Lx.router_w = nullptr;
+    Lx.bias = nullptr;
+    Lx.norm_topk = 0;
+    Lx.routed_scale = 1.0f;
+    DeviceGuard g(h->device);
+    st = ensure_workspace(h, n_rows, Lx.D, count, 1, Lx.I);
+    if (st != LFM_GPU_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace &w = h->ws;
+    Q8Rows xq = w.xq; xq.cols = Lx.D;
+    Q8Rows hq = w.hq; hq.cols = Lx.I;
+    const int grid = h->sm_count;
+    LFM_CUDA(h, lfm_launch_gguf_to_q8(static_cast<const uint8_t *>(q8_in), n_rows, xq, s));
+    LFM_CUDA(h, lfm_launch_ep_prepare(expert_ids, n_rows, first, count, w.rt, s));
+    LFM_CUDA(h, lfm_launch_dispatch(Lx, n_rows, w.rt, s));
+    LFM_CUDA(h, cudaMemsetAsync(y_out, 0, sizeof(float) * n_rows * Lx.D, s));
+    LFM_CUDA(h, lfm_launch_gateup(Lx, xq, w.rt, w.h, grid, s, false));
+    LFM_CUDA(h, lfm_launch_quant_rows(w.h, n_rows, Lx.I, hq, s, false));
+    LFM_CUDA(h, lfm_launch_down(Lx, hq, w.rt, w.y, grid, s, false));
+    LFM_CUDA(h, lfm_launch_combine(Lx, y_out, n_rows, w.rt, w.y, s, false)); /* y_out = fma(1, y, 0) = y */
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                                const float *w, const float *y, void *stream) {
+    const LayerSlot *S = nullptr;
+    lfm_gpu_status_t st = ep_layer(h, layer, &S);
+    if (st != LFM_GPU_OK) return st;
+    if (T == 0) return LFM_GPU_OK;
+    if (!x || !w || !y) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null buffer");
+    DeviceGuard g(h->device);
+    LFM_CUDA(h, lfm_launch_ep_combine(x, T, S->dev.D, S->dev.K, w, y, static_cast<cudaStream_t>(stream)));
     return LFM_GPU_OK;
 }

@@ -76,6 +76,8 @@ cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16);
 
 /* k_route.cu */
 size_t lfm_route_smem(uint32_t D);
+/* dispatch tables only, from rt.idx already filled (one block) */
+cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
                              cudaStream_t s, bool pdl);
 
@@ -98,10 +100,17 @@ cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_
                                       uint32_t n_vec, int32_t *sub_dots, int32_t *acc, int32_t *mins,
                                       float *rows_out, cudaStream_t s);
 cudaError_t lfm_launch_q8_to_gguf(Q8Rows q, uint32_t rows, uint8_t *out, cudaStream_t s);
+/* expert parallelism: given routing of received rows, and the (t, k)-ordered combine */
+cudaError_t lfm_launch_ep_prepare(const int32_t *expert_ids, uint32_t n, uint32_t first, uint32_t count,
+                                  const RouteTables &rt, cudaStream_t s);
+cudaError_t lfm_launch_ep_combine(float *x, uint32_t T, uint32_t D, uint32_t K, const float *w, const float *y,
+                                  cudaStream_t s);
 cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cudaStream_t s);
 
 /* k_synth.cu */
-cudaError_t lfm_launch_synth_q4k(uint8_t *out, uint64_t n_blocks, uint64_t seed, float stddev, cudaStream_t s);
+/* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
+cudaError_t lfm_launch_synth_q4k(uint8_t *out, uint64_t n_blocks, uint64_t seed, float stddev, cudaStream_t s,
+                                 uint64_t first = 0);
 cudaError_t lfm_launch_synth_f32(float *out, uint64_t n, uint64_t seed, float mean, float stddev,
                                  cudaStream_t s);
 

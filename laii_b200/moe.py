@@ -91,6 +91,44 @@ class GpuMoE:
                                                       bias_std, _ptr(b)))
         self.layers[layer] = ("moe", D, E, K, I)
 
+    # -- expert parallelism (laii_b200.ep) --------------------------------
+    def upload_layer_shard(self, layer: int, L: MoELayer, first: int, count: int):
+        """Full router; only experts [first, first+count) of L's expert tensors."""
+        per_gu = L.I * (L.D // 256) * 144
+        per_dn = L.D * (L.I // 256) * 144
+        g = np.ascontiguousarray(L.gate.reshape(-1)[first * per_gu:(first + count) * per_gu])
+        u = np.ascontiguousarray(L.up.reshape(-1)[first * per_gu:(first + count) * per_gu])
+        d = np.ascontiguousarray(L.down.reshape(-1)[first * per_dn:(first + count) * per_dn])
+        keep = [np.ascontiguousarray(a) for a in (L.ffn_norm, L.router_w)]
+        bias = None if L.bias is None else np.ascontiguousarray(L.bias, dtype=np.float32)
+        self._check(self._lib.lfm_gpu_moe_upload_layer_shard(
+            self._h, layer, L.D, L.E, L.K, L.I, L.eps, _ptr(keep[0]), _ptr(keep[1]), _ptr(bias), _ptr(g), _ptr(u),
+            _ptr(d), GGML_TYPE_Q4_K, int(L.norm_topk_prob), L.routed_scale, first, count))
+        self.layers[layer] = ("moe-shard", L.D, L.E, L.K, L.I)
+
+    def synth_layer_shard(self, layer: int, D: int, E: int, K: int, I: int, seeds, first: int, count: int,
+                          w_std=0.02, router_std=0.02, bias_std=0.1, bias: Optional[np.ndarray] = None,
+                          eps: float = 1e-5):
+        arr = (ctypes.c_uint64 * 5)(*[int(s) & 0xFFFFFFFFFFFFFFFF for s in seeds])
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._check(self._lib.lfm_gpu_moe_synth_layer_shard(self._h, layer, D, E, K, I, eps, arr, w_std, router_std,
+                                                            bias_std, _ptr(b), first, count))
+        self.layers[layer] = ("moe-shard", D, E, K, I)
+
+    def ep_route(self, layer: int, x_ptr: int, T: int, idx_ptr: int, w_ptr: int, q8_ptr: int, stream: int = 0):
+        self._check(self._lib.lfm_gpu_moe_ep_route(self._h, layer, ctypes.c_void_p(x_ptr), T, ctypes.c_void_p(idx_ptr),
+                                                   ctypes.c_void_p(w_ptr), ctypes.c_void_p(q8_ptr),
+                                                   ctypes.c_void_p(stream or None)))
+
+    def ep_experts(self, layer: int, q8_ptr: int, n: int, ids_ptr: int, y_ptr: int, stream: int = 0):
+        self._check(self._lib.lfm_gpu_moe_ep_experts(self._h, layer, ctypes.c_void_p(q8_ptr), n,
+                                                     ctypes.c_void_p(ids_ptr), ctypes.c_void_p(y_ptr),
+                                                     ctypes.c_void_p(stream or None)))
+
+    def ep_combine(self, layer: int, x_ptr: int, T: int, w_ptr: int, y_ptr: int, stream: int = 0):
+        self._check(self._lib.lfm_gpu_moe_ep_combine(self._h, layer, ctypes.c_void_p(x_ptr), T, ctypes.c_void_p(w_ptr),
+                                                     ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or None)))
+
     def reserve(self, max_tokens: int):
         self._check(self._lib.lfm_gpu_moe_reserve(self._h, max_tokens))
 

@@ -284,6 +284,40 @@ ORC_EXPORT int orc_moe_forward(int order, float *x, uint32_t T, uint32_t D, uint
     return 0;
 }
 
+/* Expert-parallel pieces (for the host-logic tests of expert parallelism):
+ * rows a = 0..n-1, each one (token, k) assignment given as its Q8_K blocks
+ * xq[a][D/256] and its expert ids[a] (0-based within gate/up/down, which hold
+ * the shard's experts): y[a] = Down_e(Q8_K(SwiGLU(Gate_e xq, Up_e xq))),
+ * unweighted -- the inner loop of orc_moe_forward
+ * (tools/lfm2_moe_checkpoint.c:338-363). */
+ORC_EXPORT int orc_expert_rows(int order, uint32_t D, uint32_t I, const void *gate, const void *up,
+                               const void *down, const void *xq_rows, const uint32_t *ids, uint32_t n,
+                               float *y) {
+    if (D % 256 || I % 256) return -1;
+    const uint32_t nbd = D / 256, nbi = I / 256;
+    float *h = (float *)malloc(sizeof(float) * I);
+    orc_q8k *hq = (orc_q8k *)malloc(sizeof(orc_q8k) * nbi);
+    if (!h || !hq) { free(h); free(hq); return -2; }
+    const orc_q4k *G = (const orc_q4k *)gate, *U = (const orc_q4k *)up, *Dn = (const orc_q4k *)down;
+    const orc_q8k *X = (const orc_q8k *)xq_rows;
+    for (uint32_t a = 0; a < n; ++a) {
+        const uint32_t e = ids[a];
+        orc_swiglu(order, G + (size_t)e * I * nbd, U + (size_t)e * I * nbd, D, I, X + (size_t)a * nbd, h, hq);
+        orc_q4k_rows(order, Dn + (size_t)e * D * nbi, I, 0, D, hq, y + (size_t)a * D);
+    }
+    free(h); free(hq);
+    return 0;
+}
+
+/* x[t][r] = fmaf(w[t][k], y[t*K+k][r], x[t][r]) for k = 0..K-1 in order
+ * (tools/lfm2_moe_checkpoint.c:266-269). */
+ORC_EXPORT void orc_ep_combine(float *x, uint32_t T, uint32_t D, uint32_t K, const float *w, const float *y) {
+    for (uint32_t t = 0; t < T; ++t)
+        for (uint32_t k = 0; k < K; ++k)
+            for (uint32_t r = 0; r < D; ++r)
+                x[(size_t)t * D + r] = fmaf(w[(size_t)t * K + k], y[((size_t)t * K + k) * D + r], x[(size_t)t * D + r]);
+}
+
 /* Dense SwiGLU FFN (leading layers of an lfm2moe stack), tools/lfm2_decode_1x4.c:
  * 1070-1104: RMSNorm+Q8_K, SwiGLU -> Q8_K, down, then x[r] = x[r] + down[r]. */
 ORC_EXPORT int orc_dense_ffn_forward(int order, float *x, uint32_t T, uint32_t D, uint32_t I, float eps,

@@ -56,6 +56,9 @@ class Oracle:
         lib.orc_kat_q8k_inputs.argtypes = [_vp, _u32]
         lib.orc_dense_ffn_forward.restype = _int
         lib.orc_dense_ffn_forward.argtypes = [_int, _vp, _u32, _u32, _u32, _f32, _vp, _vp, _vp, _vp]
+        lib.orc_expert_rows.restype = _int
+        lib.orc_expert_rows.argtypes = [_int, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u32, _vp]
+        lib.orc_ep_combine.argtypes = [_vp, _u32, _u32, _u32, _vp, _vp]
         self.lib = lib
 
     def quantize_q8k(self, x: np.ndarray) -> np.ndarray:
@@ -114,6 +117,45 @@ class Oracle:
         self.lib.orc_q4k_row_ints(_p(np.ascontiguousarray(row)), _p(np.ascontiguousarray(xq)), n_cols, _p(sub),
                                   _p(acc), _p(mins))
         return sub, acc, mins
+
+    # -- expert-parallel pieces (host-logic tests of laii_b200.ep) ----------
+    def ep_route(self, L, x: np.ndarray):
+        """x[T, D] -> idx[T, K] (global ids), w[T, K], q8[T, D/256*292] (block_q8_K rows)."""
+        T = x.shape[0]
+        idx = np.zeros((T, L.K), np.int32)
+        w = np.zeros((T, L.K), np.float32)
+        q8 = np.zeros((T, L.D // 256 * 292), np.uint8)
+        for t in range(T):
+            xb, q8[t] = self.rmsnorm_q8k(x[t], L.ffn_norm, L.eps)
+            i, wt, _, _ = self.route(L.router_w, L.bias, xb, L.K, L.norm_topk_prob, L.routed_scale)
+            idx[t], w[t] = i.astype(np.int32), wt
+        return idx, w, q8
+
+    def ep_expert_rows(self, L, first: int, count: int, q8: np.ndarray, ids: np.ndarray, order=ORDER_VNNI):
+        """Rows of global experts ids (all in [first, first+count)) -> y[n, D], unweighted."""
+        n = ids.shape[0]
+        per_gu = L.I * (L.D // 256) * 144
+        per_dn = L.D * (L.I // 256) * 144
+        g = np.ascontiguousarray(L.gate.reshape(-1)[first * per_gu:(first + count) * per_gu])
+        u = np.ascontiguousarray(L.up.reshape(-1)[first * per_gu:(first + count) * per_gu])
+        dn = np.ascontiguousarray(L.down.reshape(-1)[first * per_dn:(first + count) * per_dn])
+        local = np.ascontiguousarray(ids.astype(np.int64) - first, np.uint32)
+        assert np.all((ids >= first) & (ids < first + count)), "row routed to a foreign expert"
+        y = np.zeros((n, L.D), np.float32)
+        if n:
+            st = self.lib.orc_expert_rows(order, L.D, L.I, _p(g), _p(u), _p(dn), _p(np.ascontiguousarray(q8)),
+                                          _p(local), n, _p(y))
+            if st != 0:
+                raise RuntimeError(f"oracle expert_rows status {st}")
+        return y
+
+    def ep_combine(self, x: np.ndarray, w: np.ndarray, y: np.ndarray):
+        """x[T, D] in place: x[t] = fmaf(w[t, k], y[t*K + k], x[t]) for k in order."""
+        T, D = x.shape
+        K = w.shape[1]
+        self.lib.orc_ep_combine(_p(x), T, D, K, _p(np.ascontiguousarray(w, np.float32)),
+                                _p(np.ascontiguousarray(y, np.float32)))
+        return x
 
     def moe_forward(self, L, x: np.ndarray, order=ORDER_VNNI, want_h=False):
         """x[T, D] -> (x_out, idx[T,K], w[T,K], xq bytes, h[T,K,I] or None); x is not modified."""

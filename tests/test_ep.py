@@ -1,0 +1,188 @@
+"""Expert parallelism (laii_b200.ep).
+
+CPU: shard bookkeeping, and the whole exchange logic with two gloo ranks and
+the oracle as the expert compute (bit-exact against the single-process oracle
+layer).  GPU: the lfm_gpu_moe_ep_* path through the C-ABI, against the regular
+forward -- on one GPU as a world of one, and as a world of two (two handles,
+one per "rank", exchanging through an in-process mailbox; these kernels never
+wait on one another, so sharing one GPU is safe).
+"""
+import os
+import socket
+import threading
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cached_layer, rel_l2
+from laii_b200 import ep
+
+REL_L2, MAX_ABS = 1e-3, 5e-3
+
+
+class OracleOps:
+    """Test-only ops: the CPU oracle restatement as route / experts / combine."""
+
+    def __init__(self, L, first, count):
+        from oracle.oracle import Oracle
+        self.o = Oracle()
+        self.L, self.first, self.count = L, first, count
+
+    def route(self, layer, x):
+        idx, w, q8 = self.o.ep_route(self.L, x.numpy())
+        return torch.from_numpy(idx), torch.from_numpy(w), torch.from_numpy(q8)
+
+    def experts(self, layer, q8, ids):
+        return torch.from_numpy(self.o.ep_expert_rows(self.L, self.first, self.count, q8.numpy(), ids.numpy()))
+
+    def combine(self, layer, x, w, y):
+        self.o.ep_combine(x.numpy(), w.numpy(), y.numpy())
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shards_tile_the_experts():
+    for E in (1, 7, 32, 64, 256):
+        for world in (1, 2, 3, 8):
+            if world > E:
+                continue
+            seen = []
+            sizes = []
+            for r in range(world):
+                first, n = ep.shard_of(E, world, r)
+                seen += list(range(first, first + n))
+                sizes.append(n)
+            assert seen == list(range(E))
+            assert max(sizes) - min(sizes) <= 1
+            owners = ep.owner_of(torch.arange(E), E, world).tolist()
+            for r in range(world):
+                first, n = ep.shard_of(E, world, r)
+                assert owners[first:first + n] == [r] * n
+
+
+D, E, K, I, T_PER_RANK = 512, 8, 2, 512, 5
+
+
+def _gloo_rank(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from laii_b200 import synth
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        L = synth.make_moe_layer(D, E, K, I, layer=3)
+        x_all = synth.make_hidden(world * T_PER_RANK, D, seed_offset=5)
+        x = torch.from_numpy(np.array(x_all[rank * T_PER_RANK:(rank + 1) * T_PER_RANK], copy=True))
+        first, count = ep.shard_of(E, world, rank)
+        ep.ep_forward(OracleOps(L, first, count), ep.TorchComm(), 0, x, E, K)
+        np.save(os.path.join(out_dir, f"x{rank}.npy"), x.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_two_gloo_ranks_equal_the_single_rank_oracle(tmp_path):
+    import torch.multiprocessing as mp
+    from laii_b200 import synth
+    from oracle.oracle import Oracle
+    world = 2
+    mp.spawn(_gloo_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    got = np.concatenate([np.load(tmp_path / f"x{r}.npy") for r in range(world)])
+    L = synth.make_moe_layer(D, E, K, I, layer=3)
+    want, _, _, _, _ = Oracle().moe_forward(L, synth.make_hidden(world * T_PER_RANK, D, seed_offset=5))
+    assert np.array_equal(got, want)
+
+
+class MailboxComm:
+    """A world of `world` ranks as threads of one process (GPU tensors handed over in memory)."""
+
+    def __init__(self, world, rank, box, barrier):
+        self.world, self.rank, self.box, self.barrier = world, rank, box, barrier
+
+    def exchange(self, send, send_counts, recv_counts=None):
+        torch.cuda.synchronize()
+        offs = np.cumsum([0] + list(send_counts))
+        for dst in range(self.world):
+            self.box[(self.rank, dst)] = send[offs[dst]:offs[dst + 1]]
+        self.barrier.wait()
+        parts = [self.box[(src, self.rank)] for src in range(self.world)]
+        self.barrier.wait()
+        return torch.cat(parts), [p.shape[0] for p in parts]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,T", [(1, 8), (2, 6), (4, 3)])
+def test_ep_on_one_gpu_matches_forward(world, T):
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    Dg, Eg, Kg, Ig = 2048, 32, 4, 1792
+    L = cached_layer(Dg, Eg, Kg, Ig)
+    x_all = synth.make_hidden(world * T, Dg, seed_offset=31)
+    ref_h = GpuMoE(0)
+    ref_h.upload_layer(0, L)
+    want = ref_h.forward(0, np.array(x_all, copy=True))
+    ref_h.close()
+    handles = []
+    for r in range(world):
+        g = GpuMoE(0)
+        first, count = ep.shard_of(Eg, world, r)
+        g.upload_layer_shard(0, L, first, count)
+        handles.append(g)
+    box, barrier = {}, threading.Barrier(world)
+    outs = [None] * world
+    errs = []
+
+    def run(r):
+        try:
+            torch.cuda.set_device(0)
+            x = torch.from_numpy(np.array(x_all[r * T:(r + 1) * T], copy=True)).cuda()
+            comm = ep.LocalComm() if world == 1 else MailboxComm(world, r, box, barrier)
+            ep.ep_forward(ep.GpuOps(handles[r], Dg, Kg), comm, 0, x, Eg, Kg)
+            torch.cuda.synchronize()
+            handles[r].sync()
+            outs[r] = x.cpu().numpy()
+        except Exception as e:  # surfaced below
+            errs.append(e)
+            barrier.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    for g in handles:
+        g.close()
+    assert not errs, errs
+    got = np.concatenate(outs)
+    assert rel_l2(got, want) <= REL_L2
+    assert float(np.abs(got - want).max()) <= MAX_ABS
+
+
+@pytest.mark.gpu
+def test_shard_layer_refuses_the_regular_forward():
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE, MoEError
+    L = cached_layer(2048, 32, 4, 1792)
+    with GpuMoE(0) as g:
+        g.upload_layer_shard(0, L, 8, 8)
+        with pytest.raises(MoEError) as ei:
+            g.forward(0, synth.make_hidden(2, 2048))
+        assert ei.value.status == -2
+
+
+@pytest.mark.gpu
+def test_synth_shard_matches_the_full_layer_bytes():
+    from laii_b200.moe import GpuMoE
+    import bench
+    D_, E_, K_, I_ = 2048, 32, 4, 1792
+    per_gu = I_ * (D_ // 256) * 144
+    with GpuMoE(0) as g:
+        g.synth_layer(0, D_, E_, K_, I_, bench.layer_seeds(0))
+        g.synth_layer_shard(1, D_, E_, K_, I_, bench.layer_seeds(0), 20, 4)
+        full = g.read_layer(0, "gate", E_ * per_gu)
+        part = g.read_layer(1, "gate", 4 * per_gu)
+        assert np.array_equal(full[20 * per_gu:24 * per_gu], part)
