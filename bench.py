@@ -131,6 +131,15 @@ def layer_seeds(layer):
                                                    synth.SEED_ROUTER, synth.SEED_BIAS)]
 
 
+def zipf_bias_for(cfg, layer):
+    """exp_probs_b giving Zipf(s) expert popularity for the seeded router of `layer` (config 3)."""
+    from types import SimpleNamespace
+    from laii_b200 import synth
+    D, E = cfg["D"], cfg["E"]
+    router = synth.normal_f32(E * D, synth.layer_seed(synth.SEED_ROUTER, layer), std=0.02).reshape(E, D)
+    return synth.zipf_bias(SimpleNamespace(E=E, K=cfg["K"], D=D, eps=1e-5, router_w=router), s=cfg["zipf"])
+
+
 def cpu_baseline(cfg, seconds=12.0, threads=0):
     """The reference's CPU MoE FFN (built from its sources) on this host, bounded sample."""
     from laii_b200 import synth
@@ -212,7 +221,8 @@ def run_ours(args, cfg):
     R = args.ring
     g = GpuMoE(local)
     for l in range(R):
-        g.synth_layer(l, D, E, K, I, layer_seeds(l))
+        bias = zipf_bias_for(cfg, l) if cfg.get("zipf") else None
+        g.synth_layer(l, D, E, K, I, layer_seeds(l), bias=bias)
     g.reserve(T)
     x0 = synth.make_hidden(T, D, seed_offset=rank * T)
     x = torch.from_numpy(x0.copy()).cuda()
@@ -277,7 +287,13 @@ def run_ours(args, cfg):
     per_launch_bytes = {"gateup": ploads * gu_bytes / n_launch + T * D * 1.140625,
                         "down": ploads * dn_bytes / n_launch + T * K * I * 1.140625 + T * K * D * 4,
                         "moe_layer": ploads * (gu_bytes + dn_bytes) / n_launch + E * D * 4 + 2 * T * D * 4}
-    ach = per_launch_bytes.get(dom, 0.0) / (tot_ms / n_launch / 1e3) / 1e9
+    tensor_bound = dom.startswith("gemm_")
+    if tensor_bound:
+        # int8 ops of one GEMM launch: 2 * (T*K rows) * rows_out * cols (each matrix once)
+        gemm_ops = {"gemm_gate": 2.0 * T * K * I * D, "gemm_up": 2.0 * T * K * I * D, "gemm_down": 2.0 * T * K * D * I}
+        ach = gemm_ops[dom] / (tot_ms / n_launch / 1e3) / 1e12
+    else:
+        ach = per_launch_bytes.get(dom, 0.0) / (tot_ms / n_launch / 1e3) / 1e9
     total_prof = sum(v[1] for v in prof.values())
     traffic = None
     tfile = os.path.join(ROOT, "profiles", f"traffic_{dom}_cfg{args.config}.json")
@@ -314,8 +330,12 @@ def run_ours(args, cfg):
                "config": config_dict(args.config, cfg, R, {"parallelism": f"replicas x{ws}" if ws > 1 else "single",
                                                            "layer_hbm_frac": round(layer_frac, 4),
                                                            "unique_experts_per_step": loads / args.steps}),
-               "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                            "frac": ach / pk["hbm_gbs"], "traffic": traffic, "peak_src": pk["src"] + " (burst copy)",
+               "roofline": ({"bound": "tensor", "kernel": dom, "achieved": ach, "peak": 4500.0, "unit": "TOP/s (int8)",
+                             "frac": ach / 4500.0, "traffic": traffic,
+                             "peak_src": "nominal dense int8 4.5 POPS (MEASURED_PEAKS.json holds no int8 figure)"}
+                            if tensor_bound else
+                            {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": ach / pk["hbm_gbs"], "traffic": traffic, "peak_src": pk["src"] + " (burst copy)"}) | {
                             "share": tot_ms / total_prof,
                             "kernel_ms": {k: round(v[1] / v[0] * 1e3, 2) for k, v in prof.items()},
                             "kernel_ms_unit": "us per launch"},
@@ -329,12 +349,164 @@ def run_ours(args, cfg):
         torch.distributed.destroy_process_group()
 
 
+def stack_layers(cfg):
+    """(kind, layer index) of a stack config: dense layers first, then MoE layers."""
+    return [("dense", l) for l in range(cfg.get("dense", 0))] + \
+           [("moe", cfg.get("dense", 0) + m) for m in range(cfg["layers"])]
+
+
+def stack_cpu_baseline(cfg, seconds, threads=0):
+    """The reference's CPU path per (token, layer), timed on one MoE (and one dense) layer over a bounded
+    sample and extrapolated to the stack: tok/s = 1 / sum over layers of the per-token layer time."""
+    from laii_b200 import synth
+    from oracle.oracle import REF_SO, Reference
+    if not os.path.exists(REF_SO):
+        return None
+    R = Reference(threads)
+    D = cfg["D"]
+    L = synth.make_moe_layer(D, cfg["E"], cfg["K"], cfg["I"], layer=cfg.get("dense", 0))
+    per_layer = {}
+    layers = [("moe", L)]
+    if cfg.get("dense", 0):
+        layers.append(("dense", synth.make_dense_layer(D, cfg["dense_I"], layer=0)))
+    for kind, lay in layers:
+        x = synth.make_hidden(8, D, seed_offset=0)
+        fwd = (lambda xx: R.moe_forward(lay, xx, capture=False)) if kind == "moe" else (lambda xx: R.dense_forward(lay, xx))
+        fwd(x)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / len(layers):
+            fwd(x)
+            n += 1
+        per_layer[kind] = (time.perf_counter() - t0) / (n * 8)
+    t_tok = cfg["layers"] * per_layer["moe"] + cfg.get("dense", 0) * per_layer.get("dense", 0.0)
+    return {"value": 1.0 / t_tok, "unit": "tok/s", "cores": R.n_threads, "kind": "reference",
+            "sample": f"per-token layer time of the reference (one call per token, 8-token batches) on one MoE layer "
+                      f"({per_layer['moe'] * 1e6:.0f} us)" + (f" and one dense layer ({per_layer['dense'] * 1e6:.0f} us)"
+                                                              if "dense" in per_layer else "") +
+                      f", extrapolated to the {len(stack_layers(cfg))}-layer stack; {R.isa}; nproc={os.cpu_count()}"}
+
+
+def run_stack(args, cfg):
+    """Configs 4 and 5: a stack of FFN layers, T tokens in total per step (strong scaling over ranks).
+    One GPU: the stack as one captured forward.  N GPUs with --ep: experts sharded across ranks,
+    each rank's T/N tokens routed and exchanged with NCCL all-to-all (laii_b200.ep)."""
+    import torch
+    ws, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
+    from laii_b200 import ep, synth
+    from laii_b200.moe import GpuMoE
+
+    D, E, K, I, T = cfg["D"], cfg["E"], cfg["K"], cfg["I"], cfg["T"]
+    use_ep = args.ep and ws > 1
+    if T % ws:
+        raise SystemExit(f"T={T} does not split over {ws} ranks")
+    Tl = T // ws
+    g = GpuMoE(local)
+    layers = stack_layers(cfg)
+    first, count = ep.shard_of(E, ws, rank) if use_ep else (0, E)
+    for kind, l in layers:
+        if kind == "dense":
+            g.upload_dense(l, synth.make_dense_layer(D, cfg["dense_I"], layer=l))
+        elif use_ep:
+            g.synth_layer_shard(l, D, E, K, I, layer_seeds(l), first, count)
+        else:
+            g.synth_layer(l, D, E, K, I, layer_seeds(l))
+    g.reserve(max(Tl * K if use_ep else Tl, Tl))
+    x0 = synth.make_hidden(Tl, D, seed_offset=rank * Tl)
+    x = torch.from_numpy(x0.copy()).cuda()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    comm = ep.TorchComm() if use_ep else None
+    ops = ep.GpuOps(g, D, K) if use_ep else None
+
+    def step():
+        if not use_ep:
+            g.forward_device(0, x.data_ptr(), Tl, stream=sp, n_layers=len(layers))
+            return
+        for kind, l in layers:
+            if kind == "dense":
+                g.forward_device(l, x.data_ptr(), Tl, stream=sp)
+            else:
+                ep.ep_forward(ops, comm, l, x, E, K)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    st0 = g.last_stats()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    st1 = g.last_stats()
+    loads = float(st1["expert_loads"] - st0["expert_loads"])
+    if ws > 1:
+        t = torch.tensor([ms, loads], device="cuda", dtype=torch.float64)
+        mx = t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+        ms, loads = float(mx[0].item()), float(t[1].item())
+    ms_step = ms / args.steps
+    value = T * args.steps / (ms / 1e3)
+    pk = peaks()
+    n_moe, n_dense = cfg["layers"], cfg.get("dense", 0)
+    if T <= 64:  # decode: HBM-bound on the active experts' bytes
+        dense_bytes = n_dense * 3 * cfg.get("dense_I", 0) * D * Q4K // 256
+        step_bytes = loads / args.steps * expert_bytes(cfg) + n_moe * E * D * 4 + dense_bytes + 2 * T * D * 4
+        ach = step_bytes / (ms_step / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "stack step", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": ach / pk["hbm_gbs"], "traffic": None, "peak_src": pk["src"] + " (burst copy)",
+                "algorithmic_bytes_per_step": step_bytes}
+    else:  # prefill: int8 tensor-op bound
+        ops_step = 2.0 * T * K * 3 * I * D * n_moe
+        ach = ops_step / (ms_step / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": "stack step", "achieved": ach, "peak": 4500.0, "unit": "TOP/s (int8)",
+                "frac": ach / 4500.0, "traffic": None,
+                "peak_src": "nominal dense int8 4.5 POPS (MEASURED_PEAKS.json holds no int8 figure)",
+                "algorithmic_ops_per_step": ops_step}
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = stack_cpu_baseline(cfg, args.cpu_seconds)
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+               "vs_baseline": None, "dtype": "q4_k x q8_k int (dp4a), fp32 accum", "data": "synthetic (seeded)",
+               "config": {"workload": f"cfg{args.config}: {cfg['name']} ({n_dense} dense + {n_moe} lfm2moe FFN layers, "
+                                      f"D={D} E={E} top-{K} I={I}, {T} tokens per step in total)",
+                          "tokens_per_step": T, "layers": len(layers),
+                          "parallelism": f"expert-parallel x{ws} (E/{ws} experts per rank, NCCL all-to-all)"
+                          if use_ep else ("single" if ws == 1 else f"replicas x{ws}"),
+                          "l2": "the stack's weights exceed the 126 MB L2; every step streams them from HBM",
+                          "unique_experts_per_moe_layer": loads / args.steps / n_moe},
+               "roofline": roof, "cpu_baseline": cpu, "gpu_launches": None, "clocks": clk}
+        print(json.dumps(out), flush=True)
+    g.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--ep", action="store_true", help="configs 4/5 under torchrun: expert parallelism")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ring", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -344,6 +516,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif args.config >= 4:
+        run_stack(args, cfg)
     else:
         run_ours(args, cfg)
 

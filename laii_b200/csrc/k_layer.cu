@@ -509,7 +509,6 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
         }
     }
     __syncthreads();
-    const uint32_t P = (uint32_t)sh.npairs;
 
     if (alive) alive = lfm_mbar_wait(&sh.bar_in, 1, err); /* the records copied after barrier 1 */
 

@@ -45,13 +45,19 @@ struct Workspace {
     unsigned *gbar = nullptr; /* [2] grid barrier of the fused layer (counter region) */
     uint8_t *xrec = nullptr;  /* [T][D/256] Q8_K records exchanged by the fused layer */
     float *scores = nullptr;  /* [T*E][2] router scores exchanged by the fused layer */
+    float *u = nullptr;       /* [T*K][I] up projections of the prefill GEMM path (h holds gate) */
+    void *tiles_gu = nullptr; /* GEMM tile plans: gate|up rows (I), down rows (D) */
+    void *tiles_dn = nullptr;
+    int32_t *n_tiles = nullptr; /* [2] */
+    uint32_t max_tiles_gu = 0, max_tiles_dn = 0;
 };
 
 }  // namespace
 
 namespace {
-enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_COUNT };
-const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer"};
+enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D, K_COUNT };
+const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer",
+                                           "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -80,6 +86,7 @@ struct lfm_gpu_moe {
     std::vector<ProfRec> recs;
     bool use_graphs = true;
     bool use_fused = true;   /* fused decode layer for T <= LFM_FUSED_MAX_T */
+    bool use_gemm = true;    /* tensor-core grouped GEMMs for prefill-sized T */
     std::vector<GraphEntry> graphs;
 };
 
@@ -178,6 +185,11 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_y = take(sizeof(float) * TK * D);
     const size_t o_xrec = take((size_t)T * (D / 256) * 304);
     const size_t o_scores = take(sizeof(float) * 2 * T * E);
+    const size_t mt_gu = lfm_gemm_tiles_max(I, (uint32_t)TK, E), mt_dn = lfm_gemm_tiles_max(D, (uint32_t)TK, E);
+    const size_t o_u = take(sizeof(float) * TK * I);
+    const size_t o_tgu = take(lfm_gemm_tile_bytes() * mt_gu);
+    const size_t o_tdn = take(lfm_gemm_tile_bytes() * mt_dn);
+    const size_t o_nt = take(sizeof(int32_t) * 2);
     void *base = nullptr;
     /* the old workspace may still be read by queued work on any stream */
     cudaError_t e = cudaDeviceSynchronize();
@@ -215,6 +227,12 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.gbar = reinterpret_cast<unsigned *>(b + o_gbar);
     w.xrec = b + o_xrec;
     w.scores = reinterpret_cast<float *>(b + o_scores);
+    w.u = reinterpret_cast<float *>(b + o_u);
+    w.tiles_gu = b + o_tgu;
+    w.tiles_dn = b + o_tdn;
+    w.n_tiles = reinterpret_cast<int32_t *>(b + o_nt);
+    w.max_tiles_gu = (uint32_t)mt_gu;
+    w.max_tiles_dn = (uint32_t)mt_dn;
     return LFM_GPU_OK;
 }
 
@@ -273,6 +291,25 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
         return LFM_GPU_OK;
     }
     LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
+    if (h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L)) {
+        /* prefill: grouped GEMMs on the tensor cores (k_gemm.cu) */
+        LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
+            cudaError_t e = lfm_launch_gemm_plan(w.rt, L.I, w.tiles_gu, w.n_tiles, w.max_tiles_gu, s);
+            return e == cudaSuccess ? lfm_launch_gemm_plan(w.rt, L.D, w.tiles_dn, w.n_tiles + 1, w.max_tiles_dn, s) : e;
+        }));
+        LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
+            return lfm_launch_q4k_gemm(L.gate, L.I, L.D, xq, w.rt.perm, K, w.tiles_gu, w.n_tiles, w.h, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_GEMM_U, s, [&] {
+            return lfm_launch_q4k_gemm(L.up, L.I, L.D, xq, w.rt.perm, K, w.tiles_gu, w.n_tiles, w.u, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, T * K, L.I, hq, s); }));
+        LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
+            return lfm_launch_q4k_gemm(L.down, L.D, L.I, hq, nullptr, 1, w.tiles_dn, w.n_tiles + 1, w.y, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
+        return LFM_GPU_OK;
+    }
     LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, xq, w.rt, w.h, grid, s, pdl); }));
     LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * K, L.I, hq, s, pdl); }));
     LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, hq, w.rt, w.y, grid, s, pdl); }));
@@ -304,6 +341,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
     {
         const char *nf = getenv("LFM_GPU_MOE_NO_FUSED"); /* force the separate-kernel path (A/B runs) */
         h->use_fused = !(nf && nf[0] && nf[0] != '0');
+        const char *ng = getenv("LFM_GPU_MOE_NO_GEMM"); /* force the GEMV path for prefill (A/B runs) */
+        h->use_gemm = !(ng && ng[0] && ng[0] != '0');
     }
     DeviceGuard g(device_id);
     if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess ||

@@ -107,6 +107,17 @@ cudaError_t lfm_launch_ep_combine(float *x, uint32_t T, uint32_t D, uint32_t K, 
                                   cudaStream_t s);
 cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cudaStream_t s);
 
+/* k_gemm.cu: prefill grouped GEMM (tensor cores) */
+size_t lfm_gemm_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);
+size_t lfm_gemm_tile_bytes();
+cudaError_t lfm_launch_gemm_plan(const RouteTables &rt, uint32_t rows, void *tiles, int32_t *n_tiles,
+                                 uint32_t max_tiles, cudaStream_t s);
+cudaError_t lfm_launch_q4k_gemm(const uint8_t *W, uint32_t rows, uint32_t cols, Q8Rows X, const int32_t *perm,
+                                uint32_t K, const void *tiles, const int32_t *n_tiles, float *Y, uint32_t *err,
+                                int grid, cudaStream_t s);
+cudaError_t lfm_launch_swiglu_quant(const float *G, const float *U, uint32_t rows, uint32_t cols, Q8Rows dst,
+                                    cudaStream_t s);
+
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
 cudaError_t lfm_launch_synth_q4k(uint8_t *out, uint64_t n_blocks, uint64_t seed, float stddev, cudaStream_t s,

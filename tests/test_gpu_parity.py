@@ -173,6 +173,39 @@ def test_prefill_zipf_subset(oracle, gpu):
     assert np.abs(xg[sub][m] - xo[m]).max() <= MAX_ABS
 
 
+@pytest.mark.parametrize("D,E,K,I,T", [(512, 8, 2, 512, 256), (2048, 32, 4, 1792, 512)])
+def test_prefill_gemm_equals_gemv(monkeypatch, D, E, K, I, T):
+    """The tensor-core GEMM path (prefill-sized T) and the dp4a GEMV path form the
+    same exact integer sums and the same fp32 update order: identical outputs."""
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    L = cached_layer(D, E, K, I, layer=2)
+    x = synth.make_hidden(T, D, seed_offset=41)
+    with GpuMoE(0) as g:
+        g.upload_layer(0, L)
+        a = g.forward(0, np.array(x, copy=True))
+    monkeypatch.setenv("LFM_GPU_MOE_NO_GEMM", "1")
+    with GpuMoE(0) as g:
+        g.upload_layer(0, L)
+        b = g.forward(0, np.array(x, copy=True))
+    assert np.array_equal(a, b)
+
+
+def test_prefill_gemm_path_is_taken_and_dense_matches_oracle(oracle, gpu):
+    """A dense layer at T=64 goes through the GEMM path (per-kernel profile) and matches the oracle."""
+    from laii_b200 import synth
+    L = cached_dense(2048, 7168)
+    gpu.upload_dense(6, L)
+    x = synth.make_hidden(64, 2048, seed_offset=9)
+    gpu.profile(True)
+    xg = gpu.forward(6, np.array(x, copy=True))
+    prof = gpu.profile_read()
+    gpu.profile(False)
+    assert "gemm_gate" in prof and "gemm_down" in prof
+    xo = oracle.dense_forward(L, x)
+    assert rel_l2(xg, xo) <= REL_L2 and np.abs(xg - xo).max() <= MAX_ABS
+
+
 def test_device_synth_matches_host(gpu):
     """A layer generated on the device equals the host-generated one, byte for byte."""
     from laii_b200 import synth
