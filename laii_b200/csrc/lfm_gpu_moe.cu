@@ -272,27 +272,16 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
     return e;
 }
 
-/* One layer forward on device x; `stream` already resolved.
- * T <= LFM_FUSED_MAX_T: one cooperative launch of the fused layer (k_layer.cu).
- * Otherwise route(+dispatch) -> gate|up(+SwiGLU) -> h->Q8_K -> down -> combine
- * chained with programmatic dependent launch.
- * Profiling brackets each launch with events, which breaks the PDL overlap,
- * so it is turned off while profiling. */
-lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s) {
-    const MoeLayerDev &L = S.dev;
-    Workspace &w = h->ws;  /* sized for the whole call by forward_common */
-    Q8Rows xq = w.xq; xq.cols = L.D;
+/* Everything after routing: gate|up + SwiGLU, Q8_K(h), down, combine into x.
+ * Prefill-sized loads (T > 16 and >= 32 slots per expert on average) take the
+ * tensor-core grouped GEMMs (k_gemm.cu), smaller ones the grouped GEMVs. */
+lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, uint32_t T, Q8Rows xq,
+                             cudaStream_t s, bool pdl) {
+    Workspace &w = h->ws;
     Q8Rows hq = w.hq; hq.cols = L.I;
-    const bool pdl = !h->prof;
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
-    if (h->use_fused && lfm_fused_ok(L, T, grid)) {
-        LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
-        return LFM_GPU_OK;
-    }
-    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
     if (h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L)) {
-        /* prefill: grouped GEMMs on the tensor cores (k_gemm.cu) */
         LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
             cudaError_t e = lfm_launch_gemm_plan(w.rt, L.I, w.tiles_gu, w.n_tiles, w.max_tiles_gu, s);
             return e == cudaSuccess ? lfm_launch_gemm_plan(w.rt, L.D, w.tiles_dn, w.n_tiles + 1, w.max_tiles_dn, s) : e;
@@ -315,6 +304,26 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
     LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, hq, w.rt, w.y, grid, s, pdl); }));
     LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, pdl); }));
     return LFM_GPU_OK;
+}
+
+/* One layer forward on device x; `stream` already resolved.
+ * T <= LFM_FUSED_MAX_T: one cooperative launch of the fused layer (k_layer.cu).
+ * Otherwise route(+dispatch) -> gate|up(+SwiGLU) -> h->Q8_K -> down -> combine
+ * chained with programmatic dependent launch.
+ * Profiling brackets each launch with events, which breaks the PDL overlap,
+ * so it is turned off while profiling. */
+lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s) {
+    const MoeLayerDev &L = S.dev;
+    Workspace &w = h->ws;  /* sized for the whole call by forward_common */
+    Q8Rows xq = w.xq; xq.cols = L.D;
+    const bool pdl = !h->prof;
+    const int grid = h->sm_count;
+    if (h->use_fused && lfm_fused_ok(L, T, grid)) {
+        LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
+        return LFM_GPU_OK;
+    }
+    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
+    return run_experts(h, L, x, T, xq, s, pdl);
 }
 
 lfm_gpu_status_t read_device_error(lfm_gpu_moe_t *h) {
@@ -940,7 +949,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_route(lfm_gpu_moe_t *h, uint32_t layer, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     Workspace &w = h->ws;
     Q8Rows xq = w.xq; xq.cols = L.D;
-    LFM_CUDA(h, lfm_launch_route(L, x, T, xq, w.rt, s, false));
+    RouteTables rt = w.rt;
+    rt.loads = nullptr; /* expert loads are counted where the experts run (lfm_gpu_moe_ep_experts) */
+    LFM_CUDA(h, lfm_launch_route(L, x, T, xq, rt, s, false));
     LFM_CUDA(h, cudaMemcpyAsync(idx_out, w.rt.idx, sizeof(int32_t) * T * L.K, cudaMemcpyDeviceToDevice, s));
     LFM_CUDA(h, cudaMemcpyAsync(w_out, w.rt.w, sizeof(float) * T * L.K, cudaMemcpyDeviceToDevice, s));
     LFM_CUDA(h, lfm_launch_q8_to_gguf(xq, T, static_cast<uint8_t *>(q8_out), s));
@@ -970,17 +981,11 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     Workspace &w = h->ws;
     Q8Rows xq = w.xq; xq.cols = Lx.D;
-    Q8Rows hq = w.hq; hq.cols = Lx.I;
-    const int grid = h->sm_count;
     LFM_CUDA(h, lfm_launch_gguf_to_q8(static_cast<const uint8_t *>(q8_in), n_rows, xq, s));
     LFM_CUDA(h, lfm_launch_ep_prepare(expert_ids, n_rows, first, count, w.rt, s));
     LFM_CUDA(h, lfm_launch_dispatch(Lx, n_rows, w.rt, s));
     LFM_CUDA(h, cudaMemsetAsync(y_out, 0, sizeof(float) * n_rows * Lx.D, s));
-    LFM_CUDA(h, lfm_launch_gateup(Lx, xq, w.rt, w.h, grid, s, false));
-    LFM_CUDA(h, lfm_launch_quant_rows(w.h, n_rows, Lx.I, hq, s, false));
-    LFM_CUDA(h, lfm_launch_down(Lx, hq, w.rt, w.y, grid, s, false));
-    LFM_CUDA(h, lfm_launch_combine(Lx, y_out, n_rows, w.rt, w.y, s, false)); /* y_out = fma(1, y, 0) = y */
-    return LFM_GPU_OK;
+    return run_experts(h, Lx, y_out, n_rows, xq, s, false); /* y_out = fma(1, y, 0) = y */
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,

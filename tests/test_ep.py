@@ -186,3 +186,47 @@ def test_synth_shard_matches_the_full_layer_bytes():
         full = g.read_layer(0, "gate", E_ * per_gu)
         part = g.read_layer(1, "gate", 4 * per_gu)
         assert np.array_equal(full[20 * per_gu:24 * per_gu], part)
+
+
+def _nccl_rank(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    try:
+        Dg, Eg, Kg, Ig, T = 2048, 32, 4, 1792, 24
+        L = synth.make_moe_layer(Dg, Eg, Kg, Ig, layer=7)
+        x_all = synth.make_hidden(world * T, Dg, seed_offset=61)
+        g = GpuMoE(rank)
+        first, count = ep.shard_of(Eg, world, rank)
+        g.upload_layer_shard(0, L, first, count)
+        x = torch.from_numpy(np.array(x_all[rank * T:(rank + 1) * T], copy=True)).cuda()
+        ep.ep_forward(ep.GpuOps(g, Dg, Kg), ep.TorchComm(), 0, x, Eg, Kg)
+        torch.cuda.synchronize()
+        g.sync()
+        np.save(os.path.join(out_dir, f"x{rank}.npy"), x.cpu().numpy())
+        g.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_nccl_two_gpus_match_single_gpu_forward(tmp_path):
+    """Expert parallelism across two GPUs (NCCL all-to-all) against the one-GPU layer."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    world, T = 2, 24
+    mp.spawn(_nccl_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    got = np.concatenate([np.load(tmp_path / f"x{r}.npy") for r in range(world)])
+    L = synth.make_moe_layer(2048, 32, 4, 1792, layer=7)
+    with GpuMoE(0) as g:
+        g.upload_layer(0, L)
+        want = g.forward(0, synth.make_hidden(world * T, 2048, seed_offset=61))
+    assert rel_l2(got, want) <= REL_L2
+    assert float(np.abs(got - want).max()) <= MAX_ABS
