@@ -50,14 +50,21 @@ struct Workspace {
     void *tiles_dn = nullptr;
     int32_t *n_tiles = nullptr; /* [2] */
     uint32_t max_tiles_gu = 0, max_tiles_dn = 0;
+    /* tcgen05 GEMM path (k_umma.cu): 128-row tile plans, token blocks, pre-gathered tokens */
+    void *utiles_gu = nullptr, *utiles_dn = nullptr, *utbs = nullptr;
+    int32_t *ucounts = nullptr; /* [4]: tiles gu, blocks, tiles dn, blocks */
+    uint8_t *xt = nullptr;
+    uint32_t umax_gu = 0, umax_dn = 0, umax_tb = 0;
 };
 
 }  // namespace
 
 namespace {
-enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D, K_COUNT };
+enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D,
+                K_XT, K_COUNT };
 const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer",
-                                           "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down"};
+                                           "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down",
+                                           "xt_gather"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -87,6 +94,7 @@ struct lfm_gpu_moe {
     bool use_graphs = true;
     bool use_fused = true;   /* fused decode layer for T <= LFM_FUSED_MAX_T */
     bool use_gemm = true;    /* tensor-core grouped GEMMs for prefill-sized T */
+    bool use_umma = true;    /* ... on tcgen05 (k_umma.cu) where rows % 128 == 0, else mma.sync (k_gemm.cu) */
     std::vector<GraphEntry> graphs;
 };
 
@@ -190,6 +198,13 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_tgu = take(lfm_gemm_tile_bytes() * mt_gu);
     const size_t o_tdn = take(lfm_gemm_tile_bytes() * mt_dn);
     const size_t o_nt = take(sizeof(int32_t) * 2);
+    const size_t umax_tb = lfm_umma_tb_max((uint32_t)TK, E);
+    const size_t umax_gu = lfm_umma_tiles_max(I, (uint32_t)TK, E), umax_dn = lfm_umma_tiles_max(D, (uint32_t)TK, E);
+    const size_t o_utgu = take(lfm_umma_tile_bytes() * umax_gu);
+    const size_t o_utdn = take(lfm_umma_tile_bytes() * umax_dn);
+    const size_t o_utbs = take(lfm_umma_tb_bytes() * umax_tb);
+    const size_t o_ucnt = take(sizeof(int32_t) * 4);
+    const size_t o_xt = take(lfm_umma_xt_bytes(umax_tb, (D > I ? D : I) / 256));
     void *base = nullptr;
     /* the old workspace may still be read by queued work on any stream */
     cudaError_t e = cudaDeviceSynchronize();
@@ -233,6 +248,14 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.n_tiles = reinterpret_cast<int32_t *>(b + o_nt);
     w.max_tiles_gu = (uint32_t)mt_gu;
     w.max_tiles_dn = (uint32_t)mt_dn;
+    w.utiles_gu = b + o_utgu;
+    w.utiles_dn = b + o_utdn;
+    w.utbs = b + o_utbs;
+    w.ucounts = reinterpret_cast<int32_t *>(b + o_ucnt);
+    w.xt = b + o_xt;
+    w.umax_gu = (uint32_t)umax_gu;
+    w.umax_dn = (uint32_t)umax_dn;
+    w.umax_tb = (uint32_t)umax_tb;
     return LFM_GPU_OK;
 }
 
@@ -281,7 +304,32 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
     Q8Rows hq = w.hq; hq.cols = L.I;
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
-    if (h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L)) {
+    const bool prefill = h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L);
+    if (prefill && h->use_umma && lfm_umma_ok(L.I) && lfm_umma_ok(L.D)) {
+        const uint32_t TK = T * K;
+        LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
+            cudaError_t e = lfm_launch_umma_plan(w.rt, L.I, w.utiles_gu, w.utbs, w.ucounts, w.umax_gu, w.umax_tb, s);
+            return e == cudaSuccess
+                       ? lfm_launch_umma_plan(w.rt, L.D, w.utiles_dn, w.utbs, w.ucounts + 2, w.umax_dn, w.umax_tb, s)
+                       : e;
+        }));
+        const uint32_t mtb = (uint32_t)lfm_umma_tb_max(TK, lfm_layer_E(L));
+        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
+            return lfm_launch_q4k_umma(L.gate, L.I, L.D, w.xt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_GEMM_U, s, [&] {
+            return lfm_launch_q4k_umma(L.up, L.I, L.D, w.xt, w.utiles_gu, w.utbs, w.ucounts, w.u, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, TK, L.I, hq, s); }));
+        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(hq, nullptr, 1, w.utbs, w.ucounts + 3, mtb, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
+            return lfm_launch_q4k_umma(L.down, L.D, L.I, w.xt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.rt.err, grid, s);
+        }));
+        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
+        return LFM_GPU_OK;
+    }
+    if (prefill) {
         LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
             cudaError_t e = lfm_launch_gemm_plan(w.rt, L.I, w.tiles_gu, w.n_tiles, w.max_tiles_gu, s);
             return e == cudaSuccess ? lfm_launch_gemm_plan(w.rt, L.D, w.tiles_dn, w.n_tiles + 1, w.max_tiles_dn, s) : e;
@@ -352,6 +400,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
         h->use_fused = !(nf && nf[0] && nf[0] != '0');
         const char *ng = getenv("LFM_GPU_MOE_NO_GEMM"); /* force the GEMV path for prefill (A/B runs) */
         h->use_gemm = !(ng && ng[0] && ng[0] != '0');
+        const char *nu = getenv("LFM_GPU_MOE_NO_UMMA"); /* prefill GEMMs on mma.sync instead of tcgen05 (A/B runs) */
+        h->use_umma = !(nu && nu[0] && nu[0] != '0');
     }
     DeviceGuard g(device_id);
     if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess ||

@@ -118,6 +118,21 @@ cudaError_t lfm_launch_q4k_gemm(const uint8_t *W, uint32_t rows, uint32_t cols, 
 cudaError_t lfm_launch_swiglu_quant(const float *G, const float *U, uint32_t rows, uint32_t cols, Q8Rows dst,
                                     cudaStream_t s);
 
+/* k_umma.cu: prefill grouped GEMM on tcgen05 (rows % 128 == 0) */
+bool lfm_umma_ok(uint32_t rows);
+size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts);
+size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);
+size_t lfm_umma_tile_bytes();
+size_t lfm_umma_tb_bytes();
+size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb);
+cudaError_t lfm_launch_umma_plan(const RouteTables &rt, uint32_t rows, void *tiles, void *tbs, int32_t *counts,
+                                 uint32_t max_tiles, uint32_t max_tb, cudaStream_t s);
+cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
+                                 uint32_t max_tb, uint8_t *xt, cudaStream_t s);
+cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t rows, uint32_t cols, const uint8_t *xt, const void *tiles,
+                                const void *tbs, const int32_t *n_tiles, float *Y, uint32_t *err, int grid,
+                                cudaStream_t s);
+
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
 cudaError_t lfm_launch_synth_q4k(uint8_t *out, uint64_t n_blocks, uint64_t seed, float stddev, cudaStream_t s,

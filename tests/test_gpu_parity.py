@@ -191,6 +191,30 @@ def test_prefill_gemm_equals_gemv(monkeypatch, D, E, K, I, T):
     assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("D,E,K,I,T,zipf", [(2048, 32, 4, 1792, 2048, 1.1), (2048, 64, 4, 1536, 1024, None)])
+def test_prefill_tcgen05_equals_mma_sync_and_gemv(monkeypatch, D, E, K, I, T, zipf):
+    """The tcgen05 GEMM (k_umma.cu), the mma.sync GEMM (k_gemm.cu) and the dp4a GEMV
+    form the same exact integer sums and the same fp32 update order: identical outputs."""
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    L = cached_layer(D, E, K, I, layer=4, zipf=zipf)
+    x = synth.make_hidden(T, D, seed_offset=57)
+    outs = []
+    for env in ({}, {"LFM_GPU_MOE_NO_UMMA": "1"}, {"LFM_GPU_MOE_NO_GEMM": "1"}):
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        with GpuMoE(0) as g:
+            g.upload_layer(0, L)
+            g.profile(True)
+            outs.append(g.forward(0, np.array(x, copy=True)))
+            prof = g.profile_read()
+            g.profile(False)
+        if not env:
+            assert "xt_gather" in prof and "gemm_gate" in prof, prof
+    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(outs[0], outs[2])
+
+
 def test_prefill_gemm_path_is_taken_and_dense_matches_oracle(oracle, gpu):
     """A dense layer at T=64 goes through the GEMM path (per-kernel profile) and matches the oracle."""
     from laii_b200 import synth
