@@ -1,28 +1,23 @@
 /*
  * K1 router (+ K2 dispatch) of the lfm2moe MoE-FFN.
  *
- * k_route, grid (ceil(E/4), T), 64 threads: block (bx, t) scores experts
- * 4*bx .. 4*bx+3 for token t.
- *  1. Bulk (TMA) copies bring the block's 4 router rows (32 KB at D=2048) and
- *     ffn_norm into shared memory; they are issued before griddepcontrol.wait,
- *     so they overlap the tail of the kernel that produces x.  Another bulk
- *     copy brings x[t] once that kernel has finished.
- *  2. RMSNorm with the reference's evaluation order: 16 sequential FMA chains
- *     over elements l, l+16, ... then the 8/4/2/1 tree, inv = 1/sqrtf(ss/D+eps),
- *     xb = (x*inv)*w   (tools/lfm2_decode_1x4.c:98-133).
- *  3. Router logits, one expert per half-warp with the same 16-chain order
- *     as lfm2_vec_dot_f32_avx2 (include/lfm2_simd_avx2.h:676-687).
- *  4. The last block of token t (arrival counter; nobody waits) computes
- *     sigmoid, exp_probs_b-biased top-K (ties to the lowest index) and the
- *     normalised unbiased weights (tools/lfm2_moe_checkpoint.c:183-239), and
- *     Q8_K of xb (tools/lfm2_decode_1x4.c:150-186).
- *  5. The last token to finish (second counter) builds the dispatch tables:
- *     per-expert histogram, exclusive scan, slot permutation and its inverse,
- *     the list of active experts and of (expert, 8-token chunk) work pairs.
- * Dense layers skip 3-4 and route every token to expert 0 with weight 1
- * (x + down(x) exactly, tools/lfm2_decode_1x4.c:1086-1103).
- * Only exp() can differ from the reference (see lfm_expf): routing parity
- * allows near-ties.
+ * Evaluation order (the reference's, so Q8_K of x is bit-exact and only exp()
+ * can move a logit by an ulp):
+ *   RMSNorm: 16 sequential FMA chains over elements l, l+16, ... then the
+ *     8/4/2/1 tree, inv = 1/sqrtf(ss/D+eps), xb = (x*inv)*w
+ *     (tools/lfm2_decode_1x4.c:98-133);
+ *   logits: the same 16-chain order as lfm2_vec_dot_f32_avx2
+ *     (include/lfm2_simd_avx2.h:676-687);
+ *   sigmoid, exp_probs_b-biased top-K (ties to the lowest index), normalised
+ *     unbiased weights (tools/lfm2_moe_checkpoint.c:183-239);
+ *   Q8_K of xb (tools/lfm2_decode_1x4.c:150-186).
+ * Two implementations by size:
+ *   T <= 16  k_route_cluster, one thread-block cluster (below);
+ *   T > 16   k_norm_q8 + k_router_tiles + k_dispatch_wide.
+ * Dispatch tables (route_dispatch): per-expert histogram, exclusive scan,
+ * slot permutation and its inverse, the active experts and their (expert,
+ * 8-token chunk) work pairs.  Dense layers route every token to expert 0 with
+ * weight 1 (x + down(x) exactly, tools/lfm2_decode_1x4.c:1086-1103).
  */
 #include <cooperative_groups.h>
 
@@ -33,9 +28,6 @@ namespace cg = cooperative_groups;
 
 namespace {
 
-constexpr int kRouteThreads = 64;
-constexpr int kExpertsPerBlock = 4;
-
 struct RouteSmem {
     uint64_t bar_w, bar_x;
     float inv;
@@ -43,17 +35,27 @@ struct RouteSmem {
     int cnt[LFM_GPU_MAX_EXPERTS_DEV];
     int off[LFM_GPU_MAX_EXPERTS_DEV + 1];
     int cur[LFM_GPU_MAX_EXPERTS_DEV];
+    int act[LFM_GPU_MAX_EXPERTS_DEV]; /* active experts, in id order */
+    int pb[LFM_GPU_MAX_EXPERTS_DEV];  /* first work pair of each active expert */
+    int uniq;
 };
 
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
     const uint32_t n = T * K;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
     __syncthreads();
-    for (uint32_t a = threadIdx.x; a < n; a += blockDim.x) {
-        const int e = __ldcg(rt.idx + a);
-        if ((unsigned)e < E) atomicAdd(&s.cnt[e], 1);
-        else atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
+    /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
+    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
+        const uint32_t a = b0 + threadIdx.x;
+        int e = -1;
+        if (a < n) {
+            e = __ldcg(rt.idx + a);
+            if ((unsigned)e >= E) { atomicOr(rt.err, LFM_DEVERR_EXPERT_ID); e = -1; }
+        }
+        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+        if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -63,14 +65,14 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
             acc += s.cnt[e];
             mx = max(mx, s.cnt[e]);
             if (s.cnt[e] > 0) {
-                rt.act[uniq] = (int)e;
-                const int nch = (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
-                for (int c = 0; c < nch; ++c) rt.pairs[pairs + c] = make_int2(uniq, c);
-                pairs += nch;
+                s.act[uniq] = (int)e;
+                s.pb[uniq] = pairs;
+                pairs += (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
                 ++uniq;
             }
         }
         s.off[E] = acc;
+        s.uniq = uniq;
         rt.summary[0] = uniq;
         rt.summary[1] = mx;
         rt.summary[2] = acc;
@@ -82,13 +84,31 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
         rt.offsets[e] = s.off[e];
         if (e < E) rt.counts[e] = s.cnt[e];
     }
-    for (uint32_t a = threadIdx.x; a < n; a += blockDim.x) {
-        const int e = __ldcg(rt.idx + a);
-        if ((unsigned)e < E) {
-            const int pos = s.off[e] + atomicAdd(&s.cur[e], 1);
+    /* active experts and their (expert, 8-token chunk) work pairs */
+    for (int u = warp; u < s.uniq; u += nwarps) {
+        const int e = s.act[u];
+        if (lane == 0) rt.act[u] = e;
+        const int nch = (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
+        for (int c = lane; c < nch; c += 32) rt.pairs[s.pb[u] + c] = make_int2(u, c);
+    }
+    /* slots: a run of equal ids in a warp takes consecutive slots with one atomic */
+    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
+        const uint32_t a = b0 + threadIdx.x;
+        int e = -1;
+        if (a < n) {
+            e = __ldcg(rt.idx + a);
+            if ((unsigned)e >= E) e = -1;
+        }
+        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+        const int leader = __ffs(m) - 1;
+        int base = 0;
+        if (e >= 0 && lane == leader) base = atomicAdd(&s.cur[e], __popc(m));
+        base = __shfl_sync(LFM_FULL_MASK, base, leader);
+        if (e >= 0) {
+            const int pos = s.off[e] + base + __popc(m & ((1u << lane) - 1u));
             rt.perm[pos] = (int)a;
             rt.inv[a] = pos;
-        } else {
+        } else if (a < n) {
             rt.inv[a] = -1;
         }
     }
@@ -153,107 +173,6 @@ __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &
     }
 }
 
-__global__ void __launch_bounds__(kRouteThreads) k_route(MoeLayerDev L, const float *__restrict__ x, uint32_t T,
-                                                         Q8Rows xq, RouteTables rt) {
-    extern __shared__ __align__(128) uint8_t dsm[];
-    __shared__ RouteSmem s;
-    const uint32_t t = blockIdx.y, D = L.D;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float *xs = reinterpret_cast<float *>(dsm); /* [D] raw x, then xb */
-    float *nw = xs + D;                         /* [D] ffn_norm        */
-    float *ws = nw + D;                         /* [4][D] router rows  */
-    const uint32_t e0 = blockIdx.x * kExpertsPerBlock;
-    const uint32_t ne = L.dense ? 0u : min((uint32_t)kExpertsPerBlock, L.E - e0);
-    const uint32_t w_bytes = (ne + (L.ffn_norm ? 1u : 0u)) * D * 4;
-
-    if (threadIdx.x == 0) {
-        lfm_mbar_init(&s.bar_w, 1);
-        lfm_mbar_init(&s.bar_x, 1);
-        lfm_fence_mbar_init();
-    }
-    __syncthreads();
-    lfm_pdl_launch_dependents();
-    /* constant weights: fetch before waiting on the producer of x */
-    if (threadIdx.x == 0 && w_bytes > 0) {
-        lfm_mbar_arrive_tx(&s.bar_w, w_bytes);
-        if (ne > 0) lfm_bulk_g2s_plain(ws, L.router_w + (size_t)e0 * D, ne * D * 4, &s.bar_w);
-        if (L.ffn_norm) lfm_bulk_g2s_plain(nw, L.ffn_norm, D * 4, &s.bar_w);
-    }
-    lfm_pdl_wait(); /* x is produced by the previous kernel on the stream */
-    if (threadIdx.x == 0) {
-        lfm_mbar_arrive_tx(&s.bar_x, D * 4);
-        lfm_bulk_g2s_plain(xs, x + (size_t)t * D, D * 4, &s.bar_x);
-    }
-    const bool ok_x = lfm_mbar_wait(&s.bar_x, 0, rt.err);
-
-    if (warp == 0) {
-        float acc = 0.0f;
-        if (lane < 16 && ok_x) {
-#pragma unroll 16
-            for (uint32_t i = 0; i < D; i += 16) {
-                const float v = xs[i + lane];
-                acc = __fmaf_rn(v, v, acc);
-            }
-        }
-        const float ss = lfm_hsum16_ref(acc);
-        if (lane == 0) s.inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
-    }
-    const bool ok_w = w_bytes == 0 || lfm_mbar_wait(&s.bar_w, 0, rt.err);
-    __syncthreads();
-    const float inv = s.inv;
-    for (uint32_t i = threadIdx.x; i < D; i += kRouteThreads) {
-        const float n = __fmul_rn(xs[i], inv);
-        xs[i] = L.ffn_norm ? __fmul_rn(n, nw[i]) : n;
-    }
-    __syncthreads();
-
-    if (ne > 0) {
-        const uint32_t el = warp * 2 + (lane >> 4), l16 = lane & 15;
-        float acc = 0.0f;
-        if (el < ne && ok_w) {
-            const float *wr = ws + (size_t)el * D;
-#pragma unroll 16
-            for (uint32_t i = 0; i < D; i += 16) acc = __fmaf_rn(wr[i + l16], xs[i + l16], acc);
-        }
-        const float z = lfm_hsum16_ref(acc);
-        if (l16 == 0 && el < ne) rt.logits[(size_t)t * L.E + e0 + el] = z;
-        __threadfence();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&rt.tok_count[t], 1u);
-        s.last = prev == gridDim.x - 1;
-        if (s.last) rt.tok_count[t] = 0; /* every other block of this token has arrived */
-    }
-    __syncthreads();
-    if (!s.last) return;
-    __threadfence();
-
-    if (L.dense) {
-        if (threadIdx.x == 0) { rt.idx[t] = 0; rt.w[t] = 1.0f; }
-    } else if (warp == 0) {
-        route_topk(L, t, rt, rt.logits + (size_t)t * L.E, true);
-    }
-    const uint32_t nb = D / 256;
-    for (uint32_t b = warp; b < nb; b += kRouteThreads / 32) {
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = xs[256 * b + 8 * lane + i];
-        lfm_quant_block_warp(v, xq, t, b);
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(rt.done, 1u);
-        s.last = prev == T - 1;
-        if (s.last) *rt.done = 0;
-    }
-    __syncthreads();
-    if (!s.last) return;
-    __threadfence();
-    route_dispatch(L, T, rt, s);
-}
-
 /*
  * Decode-size router (T <= 16): one thread-block cluster of C <= 8 CTAs.
  * CTA c scores experts [c*epc, c*epc + epc) for every token (router rows and
@@ -261,7 +180,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(MoeLayerDev L, const fl
  * token's RMSNorm itself, and writes its logits straight into CTA 0's shared
  * memory (distributed shared memory).  One cluster barrier later CTA 0 runs
  * top-K, Q8_K and the dispatch for all tokens: no global atomics or fences on
- * the critical path.  Same evaluation order as k_route.
+ * the critical path.  Same evaluation order as the prefill router.
  */
 constexpr int kClusterThreads = 512;
 constexpr int kClusterMaxT = 16;
@@ -367,6 +286,188 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
     route_dispatch(L, T, rt, s);
 }
 
+/*
+ * Prefill-size router (T > 16): three launches instead of one block per
+ * (token, 4 experts).
+ *  k_norm_q8      one warp per token: the RMSNorm sum of squares (the
+ *                 reference's 16 chains + tree), then Q8_K of xb; 1/rms is kept
+ *                 for the next pass.  Dense layers route every token to expert
+ *                 0 with weight 1 here.
+ *  k_router_tiles a CTA scores TT tokens against every expert from 256-column
+ *                 slices of the router rows and of x (tensor copies, four
+ *                 slices in flight), then takes each token's top-K.
+ *  k_dispatch_wide the dispatch tables from one 1024-thread block.
+ */
+constexpr int kNormWarps = 4;
+
+/* One warp per token: the row lands in shared memory with 16-byte loads issued
+ * together, lanes 0-15 run the sum-of-squares chains over it, then the warp
+ * quantises xb = (x * inv) * ffn_norm one 256-block at a time.  Dynamic shared
+ * memory: kNormWarps * D floats. */
+__global__ void __launch_bounds__(kNormWarps * 32) k_norm_q8(MoeLayerDev L, const float *__restrict__ x, uint32_t T,
+                                                             Q8Rows xq, RouteTables rt) {
+    extern __shared__ __align__(16) float nsm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t t = blockIdx.x * kNormWarps + warp;
+    if (t >= T) return;
+    const uint32_t D = L.D;
+    float *xs = nsm + (size_t)warp * D;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)t * D);
+    for (uint32_t i = lane; i < D / 4; i += 32) reinterpret_cast<float4 *>(xs)[i] = __ldg(xr + i);
+    __syncwarp();
+    float acc = 0.0f;
+    if (lane < 16) {
+#pragma unroll 16
+        for (uint32_t i = 0; i < D; i += 16) {
+            const float v = xs[i + lane];
+            acc = __fmaf_rn(v, v, acc);
+        }
+    }
+    const float ss = lfm_hsum16_ref(acc);
+    const float inv = __shfl_sync(LFM_FULL_MASK, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps))), 0);
+    if (lane == 0) {
+        rt.rms[t] = inv;
+        if (L.dense) { rt.idx[t] = 0; rt.w[t] = 1.0f; }
+    }
+    for (uint32_t b = 0; b < D / 256; ++b) {
+        const float4 p0 = reinterpret_cast<const float4 *>(xs + 256 * b + 8 * lane)[0];
+        const float4 p1 = reinterpret_cast<const float4 *>(xs + 256 * b + 8 * lane)[1];
+        const float xv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        float nw[8] = {1, 1, 1, 1, 1, 1, 1, 1};
+        if (L.ffn_norm) {
+            const float4 w0 = __ldg(reinterpret_cast<const float4 *>(L.ffn_norm + 256 * b + 8 * lane));
+            const float4 w1 = __ldg(reinterpret_cast<const float4 *>(L.ffn_norm + 256 * b + 8 * lane) + 1);
+            nw[0] = w0.x; nw[1] = w0.y; nw[2] = w0.z; nw[3] = w0.w; nw[4] = w1.x; nw[5] = w1.y; nw[6] = w1.z; nw[7] = w1.w;
+        }
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float n = __fmul_rn(xv[i], inv);
+            v[i] = L.ffn_norm ? __fmul_rn(n, nw[i]) : n;
+        }
+        lfm_quant_block_warp(v, xq, t, b);
+    }
+}
+
+constexpr int kRtSlice = 256;   /* columns per slice */
+constexpr int kRtExperts = 32;  /* experts per pass  */
+constexpr int kRtStages = 4;
+
+template <int TT, int TPT>
+struct RouterTile {
+    static constexpr int kW = kRtExperts * kRtSlice * 4;  /* router rows of a slice (tensor copy, zero-filled) */
+    static constexpr int kX = TT * kRtSlice * 4;          /* the tokens' x of a slice (tensor copy)            */
+    static constexpr int kStage = kW + kX + kRtSlice * 4; /* + ffn_norm of the slice                            */
+    static constexpr int kGroups = 16;
+    static constexpr int kTokGroups = TT / TPT;
+    static constexpr int kEpt = kRtExperts / (kGroups / kTokGroups); /* experts per thread per pass */
+};
+
+/* A CTA scores TT tokens against every expert.  Per 256-column slice: the
+ * router rows (box 256 x 32 of router_w, rows past E read as zero) and the
+ * tokens' x (box 256 x TT) arrive by one tensor copy each, ffn_norm by a bulk
+ * copy, kRtStages slices in flight; xb is rebuilt in place from x, 1/rms and
+ * ffn_norm exactly as k_norm_q8 forms it; thread (chain l, group g) advances
+ * chain l of TPT tokens x EPT experts through the slice -- each chain in the
+ * reference's column order -- and after the last slice of a pass the 16-lane
+ * tree gives the logits.  One warp per token then takes the top-K. */
+template <int TT, int TPT>
+__global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CUtensorMap tmw,
+                                                      const __grid_constant__ CUtensorMap tmx, MoeLayerDev L,
+                                                      uint32_t T, RouteTables rt) {
+    using RT = RouterTile<TT, TPT>;
+    constexpr int EPT = RT::kEpt;
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ uint64_t bars[kRtStages];
+    __shared__ float s_inv[TT];
+    const uint32_t D = L.D, E = L.E;
+    const uint32_t tok0 = blockIdx.x * TT;
+    const uint32_t nt = min((uint32_t)TT, T - tok0);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int l = threadIdx.x & 15, g = threadIdx.x >> 4;
+    const int tg = g % RT::kTokGroups, eg = g / RT::kTokGroups;
+    float *lg = reinterpret_cast<float *>(dsm + kRtStages * RT::kStage); /* [TT][E] logits */
+    const uint32_t nsl = D / kRtSlice, npass = (E + kRtExperts - 1) / kRtExperts;
+    const uint32_t nq = nsl * npass;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRtStages; ++i) lfm_mbar_init(&bars[i], 1);
+        lfm_fence_mbar_init();
+    }
+    if (threadIdx.x < TT) s_inv[threadIdx.x] = threadIdx.x < nt ? __ldcg(rt.rms + tok0 + threadIdx.x) : 0.0f;
+    __syncthreads();
+    auto issue = [&](uint32_t q) {
+        const uint32_t p = q / nsl, sl = q % nsl;
+        uint8_t *st = dsm + (q % kRtStages) * RT::kStage;
+        uint64_t *bar = &bars[q % kRtStages];
+        lfm_mbar_arrive_tx(bar, RT::kW + RT::kX + (L.ffn_norm ? kRtSlice * 4 : 0));
+        lfm_tma_load_2d(st, &tmw, sl * kRtSlice, p * kRtExperts, bar);
+        lfm_tma_load_2d(st + RT::kW, &tmx, sl * kRtSlice, tok0, bar);
+        if (L.ffn_norm) lfm_bulk_g2s_plain(st + RT::kW + RT::kX, L.ffn_norm + sl * kRtSlice, kRtSlice * 4, bar);
+    };
+    if (threadIdx.x == 0)
+        for (uint32_t q = 0; q < nq && q < kRtStages - 1; ++q) issue(q);
+    float acc[TPT][EPT];
+    bool ok = true;
+    for (uint32_t q = 0; q < nq; ++q) {
+        const uint32_t p = q / nsl, sl = q % nsl;
+        if (sl == 0) {
+#pragma unroll
+            for (int j = 0; j < TPT; ++j)
+#pragma unroll
+                for (int k = 0; k < EPT; ++k) acc[j][k] = 0.0f;
+        }
+        /* stage (q + 3) % 4 was last read in iteration q - 1, which every thread has left */
+        if (threadIdx.x == 0 && q + kRtStages - 1 < nq) issue(q + kRtStages - 1);
+        ok = ok && lfm_mbar_wait(&bars[q % kRtStages], (q / kRtStages) & 1u, rt.err);
+        float *st = reinterpret_cast<float *>(dsm + (q % kRtStages) * RT::kStage);
+        const float *ws = st;
+        float *xs = st + kRtExperts * kRtSlice;
+        const float *nw = xs + TT * kRtSlice;
+        for (uint32_t i = threadIdx.x; i < nt * kRtSlice; i += blockDim.x) {
+            const uint32_t t = i / kRtSlice, c = i % kRtSlice;
+            const float n = __fmul_rn(xs[i], s_inv[t]);
+            xs[i] = L.ffn_norm ? __fmul_rn(n, nw[c]) : n;
+        }
+        __syncthreads();
+        if (ok) {
+#pragma unroll 4
+            for (int c = 0; c < kRtSlice / 16; ++c) {
+                const int i = 16 * c + l;
+                float xv[TPT];
+#pragma unroll
+                for (int j = 0; j < TPT; ++j) xv[j] = xs[(tg * TPT + j) * kRtSlice + i];
+#pragma unroll
+                for (int k = 0; k < EPT; ++k) {
+                    const float wv = ws[(eg * EPT + k) * kRtSlice + i];
+#pragma unroll
+                    for (int j = 0; j < TPT; ++j) acc[j][k] = __fmaf_rn(wv, xv[j], acc[j][k]);
+                }
+            }
+        }
+        if (sl == nsl - 1) {
+#pragma unroll
+            for (int j = 0; j < TPT; ++j)
+#pragma unroll
+                for (int k = 0; k < EPT; ++k) {
+                    const float z = lfm_hsum16_ref(acc[j][k]);
+                    const uint32_t t = tg * TPT + j, e = p * kRtExperts + eg * EPT + k;
+                    if (l == 0 && e < E) lg[t * E + e] = z;
+                }
+        }
+        __syncthreads();
+    }
+    if (!ok) return;
+    for (uint32_t t = warp; t < nt; t += blockDim.x / 32) {
+        for (uint32_t e = lane; e < E; e += 32) rt.logits[(size_t)(tok0 + t) * E + e] = lg[t * E + e];
+        route_topk(L, tok0 + t, rt, lg + t * E, false);
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt) {
+    __shared__ RouteSmem s;
+    route_dispatch(L, T, rt, s);
+}
+
 /* Dispatch tables alone, for rows whose experts are given (expert parallelism). */
 __global__ void __launch_bounds__(256) k_dispatch_only(MoeLayerDev L, uint32_t T, RouteTables rt) {
     __shared__ RouteSmem s;
@@ -381,7 +482,42 @@ cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTab
     return cudaGetLastError();
 }
 
-size_t lfm_route_smem(uint32_t D) { return sizeof(float) * D * (2 + kExpertsPerBlock); }
+template <int TT, int TPT>
+static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uint32_t T, const RouteTables &rt,
+                                       cudaStream_t s) {
+    using RT = RouterTile<TT, TPT>;
+    CUtensorMap tmw, tmx;
+    if (!lfm_tmap_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.router_w, L.D, L.E, (uint64_t)L.D * 4, kRtSlice,
+                     kRtExperts) ||
+        !lfm_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, L.D, T, (uint64_t)L.D * 4, kRtSlice, TT))
+        return cudaErrorInvalidValue;
+    const size_t smem = kRtStages * RT::kStage + sizeof(float) * TT * L.E;
+    static size_t cache[16];
+    cudaError_t e = lfm_smem_attr((const void *)k_router_tiles<TT, TPT>, smem, cache);
+    if (e != cudaSuccess) return e;
+    k_router_tiles<TT, TPT><<<(T + TT - 1) / TT, 256, smem, s>>>(tmw, tmx, L, T, rt);
+    return cudaGetLastError();
+}
+
+/* T > 16: normalise + quantise, score (all experts per CTA), dispatch. */
+static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
+                                        const RouteTables &rt, cudaStream_t s) {
+    const size_t nsmem = sizeof(float) * kNormWarps * L.D;
+    static size_t cache[16];
+    cudaError_t e = lfm_smem_attr((const void *)k_norm_q8, nsmem, cache);
+    if (e != cudaSuccess) return e;
+    k_norm_q8<<<(T + kNormWarps - 1) / kNormWarps, kNormWarps * 32, nsmem, s>>>(L, x, T, xq, rt);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (!L.dense) {
+        if (T >= 1024) e = launch_router_tiles<16, 2>(L, x, T, rt, s);
+        else if (T >= 256) e = launch_router_tiles<8, 1>(L, x, T, rt, s);
+        else e = launch_router_tiles<4, 1>(L, x, T, rt, s);
+        if (e != cudaSuccess) return e;
+    }
+    k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt);
+    return cudaGetLastError();
+}
 
 /* Shared memory of the cluster router, or 0 when (T, D, E) does not fit it. */
 static size_t route_cluster_smem(const MoeLayerDev &L, uint32_t T, uint32_t *epc_out) {
@@ -419,20 +555,5 @@ cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q
         cfg.numAttrs = 2;
         return cudaLaunchKernelEx(&cfg, k_route_cluster, L, x, T, epc, xq, rt);
     }
-    const uint32_t gx = L.dense ? 1u : (L.E + kExpertsPerBlock - 1) / kExpertsPerBlock;
-    static size_t cache[16];
-    const size_t smem = lfm_route_smem(L.D);
-    cudaError_t e = lfm_smem_attr((const void *)k_route, smem, cache);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(gx, T);
-    cfg.blockDim = dim3(kRouteThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_route, L, x, T, xq, rt);
+    return launch_route_prefill(L, x, T, xq, rt, s);
 }

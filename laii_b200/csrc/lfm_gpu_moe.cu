@@ -186,6 +186,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_pairs = take(sizeof(int2) * n_pairs);
     const size_t o_sum = take(sizeof(int32_t) * 4);
     const size_t o_log = take(sizeof(float) * T * E);
+    const size_t o_rms = take(sizeof(float) * T);
     const size_t o_h = take(sizeof(float) * TK * I);
     const size_t o_hq = take(TK * I);
     const size_t o_hd = take(sizeof(float) * TK * (I / 256));
@@ -198,13 +199,16 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_tgu = take(lfm_gemm_tile_bytes() * mt_gu);
     const size_t o_tdn = take(lfm_gemm_tile_bytes() * mt_dn);
     const size_t o_nt = take(sizeof(int32_t) * 2);
-    const size_t umax_tb = lfm_umma_tb_max((uint32_t)TK, E);
-    const size_t umax_gu = lfm_umma_tiles_max(I, (uint32_t)TK, E), umax_dn = lfm_umma_tiles_max(D, (uint32_t)TK, E);
+    /* tcgen05 GEMM scratch for the smallest token block (the most blocks) and the largest (the most bytes) */
+    const size_t umax_tb = lfm_umma_tb_max((uint32_t)TK, E, 16);
+    const size_t umax_gu = lfm_umma_tiles_max(I, (uint32_t)TK, E, 16), umax_dn = lfm_umma_tiles_max(D, (uint32_t)TK, E, 16);
+    const uint32_t nbx = (D > I ? D : I) / 256;
+    const size_t xt16 = lfm_umma_xt_bytes(umax_tb, nbx, 16), xt128 = lfm_umma_xt_bytes(lfm_umma_tb_max((uint32_t)TK, E, 128), nbx, 128);
     const size_t o_utgu = take(lfm_umma_tile_bytes() * umax_gu);
     const size_t o_utdn = take(lfm_umma_tile_bytes() * umax_dn);
     const size_t o_utbs = take(lfm_umma_tb_bytes() * umax_tb);
     const size_t o_ucnt = take(sizeof(int32_t) * 4);
-    const size_t o_xt = take(lfm_umma_xt_bytes(umax_tb, (D > I ? D : I) / 256));
+    const size_t o_xt = take(xt16 > xt128 ? xt16 : xt128);
     void *base = nullptr;
     /* the old workspace may still be read by queued work on any stream */
     cudaError_t e = cudaDeviceSynchronize();
@@ -233,6 +237,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
     w.rt.done = reinterpret_cast<uint32_t *>(b + o_done);
     w.rt.logits = reinterpret_cast<float *>(b + o_log);
+    w.rt.rms = reinterpret_cast<float *>(b + o_rms);
     w.rt.err = h->dev_err;
     w.rt.loads = h->loads;
     w.h = reinterpret_cast<float *>(b + o_h);
@@ -296,8 +301,9 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
 }
 
 /* Everything after routing: gate|up + SwiGLU, Q8_K(h), down, combine into x.
- * Prefill-sized loads (T > 16 and >= 32 slots per expert on average) take the
- * tensor-core grouped GEMMs (k_gemm.cu), smaller ones the grouped GEMVs. */
+ * T > 16: grouped GEMMs on the tensor cores -- tcgen05 (k_umma.cu, token
+ * blocks sized to the tokens per expert) where rows % 128 == 0, else mma.sync
+ * (k_gemm.cu) for prefill-sized loads; otherwise the grouped GEMVs. */
 lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, uint32_t T, Q8Rows xq,
                              cudaStream_t s, bool pdl) {
     Workspace &w = h->ws;
@@ -305,26 +311,27 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
     const bool prefill = h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L);
-    if (prefill && h->use_umma && lfm_umma_ok(L.I) && lfm_umma_ok(L.D)) {
-        const uint32_t TK = T * K;
+    if (h->use_gemm && h->use_umma && T > LFM_FUSED_MAX_T && lfm_umma_ok(L.I) && lfm_umma_ok(L.D)) {
+        const uint32_t TK = T * K, E = lfm_layer_E(L);
+        const uint32_t nt = lfm_umma_nt(TK, E);
+        const uint32_t mtb = (uint32_t)lfm_umma_tb_max(TK, E, nt);
+        const uint32_t mgu = (uint32_t)lfm_umma_tiles_max(L.I, TK, E, nt), mdn = (uint32_t)lfm_umma_tiles_max(L.D, TK, E, nt);
         LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
-            cudaError_t e = lfm_launch_umma_plan(w.rt, L.I, w.utiles_gu, w.utbs, w.ucounts, w.umax_gu, w.umax_tb, s);
-            return e == cudaSuccess
-                       ? lfm_launch_umma_plan(w.rt, L.D, w.utiles_dn, w.utbs, w.ucounts + 2, w.umax_dn, w.umax_tb, s)
-                       : e;
+            cudaError_t e = lfm_launch_umma_plan(w.rt, L.I, nt, w.utiles_gu, w.utbs, w.ucounts, mgu, mtb, s);
+            return e == cudaSuccess ? lfm_launch_umma_plan(w.rt, L.D, nt, w.utiles_dn, w.utbs, w.ucounts + 2, mdn, mtb, s)
+                                    : e;
         }));
-        const uint32_t mtb = (uint32_t)lfm_umma_tb_max(TK, lfm_layer_E(L));
-        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
-            return lfm_launch_q4k_umma(L.gate, L.I, L.D, w.xt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.rt.err, grid, s);
+            return lfm_launch_q4k_umma(L.gate, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_GEMM_U, s, [&] {
-            return lfm_launch_q4k_umma(L.up, L.I, L.D, w.xt, w.utiles_gu, w.utbs, w.ucounts, w.u, w.rt.err, grid, s);
+            return lfm_launch_q4k_umma(L.up, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.u, w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, TK, L.I, hq, s); }));
-        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(hq, nullptr, 1, w.utbs, w.ucounts + 3, mtb, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(hq, nullptr, 1, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
-            return lfm_launch_q4k_umma(L.down, L.D, L.I, w.xt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.rt.err, grid, s);
+            return lfm_launch_q4k_umma(L.down, E, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
         return LFM_GPU_OK;
@@ -893,7 +900,8 @@ static size_t noalloc_layout(uint32_t T, const MoeLayerDev &L, uint8_t *b, Works
                  o_cnt = take(sizeof(int32_t) * E), o_off = take(sizeof(int32_t) * (E + 1)),
                  o_perm = take(sizeof(int32_t) * TK), o_inv = take(sizeof(int32_t) * TK),
                  o_act = take(sizeof(int32_t) * E), o_pairs = take(sizeof(int2) * n_pairs),
-                 o_sum = take(sizeof(int32_t) * 4), o_log = take(sizeof(float) * T * E);
+                 o_sum = take(sizeof(int32_t) * 4), o_log = take(sizeof(float) * T * E),
+                 o_rms = take(sizeof(float) * T);
     const size_t o_h = take(sizeof(float) * TK * I), o_hq = take(TK * I), o_hd = take(sizeof(float) * TK * (I / 256)),
                  o_hb = take(sizeof(int16_t) * TK * (I / 256) * 16), o_y = take(sizeof(float) * TK * D);
     if (!b) return off;
@@ -914,6 +922,7 @@ static size_t noalloc_layout(uint32_t T, const MoeLayerDev &L, uint8_t *b, Works
     w->rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
     w->rt.done = reinterpret_cast<uint32_t *>(b + o_done);
     w->rt.logits = reinterpret_cast<float *>(b + o_log);
+    w->rt.rms = reinterpret_cast<float *>(b + o_rms);
     w->h = reinterpret_cast<float *>(b + o_h);
     w->hq = Q8Rows{reinterpret_cast<int8_t *>(b + o_hq), reinterpret_cast<float *>(b + o_hd),
                    reinterpret_cast<int16_t *>(b + o_hb), L.I};

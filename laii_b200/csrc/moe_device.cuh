@@ -129,6 +129,18 @@ __device__ __forceinline__ void lfm_bulk_g2s_plain(void *dst, const void *src, u
                  : "memory");
 }
 
+/* 2-D tiled tensor copy (no multicast) of the box at element coordinates
+ * (x, y) into shared memory, completing on `bar`; x * element size must be a
+ * multiple of 16 bytes. */
+__device__ __forceinline__ void lfm_tma_load_2d(void *dst, const CUtensorMap *tm, uint32_t x, uint32_t y,
+                                                uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            lfm_smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(lfm_smem_u32(bar))
+        : "memory");
+}
+
 /* Bulk prefetch of global memory into L2 (bytes % 16 == 0, 16-byte aligned). */
 __device__ __forceinline__ void lfm_prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

@@ -13,6 +13,7 @@
 #ifndef LFM_MOE_INTERNAL_H
 #define LFM_MOE_INTERNAL_H
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -51,6 +52,7 @@ struct RouteTables {
     uint32_t *tok_count; /* [T]   per-token router-block arrival counters (kept at 0)     */
     uint32_t *done;      /* [1]   routed-token counter (kept at 0)                        */
     float *logits;       /* [T*E] router logits                                          */
+    float *rms;          /* [T]   1/rms of x (the prefill router's two passes)            */
     uint32_t *err;       /* device error word                                            */
     unsigned long long *loads; /* [2] running sum of unique experts, MoE layer runs      */
 };
@@ -75,7 +77,6 @@ __host__ __device__ inline uint32_t lfm_layer_K(const MoeLayerDev &L) { return L
 cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16);
 
 /* k_route.cu */
-size_t lfm_route_smem(uint32_t D);
 /* dispatch tables only, from rt.idx already filled (one block) */
 cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
@@ -118,20 +119,28 @@ cudaError_t lfm_launch_q4k_gemm(const uint8_t *W, uint32_t rows, uint32_t cols, 
 cudaError_t lfm_launch_swiglu_quant(const float *G, const float *U, uint32_t rows, uint32_t cols, Q8Rows dst,
                                     cudaStream_t s);
 
-/* k_umma.cu: prefill grouped GEMM on tcgen05 (rows % 128 == 0) */
+/* 2-D tiled tensor map (no swizzle, no interleave, zero fill) over a row-major
+ * matrix [outer][inner] of elem_bytes elements with rows row_bytes apart, box
+ * box_inner x box_outer; false when the driver refuses it (k_umma.cu). */
+bool lfm_tmap_2d(CUtensorMap *tm, CUtensorMapDataType type, uint32_t elem_bytes, const void *base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
+/* k_umma.cu: grouped GEMM on tcgen05 (rows % 128 == 0), nt tokens per block (16..128) */
 bool lfm_umma_ok(uint32_t rows);
-size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts);
-size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);
+uint32_t lfm_umma_nt(uint32_t slots, uint32_t experts);
+size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts, uint32_t nt);
+size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint32_t nt);
 size_t lfm_umma_tile_bytes();
 size_t lfm_umma_tb_bytes();
-size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb);
-cudaError_t lfm_launch_umma_plan(const RouteTables &rt, uint32_t rows, void *tiles, void *tbs, int32_t *counts,
-                                 uint32_t max_tiles, uint32_t max_tb, cudaStream_t s);
+size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt);
+cudaError_t lfm_launch_umma_plan(const RouteTables &rt, uint32_t rows, uint32_t nt, void *tiles, void *tbs,
+                                 int32_t *counts, uint32_t max_tiles, uint32_t max_tb, cudaStream_t s);
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
-                                 uint32_t max_tb, uint8_t *xt, cudaStream_t s);
-cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t rows, uint32_t cols, const uint8_t *xt, const void *tiles,
-                                const void *tbs, const int32_t *n_tiles, float *Y, uint32_t *err, int grid,
-                                cudaStream_t s);
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+/* W: `experts` tensors [rows][cols/256] Q4_K back to back */
+cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t experts, uint32_t rows, uint32_t cols, const uint8_t *xt,
+                                uint32_t nt, const void *tiles, const void *tbs, const int32_t *n_tiles, float *Y,
+                                uint32_t *err, int grid, cudaStream_t s);
 
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */

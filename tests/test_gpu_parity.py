@@ -191,10 +191,14 @@ def test_prefill_gemm_equals_gemv(monkeypatch, D, E, K, I, T):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("D,E,K,I,T,zipf", [(2048, 32, 4, 1792, 2048, 1.1), (2048, 64, 4, 1536, 1024, None)])
+@pytest.mark.parametrize("D,E,K,I,T,zipf", [(2048, 32, 4, 1792, 2048, 1.1), (2048, 64, 4, 1536, 1024, None),
+                                             (2048, 32, 4, 1792, 64, None), (2048, 32, 4, 1792, 24, None),
+                                             (2048, 32, 4, 1792, 200, None)])
 def test_prefill_tcgen05_equals_mma_sync_and_gemv(monkeypatch, D, E, K, I, T, zipf):
-    """The tcgen05 GEMM (k_umma.cu), the mma.sync GEMM (k_gemm.cu) and the dp4a GEMV
-    form the same exact integer sums and the same fp32 update order: identical outputs."""
+    """The tcgen05 GEMM (k_umma.cu: A from shared memory for large token blocks,
+    from tensor memory for small ones), the mma.sync GEMM (k_gemm.cu) and the
+    dp4a GEMV form the same exact integer sums and the same fp32 update order:
+    identical outputs."""
     from laii_b200 import synth
     from laii_b200.moe import GpuMoE
     L = cached_layer(D, E, K, I, layer=4, zipf=zipf)
