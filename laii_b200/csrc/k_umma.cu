@@ -57,40 +57,46 @@ constexpr int kTokInfo = kN * 4 + kN * 16;   /* d8[nt] fp32 + sub-block bsum pai
 __host__ __device__ constexpr uint32_t xt_sb_bytes(uint32_t nt) { return nt * (2 * kHalf + 20); }
 constexpr int kRaw = LFM_Q4K_BYTES;
 constexpr int kRawSlot = kM * kRaw;
-constexpr int kRowInfo = kM * 16;            /* d, dmin, m0..3, m4..7 per row              */
-constexpr int kSA = 3;                       /* A1/A2 and B stages                         */
+constexpr uint32_t kSI = 4;                  /* super-blocks of row/token scales in flight */
+constexpr uint32_t kCtaTiles = 96;           /* tiles of a CTA kept in shared memory       */
+constexpr int kMaxSB = 16;                   /* most B (token) stages                      */
 constexpr uint32_t kTmemCols = 512;
 
 /* Two arrangements of the same pipeline.
- *  prefill (kTs = false, nt > 64): A1/A2 expanded into shared memory (SS MMA);
- *    8 epilogue warps (two per TMEM lane quarter, half of the tokens each), 4
- *    producer warps (one row each, both halves of a super-block); TMEM holds
- *    D1/D2 for nt <= 128 tokens, double buffered (4 x 128 columns).
- *  decode (kTs = true, nt <= 64): A1/A2 expanded into tensor memory with
- *    tcgen05.st (A-from-TMEM MMA), which spares shared memory the expanded
- *    rows -- at few tokens per expert that traffic, not the tensor core, is
- *    the limit; 4 epilogue warps, 8 producer warps (one row each, one half of
- *    the super-block), a deeper raw-weight ring.  TMEM: D1/D2 for nt <= 64
- *    double buffered (columns 0-255), then 3 stages of A1|A2 (64 columns each). */
-template <bool kTs>
+ *  prefill (kDec = false, nt > 32): A1 = b*q4 and A2 = a*q4 in shared memory,
+ *    acc = D1 + 16*D2 accumulated over the super-block by the tensor core
+ *    (16 MMAs a super-block); 8 epilogue warps (two per TMEM lane quarter,
+ *    half of the tokens each), 4 producer warps (one row each, both halves of
+ *    a super-block); TMEM: D1/D2 for nt <= 128, double buffered.
+ *  decode (kDec = true, nt <= 32): A = the raw nibbles as bytes and one
+ *    accumulator per sub-block, D_j = q4 . q8 over its 32 K, so a super-block
+ *    takes 8 MMAs; the epilogue forms acc = sum_j sc_j * D_j (exact).  At few
+ *    tokens per expert a tcgen05.mma costs about the same whatever N, so the
+ *    instruction count, not the arithmetic, sets the pace.  4 epilogue warps,
+ *    8 producer warps (one row each, one half of every super-block), a deeper
+ *    raw-weight ring; TMEM: 8 accumulators x 32 columns, double buffered. */
+template <bool kDec>
 struct UCfg {
-    static constexpr int kEpi = kTs ? 4 : 8;
-    static constexpr int kProd = kTs ? 8 : 4;
-    static constexpr int kSR = kTs ? 8 : 3;
-    static constexpr int kWarpMma = kEpi + kProd;
-    static constexpr int kWarpLoad = kWarpMma + 1;
+    static constexpr int kEpi = kDec ? 4 : 8;
+    static constexpr int kProd = kDec ? 8 : 4;
+    static constexpr int kSR = kDec ? 5 : 3;                   /* raw weight ring (super-blocks)      */
+    static constexpr int kSA = kDec ? 4 : 3;  /* A stages: decode 2 per half super-block, prefill 3 shared */
+    static constexpr int kAStage = kDec ? kOp : 2 * kOp;       /* A, or A1|A2                         */
+    static constexpr int kBBytes = kDec ? 32 * 1024 : 48 * 1024; /* B ring: as many nt-token stages as fit */
+    static constexpr int kRowInfo = kM * (kDec ? 32 : 16);    /* d, dmin, m0..3, m4..7 (, sc0..3, sc4..7) */
+    static constexpr int kWarpMma = kEpi + kProd;  /* two MMA-issuing warps: kWarpMma, kWarpMma + 1 */
+    static constexpr int kWarpLoad = kWarpMma + 2;
     static constexpr int kThreads = (kWarpLoad + 1) * 32;
     static constexpr int kOffA = 0;
-    static constexpr int kOffB = kOffA + (kTs ? 0 : kSA * 2 * kOp);
-    static constexpr int kOffR = kOffB + kSA * kOp;
+    static constexpr int kOffB = kOffA + kSA * kAStage;
+    static constexpr int kOffR = kOffB + kBBytes;
     static constexpr int kOffT = kOffR + kSR * kRawSlot;
-    static constexpr int kOffW = kOffT + 2 * kTokInfo;
-    static constexpr int kSmem = kOffW + 2 * kRowInfo;
-    static constexpr uint32_t kDbuf = kTs ? 128u : 256u; /* TMEM columns of one D1|D2 buffer */
-    static constexpr uint32_t kD2 = kTs ? 64u : 128u;    /* D2 after D1                      */
-    static constexpr uint32_t kA0 = 256u;                /* first A stage (decode)           */
+    static constexpr int kOffW = kOffT + kSI * kTokInfo;
+    static constexpr int kSmem = kOffW + kSI * kRowInfo;
+    static constexpr uint32_t kDbuf = 256u;             /* TMEM columns of one accumulator buffer   */
+    static constexpr uint32_t kDstep = kDec ? 32u : 128u; /* D_j (decode) / D2 (prefill) column step */
 };
-constexpr uint32_t kNtDecode = 64; /* largest token block of the decode arrangement */
+constexpr uint32_t kNtDecode = 32; /* largest token block of the decode arrangement */
 static_assert(UCfg<false>::kSmem <= 227 * 1024 && UCfg<true>::kSmem <= 227 * 1024, "shared memory");
 static_assert(UCfg<false>::kThreads == UCfg<true>::kThreads, "one block size");
 constexpr int kThreads = UCfg<false>::kThreads;
@@ -111,6 +117,7 @@ struct UmmaArgs {
     uint32_t rows, nb;
     const uint8_t *xt;    /* pre-gathered tokens [block][nb][xt_sb_bytes(nt)] */
     uint32_t nt;          /* tokens per block (MMA N): a multiple of 16, <= 128 */
+    uint32_t nsb;         /* B stages of nt * 128 bytes in the B ring (<= kMaxSB) */
     const UTile *tiles;
     const UTokBlock *tbs;
     const int32_t *n_tiles;
@@ -119,8 +126,8 @@ struct UmmaArgs {
 };
 
 struct UmmaBars {
-    uint64_t a_full[kSA], a_empty[kSA], b_full[kSA], b_empty[kSA], r_full[8], r_empty[8];
-    uint64_t t_full[2], t_empty[2], ti_full[2], ri_full[2], i_empty[2];
+    uint64_t a_full[4], a_empty[4], b_full[kMaxSB], b_empty[kMaxSB], r_full[8], r_empty[8];
+    uint64_t t_full[2], t_empty[2], ti_full[kSI], ri_full[kSI], i_empty[kSI];
     uint32_t tmem;
     int abort;
 };
@@ -177,26 +184,33 @@ __device__ __forceinline__ void tmem_wait(uint32_t (&a)[8], uint32_t (&b)[8]) {
                    "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])::"memory");
 }
 
-/* 32 consecutive 32-bit columns of this thread's TMEM lane from registers. */
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
+/* Tie registers to a completed tcgen05.wait::ld so no use is scheduled before it. */
+__device__ __forceinline__ void tmem_tie(uint32_t (&a)[8]) {
+    asm volatile("" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7])::"memory");
 }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-/* A from tensor memory: tcgen05.mma with the A operand's TMEM address. */
-__device__ __forceinline__ void umma_i8_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d),
-        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
+/* Two fp32 lanes at once (fma/mul .rn.ftz .f32x2): the same IEEE operations
+ * as the scalar forms, lane by lane. */
+__device__ __forceinline__ uint64_t pk2(float x, float y) {
+    return (uint64_t)__float_as_uint(x) | ((uint64_t)__float_as_uint(y) << 32);
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+/* mins = sum_j m_j * bsum_j from the token's sub-block sums (pairs) and the row's m bytes. */
+__device__ __forceinline__ int mins_of(const uint4 bp, uint32_t mA, uint32_t mB) {
+    int m = __dp2a_lo((int)bp.x, (int)mA, 0);
+    m = __dp2a_hi((int)bp.y, (int)mA, m);
+    m = __dp2a_lo((int)bp.z, (int)mB, m);
+    return __dp2a_hi((int)bp.w, (int)mB, m);
 }
 
 __device__ __forceinline__ void sts128(uint8_t *p, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
@@ -219,26 +233,33 @@ __device__ __forceinline__ bool uwait(uint64_t *bar, uint32_t parity, volatile i
     return true;
 }
 
-template <bool kTs>
+template <bool kDec>
 __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw, UmmaArgs A) {
-    using C = UCfg<kTs>;
+    using C = UCfg<kDec>;
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ UmmaBars bars;
+    __shared__ UTile s_tile[kCtaTiles];    /* this CTA's tiles, in walking order */
+    __shared__ UTokBlock s_blk[kCtaTiles]; /* and their token blocks           */
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < kSA; ++i) {
+        /* decode: each half super-block feeds one MMA stream; prefill: both streams read every stage */
+        for (int i = 0; i < C::kSA; ++i) {
             lfm_mbar_init(&bars.a_full[i], kM); /* one arrival per row of the half super-block */
-            lfm_mbar_init(&bars.a_empty[i], 1);
+            lfm_mbar_init(&bars.a_empty[i], kDec ? 1 : 2);
+        }
+        for (uint32_t i = 0; i < A.nsb; ++i) {
             lfm_mbar_init(&bars.b_full[i], 1);
-            lfm_mbar_init(&bars.b_empty[i], 1);
+            lfm_mbar_init(&bars.b_empty[i], kDec ? 1 : 2);
         }
         for (int i = 0; i < C::kSR; ++i) {
             lfm_mbar_init(&bars.r_full[i], 1);
             lfm_mbar_init(&bars.r_empty[i], C::kProd * 32);
         }
         for (int i = 0; i < 2; ++i) {
-            lfm_mbar_init(&bars.t_full[i], 1);
+            lfm_mbar_init(&bars.t_full[i], 2); /* one commit from each MMA stream */
             lfm_mbar_init(&bars.t_empty[i], C::kEpi);
+        }
+        for (uint32_t i = 0; i < kSI; ++i) {
             lfm_mbar_init(&bars.ti_full[i], 1);
             lfm_mbar_init(&bars.ri_full[i], kM);
             lfm_mbar_init(&bars.i_empty[i], C::kEpi);
@@ -251,19 +272,58 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
         tmem_relinquish();
         tc_fence_before();
     }
+    const int n_tiles = __ldcg(A.n_tiles);
+    const uint32_t my_tiles =
+        (int)blockIdx.x < n_tiles ? (uint32_t)(n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / gridDim.x : 0u;
+    /* the tile list off the critical path: a dependent global load per super-block would serialise the issue */
+    for (uint32_t it = tid; it < my_tiles && it < kCtaTiles; it += blockDim.x) {
+        const UTile t = A.tiles[blockIdx.x + it * gridDim.x];
+        s_tile[it] = t;
+        s_blk[it] = A.tbs[t.tb];
+    }
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars.tmem;
     volatile int *abort = &bars.abort;
-    const int n_tiles = __ldcg(A.n_tiles);
-    const uint32_t my_tiles =
-        (int)blockIdx.x < n_tiles ? (uint32_t)(n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / gridDim.x : 0u;
     const uint32_t nb = A.nb;
     const uint32_t G = my_tiles * nb; /* super-blocks this CTA walks, tile-major */
+    auto tile_at = [&](uint32_t it) -> UTile {
+        return it < kCtaTiles ? s_tile[it] : A.tiles[blockIdx.x + it * gridDim.x];
+    };
+    /* Stage slot and phase parity of half h of super-block g; true on a slot's first use.
+     * prefill: one ring in half-super-block order (both MMA streams read every stage);
+     * decode: one ring per half, so each MMA stream waits on its own barriers in order. */
+    auto aslot = [&](uint32_t g, uint32_t h, uint32_t &idx, uint32_t &par) -> bool {
+        if constexpr (kDec) {
+            constexpr uint32_t n = C::kSA / 2;
+            idx = h * n + g % n;
+            par = (g / n) & 1u;
+            return g < n;
+        } else {
+            const uint32_t q = 2 * g + h;
+            idx = q % C::kSA;
+            par = (q / C::kSA) & 1u;
+            return q < (uint32_t)C::kSA;
+        }
+    };
+    auto bslot = [&](uint32_t g, uint32_t h, uint32_t &idx, uint32_t &par) -> bool {
+        if constexpr (kDec) {
+            const uint32_t n = A.nsb / 2;
+            idx = h * n + g % n;
+            par = (g / n) & 1u;
+            return g < n;
+        } else {
+            const uint32_t q = 2 * g + h;
+            idx = q % A.nsb;
+            par = (q / A.nsb) & 1u;
+            return q < A.nsb;
+        }
+    };
     uint8_t *sA = sm + C::kOffA, *sB = sm + C::kOffB, *sR = sm + C::kOffR, *sT = sm + C::kOffT, *sW = sm + C::kOffW;
 
     if (warp < C::kEpi) {
         /* ---------------- epilogue ---------------- */
+        constexpr int kCols = kDec ? (int)kNtDecode : kN / 2; /* most columns of one warp */
         const int q4 = warp & 3, ch = warp >> 2;
         const int r = 32 * q4 + lane;
         const int half = (int)A.nt / (C::kEpi / 4); /* columns of this warp: [ch * half, ch * half + half) */
@@ -271,59 +331,85 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
         uint32_t g = 0;
         bool ok = true;
         for (uint32_t it = 0; it < my_tiles && ok; ++it) {
-            const UTile tile = A.tiles[blockIdx.x + it * gridDim.x];
-            const UTokBlock blk = A.tbs[tile.tb];
+            const UTile tile = tile_at(it);
+            const UTokBlock blk = it < kCtaTiles ? s_blk[it] : A.tbs[tile.tb];
             const int nv = min(blk.ntok - ch * half, half); /* valid tokens in this warp's columns */
-            float S[64];
+            float S[kCols];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) S[i] = 0.0f;
+            for (int i = 0; i < kCols; ++i) S[i] = 0.0f;
             for (uint32_t sb = 0; sb < nb; ++sb, ++g) {
                 const uint32_t buf = g & 1u, ph = (g >> 1) & 1u;
                 /* every decision that leaves a loop is warp-uniform: tcgen05.ld is .sync.aligned */
                 ok = __all_sync(LFM_FULL_MASK, uwait(&bars.t_full[buf], ph, abort, A.err) &&
-                                                   uwait(&bars.ti_full[buf], ph, abort, A.err) &&
-                                                   uwait(&bars.ri_full[buf], ph, abort, A.err));
+                                                   uwait(&bars.ti_full[g % kSI], (g / kSI) & 1u, abort, A.err) &&
+                                                   uwait(&bars.ri_full[g % kSI], (g / kSI) & 1u, abort, A.err));
                 if (!ok) break;
-                tc_fence_after();
-                const uint4 ri = *reinterpret_cast<const uint4 *>(sW + buf * kRowInfo + r * 16);
-                const float d = __uint_as_float(ri.x), dmin = __uint_as_float(ri.y);
-                const float *d8s = reinterpret_cast<const float *>(sT + buf * kTokInfo) + ch * half;
-                const uint4 *bps = reinterpret_cast<const uint4 *>(sT + buf * kTokInfo + A.nt * 4) + ch * half;
+                const uint32_t is = g % kSI;
+                const uint4 ri = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * (kDec ? 32 : 16));
+                const uint64_t dd = pk2(__uint_as_float(ri.x), __uint_as_float(ri.x));
+                const uint64_t nm = pk2(-__uint_as_float(ri.y), -__uint_as_float(ri.y)); /* -dmin */
+                const float *d8s = reinterpret_cast<const float *>(sT + is * kTokInfo) + ch * half;
+                const uint4 *bps = reinterpret_cast<const uint4 *>(sT + is * kTokInfo + A.nt * 4) + ch * half;
+                int sc[8];
+                if constexpr (kDec) {
+                    const uint4 r2 = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * 32 + 16);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                    for (int j = 0; j < 8; ++j) sc[j] = (int)(((j < 4 ? r2.x : r2.y) >> (8 * (j & 3))) & 0xFFu);
+                }
+#pragma unroll
+                for (int c = 0; c < kCols / 8; ++c) {
                     if (8 * c < nv) { /* warp-uniform */
-                        uint32_t v1[8], v2[8];
                         const uint32_t col = buf * C::kDbuf + (uint32_t)(ch * half) + 8u * c;
-                        tmem_ld8(tl + col, v1);
-                        tmem_ld8(tl + col + C::kD2, v2);
-                        tmem_wait(v1, v2);
+                        int acc[8];
+                        if constexpr (kDec) {
+                            /* acc = sum_j sc_j * D_j, D_j at column block 32 j */
+                            uint32_t v[8][8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                            for (int j = 0; j < 8; ++j) tmem_ld8(tl + col + C::kDstep * j, v[j]);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) tmem_tie(v[j]);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                int a = 0;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) a += sc[j] * (int)v[j][i];
+                                acc[i] = a;
+                            }
+                        } else {
+                            uint32_t v1[8], v2[8];
+                            tmem_ld8(tl + col, v1);
+                            tmem_ld8(tl + col + C::kDstep, v2);
+                            tmem_wait(v1, v2);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) acc[i] = (int)v1[i] + 16 * (int)v2[i];
+                        }
+                        /* S = fma(d8*d, acc, fma(-(d8*dmin), mins, S)), two tokens a step; a d8 == 0
+                         * block has acc = mins = 0 (all its codes are 0) and adds exact zeros */
+#pragma unroll
+                        for (int i = 0; i < 8; i += 2) {
                             const int t = 8 * c + i;
-                            const float d8 = d8s[t];
-                            const uint4 bp = bps[t];
-                            const int acc = (int)v1[i] + 16 * (int)v2[i];
-                            int mins = __dp2a_lo((int)bp.x, (int)ri.z, 0);
-                            mins = __dp2a_hi((int)bp.y, (int)ri.z, mins);
-                            mins = __dp2a_lo((int)bp.z, (int)ri.w, mins);
-                            mins = __dp2a_hi((int)bp.w, (int)ri.w, mins);
-                            if (d8 != 0.0f)
-                                S[8 * c + i] = __fmaf_rn(__fmul_rn(d8, d), (float)acc,
-                                                         __fmaf_rn(-__fmul_rn(d8, dmin), (float)mins, S[8 * c + i]));
+                            const float2 d8 = *reinterpret_cast<const float2 *>(d8s + t);
+                            const uint64_t d8p = pk2(d8.x, d8.y);
+                            const int m0 = mins_of(bps[t], ri.z, ri.w), m1 = mins_of(bps[t + 1], ri.z, ri.w);
+                            const uint64_t inner = fma2(mul2(d8p, nm), pk2((float)m0, (float)m1), pk2(S[t], S[t + 1]));
+                            const uint64_t out = fma2(mul2(d8p, dd), pk2((float)acc[i], (float)acc[i + 1]), inner);
+                            S[t] = __uint_as_float((uint32_t)out);
+                            S[t + 1] = __uint_as_float((uint32_t)(out >> 32));
                         }
                     }
                 }
-                tc_fence_before();
+                /* the loads above completed (tcgen05.wait::ld): the accumulator may be overwritten */
                 __syncwarp();
                 if (lane == 0) {
                     lfm_mbar_arrive(&bars.t_empty[buf]);
-                    lfm_mbar_arrive(&bars.i_empty[buf]);
+                    lfm_mbar_arrive(&bars.i_empty[is]);
                 }
             }
             if (!ok) break;
             float *yb = A.Y + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
 #pragma unroll
-            for (int t = 0; t < 64; ++t)
+            for (int t = 0; t < kCols; ++t)
                 if (t < nv) yb[(size_t)t * A.rows] = S[t];
         }
         if (!ok) *abort = 1;
@@ -331,13 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
         /* ---------------- producers ---------------- */
         const int pt = tid - C::kEpi * 32;
         const int p = pt & (kM - 1);             /* weight row of the tile                          */
-        const int h0 = kTs ? pt / kM : 0;        /* decode: this thread's half of every super-block */
-        const int nh = kTs ? 1 : 2;
+        const int h0 = kDec ? pt / kM : 0;       /* decode: this thread's half of every super-block */
+        const int nh = kDec ? 1 : 2;
         const uint32_t rowoff = (uint32_t)(p >> 3) * 128u + (uint32_t)(p & 7) * 16u;
-        const uint32_t tla = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::kA0; /* decode: this lane quarter */
         /* producer 0 issues: the tile's 128 rows x super-block gg (144 bytes at x = 144 * sb) */
         auto issue_raw = [&](uint32_t gg) {
-            const UTile tile = A.tiles[blockIdx.x + (gg / nb) * gridDim.x];
+            const UTile tile = tile_at(gg / nb);
             uint64_t *bar = &bars.r_full[gg % C::kSR];
             lfm_mbar_arrive_tx(bar, kRawSlot);
             lfm_tma_load_2d(sR + (gg % C::kSR) * kRawSlot, &tmw, (gg % nb) * kRaw,
@@ -346,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
         bool ok = true;
         if (pt == 0)
             for (uint32_t gg = 0; gg < G && gg < C::kSR - 1; ++gg) issue_raw(gg);
-        /* every decision that leaves a loop is warp-uniform (tcgen05.st is .sync.aligned) */
+        /* every decision that leaves a loop is warp-uniform */
         for (uint32_t g = 0; g < G && ok; ++g) {
             bool w = true;
             /* slot (g - 1) % kSR held super-block g - 1: reissue it once every producer has left it */
@@ -361,65 +446,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
             const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
             const uint32_t scA = s0 & 0x3F3F3F3Fu;
             const uint32_t scB = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-            const uint32_t buf = g & 1u;
             if (h0 == 0) {
                 const uint32_t mA = s1 & 0x3F3F3F3Fu;
                 const uint32_t mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-                w = g < 2 || uwait(&bars.i_empty[buf], ((g >> 1) & 1u) ^ 1u, abort, A.err);
+                w = g < kSI || uwait(&bars.i_empty[g % kSI], ((g / kSI) & 1u) ^ 1u, abort, A.err);
                 if (!__all_sync(LFM_FULL_MASK, w)) { ok = false; break; }
-                sts128(sW + buf * kRowInfo + p * 16, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
+                uint8_t *ri = sW + (g % kSI) * C::kRowInfo + p * (kDec ? 32 : 16);
+                sts128(ri, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
                        __float_as_uint(lfm_h2f((uint16_t)(hdr.x >> 16))), mA, mB);
-                lfm_mbar_arrive(&bars.ri_full[buf]);
+                if (kDec) sts128(ri + 16, scA, scB, 0u, 0u);
+                lfm_mbar_arrive(&bars.ri_full[g % kSI]);
             }
             for (int hh = 0; hh < nh; ++hh) {
                 const uint32_t h = (uint32_t)(h0 + hh);
-                const uint32_t q = 2 * g + h, s = q % kSA;
-                w = q < kSA || uwait(&bars.a_empty[s], ((q / kSA) & 1u) ^ 1u, abort, A.err);
+                uint32_t s, ap;
+                const bool first = aslot(g, h, s, ap);
+                w = first || uwait(&bars.a_empty[s], ap ^ 1u, abort, A.err);
                 if (!__all_sync(LFM_FULL_MASK, w)) { ok = false; break; }
+                uint8_t *a1 = sA + s * C::kAStage, *a2 = a1 + kOp;
                 const uint32_t scw = h ? scB : scA; /* nibble groups 2h, 2h+1: sub-blocks 4h..4h+3 */
-                if constexpr (kTs) {
-                    /* K byte 4j..4j+3 of the half in TMEM column j: word j of nibble group 2h + j/16 */
-                    tc_fence_after();
-                    uint32_t a1[32], a2[32];
 #pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) {
-                        const uint32_t slo = (scw >> (16 * cc)) & 0xFFu, shi = (scw >> (16 * cc + 8)) & 0xFFu;
-                        const uint32_t bl = slo & 15u, al = slo >> 4, bh = shi & 15u, ah = shi >> 4;
+                for (int cc = 0; cc < 2; ++cc) {
+                    const uint32_t slo = (scw >> (16 * cc)) & 0xFFu, shi = (scw >> (16 * cc + 8)) & 0xFFu;
+                    const uint32_t bl = slo & 15u, al = slo >> 4, bh = shi & 15u, ah = shi >> 4;
 #pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            const uint4 w = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc) + 16 * hf);
-                            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                            for (int m = 0; m < 4; ++m) {
-                                const uint32_t lo = ww[m] & 0x0F0F0F0Fu, hi = (ww[m] >> 4) & 0x0F0F0F0Fu;
-                                /* bytes of a nibble word times a scalar <= 15 stay below 256: no carries */
-                                a1[16 * cc + 4 * hf + m] = lo * bl;
-                                a2[16 * cc + 4 * hf + m] = lo * al;
-                                a1[16 * cc + 8 + 4 * hf + m] = hi * bh;
-                                a2[16 * cc + 8 + 4 * hf + m] = hi * ah;
-                            }
-                        }
-                    }
-                    tmem_st32(tla + 64u * s, a1);
-                    tmem_st32(tla + 64u * s + 32u, a2);
-                    tmem_wait_st();
-                    tc_fence_before();
-                } else {
-                    uint8_t *a1 = sA + s * 2 * kOp, *a2 = a1 + kOp;
-#pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) {
-                        const uint32_t slo = (scw >> (16 * cc)) & 0xFFu, shi = (scw >> (16 * cc + 8)) & 0xFFu;
-                        const uint32_t bl = slo & 15u, al = slo >> 4, bh = shi & 15u, ah = shi >> 4;
-#pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            /* bytes 16*hf.. of nibble group 2h+cc: elements 16*hf.. of sub-blocks 4h+2cc (low
-                             * nibbles) and 4h+2cc+1 (high); their 16-byte K chunks within the half: 4cc+hf, 4cc+2+hf */
-                            const uint4 w = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc) + 16 * hf);
-                            const uint32_t l0 = w.x & 0x0F0F0F0Fu, l1 = w.y & 0x0F0F0F0Fu, l2 = w.z & 0x0F0F0F0Fu,
-                                           l3 = w.w & 0x0F0F0F0Fu;
-                            const uint32_t x0 = (w.x >> 4) & 0x0F0F0F0Fu, x1 = (w.y >> 4) & 0x0F0F0F0Fu,
-                                           x2 = (w.z >> 4) & 0x0F0F0F0Fu, x3 = (w.w >> 4) & 0x0F0F0F0Fu;
-                            const uint32_t klo = (4 * cc + hf) * kCoreK + rowoff, khi = (4 * cc + 2 + hf) * kCoreK + rowoff;
+                    for (int hf = 0; hf < 2; ++hf) {
+                        /* bytes 16*hf.. of nibble group 2h+cc: elements 16*hf.. of sub-blocks 4h+2cc (low
+                         * nibbles) and 4h+2cc+1 (high); their 16-byte K chunks within the half: 4cc+hf, 4cc+2+hf */
+                        const uint4 w4 = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc) + 16 * hf);
+                        const uint32_t l0 = w4.x & 0x0F0F0F0Fu, l1 = w4.y & 0x0F0F0F0Fu, l2 = w4.z & 0x0F0F0F0Fu,
+                                       l3 = w4.w & 0x0F0F0F0Fu;
+                        const uint32_t x0 = (w4.x >> 4) & 0x0F0F0F0Fu, x1 = (w4.y >> 4) & 0x0F0F0F0Fu,
+                                       x2 = (w4.z >> 4) & 0x0F0F0F0Fu, x3 = (w4.w >> 4) & 0x0F0F0F0Fu;
+                        const uint32_t klo = (4 * cc + hf) * kCoreK + rowoff, khi = (4 * cc + 2 + hf) * kCoreK + rowoff;
+                        if constexpr (kDec) {
+                            /* the nibbles themselves; the scales are applied per sub-block in the epilogue */
+                            sts128(a1 + klo, l0, l1, l2, l3);
+                            sts128(a1 + khi, x0, x1, x2, x3);
+                        } else {
                             /* bytes of a nibble word times a scalar <= 15 stay below 256: no carries */
                             sts128(a1 + klo, l0 * bl, l1 * bl, l2 * bl, l3 * bl);
                             sts128(a2 + klo, l0 * al, l1 * al, l2 * al, l3 * al);
@@ -427,47 +491,49 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
                             sts128(a2 + khi, x0 * ah, x1 * ah, x2 * ah, x3 * ah);
                         }
                     }
-                    fence_async_smem(); /* generic-proxy writes -> the tensor core's reads */
                 }
+                fence_async_smem(); /* generic-proxy writes -> the tensor core's reads */
                 lfm_mbar_arrive(&bars.a_full[s]);
             }
             if (ok) lfm_mbar_arrive(&bars.r_empty[g % C::kSR]);
         }
         if (!ok) *abort = 1;
-    } else if (warp == C::kWarpMma) {
-        /* ---------------- MMA issue ---------------- */
+    } else if (warp < C::kWarpLoad) {
+        /* ---------------- MMA issue: two streams of independent accumulators ----------------
+         * decode: stream h issues the K steps of half h (sub-blocks 4h..4h+3 -> D_4h..D_4h+3);
+         * prefill: stream 0 issues A1 -> D1, stream 1 A2 -> D2, each over the whole super-block. */
+        const uint32_t st = (uint32_t)(warp - C::kWarpMma);
         if (lane == 0) {
             bool ok = true;
             const uint32_t idesc = kIdescBase | ((A.nt >> 3) << 17), blbo = A.nt * 16u;
             for (uint32_t g = 0; g < G && ok; ++g) {
                 const uint32_t buf = g & 1u;
                 if (g >= 2 && !uwait(&bars.t_empty[buf], ((g >> 1) & 1u) ^ 1u, abort, A.err)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t d1 = tmem + buf * C::kDbuf, d2 = d1 + C::kD2;
-                for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t q = 2 * g + h, s = q % kSA, ph = (q / kSA) & 1u;
-                    if (!uwait(&bars.a_full[s], ph, abort, A.err) || !uwait(&bars.b_full[s], ph, abort, A.err)) {
+                const uint32_t d0 = tmem + buf * C::kDbuf;
+                for (uint32_t h = kDec ? st : 0u; h < (kDec ? st + 1 : 2u); ++h) {
+                    uint32_t s, ph, sb, pb;
+                    aslot(g, h, s, ph);
+                    bslot(g, h, sb, pb);
+                    /* operands written by threads (fence.proxy.async before their arrival) or by bulk
+                     * copies: the barrier alone orders them before the MMA's reads */
+                    if (!uwait(&bars.a_full[s], ph, abort, A.err) || !uwait(&bars.b_full[sb], pb, abort, A.err)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t b = lfm_smem_u32(sB + s * kOp);
+                    const uint32_t b = lfm_smem_u32(sB + sb * A.nt * kHalf);
+                    const uint32_t a = lfm_smem_u32(sA + s * C::kAStage) + (kDec ? 0u : st * kOp);
 #pragma unroll
                     for (uint32_t k = 0; k < 4; ++k) {
-                        const uint32_t en = (h | k) ? 1u : 0u;
                         const uint64_t bd = udesc(b + 2 * k * blbo, blbo);
-                        if constexpr (kTs) {
-                            const uint32_t a1 = tmem + C::kA0 + 64u * s + 8u * k; /* 8 columns = 32 K bytes */
-                            umma_i8_ts(d1, a1, bd, idesc, en);
-                            umma_i8_ts(d2, a1 + 32u, bd, idesc, en);
+                        if constexpr (kDec) {
+                            /* K step k of half h = sub-block 4h + k, into its own accumulator */
+                            umma_i8(d0 + C::kDstep * (4 * h + k), udesc(a + 2 * k * kCoreK, kCoreK), bd, idesc, 0u);
                         } else {
-                            const uint32_t a1 = lfm_smem_u32(sA + s * 2 * kOp), a2 = a1 + kOp;
-                            umma_i8(d1, udesc(a1 + 2 * k * kCoreK, kCoreK), bd, idesc, en);
-                            umma_i8(d2, udesc(a2 + 2 * k * kCoreK, kCoreK), bd, idesc, en);
+                            umma_i8(d0 + C::kDstep * st, udesc(a + 2 * k * kCoreK, kCoreK), bd, idesc, (h | k) ? 1u : 0u);
                         }
                     }
                     umma_commit(&bars.a_empty[s]);
-                    umma_commit(&bars.b_empty[s]);
+                    umma_commit(&bars.b_empty[sb]);
                 }
                 if (ok) umma_commit(&bars.t_full[buf]);
             }
@@ -478,21 +544,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
         if (lane == 0) {
             bool ok = true;
             for (uint32_t g = 0; g < G && ok; ++g) {
-                const UTile tile = A.tiles[blockIdx.x + (g / nb) * gridDim.x];
+                const UTile tile = tile_at(g / nb);
                 const uint32_t opb = A.nt * kHalf; /* one half super-block of the block's codes */
                 const uint8_t *src = A.xt + ((size_t)tile.tb * nb + g % nb) * xt_sb_bytes(A.nt);
-                const uint32_t buf = g & 1u;
-                if (g >= 2 && !uwait(&bars.i_empty[buf], ((g >> 1) & 1u) ^ 1u, abort, A.err)) { ok = false; break; }
-                lfm_mbar_arrive_tx(&bars.ti_full[buf], A.nt * 20u);
-                lfm_bulk_g2s_plain(sT + buf * kTokInfo, src + 2 * opb, A.nt * 20u, &bars.ti_full[buf]);
+                const uint32_t is = g % kSI;
+                if (g >= kSI && !uwait(&bars.i_empty[is], ((g / kSI) & 1u) ^ 1u, abort, A.err)) { ok = false; break; }
+                lfm_mbar_arrive_tx(&bars.ti_full[is], A.nt * 20u);
+                lfm_bulk_g2s_plain(sT + is * kTokInfo, src + 2 * opb, A.nt * 20u, &bars.ti_full[is]);
                 for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t q = 2 * g + h, s = q % kSA;
-                    if (q >= kSA && !uwait(&bars.b_empty[s], ((q / kSA) & 1u) ^ 1u, abort, A.err)) {
+                    uint32_t s, bp;
+                    const bool first = bslot(g, h, s, bp);
+                    if (!first && !uwait(&bars.b_empty[s], bp ^ 1u, abort, A.err)) {
                         ok = false;
                         break;
                     }
                     lfm_mbar_arrive_tx(&bars.b_full[s], opb);
-                    lfm_bulk_g2s_plain(sB + s * kOp, src + h * opb, opb, &bars.b_full[s]);
+                    lfm_bulk_g2s_plain(sB + s * opb, src + h * opb, opb, &bars.b_full[s]);
                 }
             }
             if (!ok) *abort = 1;
@@ -677,9 +744,12 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t experts, uint32_t row
     const uint64_t row_bytes = (uint64_t)(cols / 256) * kRaw;
     if (!lfm_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, row_bytes, (uint64_t)experts * rows, row_bytes, kRaw, kM))
         return cudaErrorInvalidValue;
-    UmmaArgs a{W, rows, cols / 256, xt, nt, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
+    const bool dec = nt <= kNtDecode;
+    uint32_t nsb = min((uint32_t)kMaxSB, (uint32_t)(dec ? UCfg<true>::kBBytes : UCfg<false>::kBBytes) / (nt * kHalf));
+    if (dec) nsb &= ~1u; /* one B ring per half super-block */
+    UmmaArgs a{W, rows, cols / 256, xt, nt, nsb, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
                n_tiles, Y, err};
-    if (nt <= kNtDecode) {
+    if (dec) {
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<true>, UCfg<true>::kSmem, cache);
         if (e != cudaSuccess) return e;
