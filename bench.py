@@ -328,7 +328,7 @@ def run_ours(args, cfg):
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-               "vs_baseline": None, "dtype": "q4_k x q8_k int (dp4a), fp32 accum", "data": "synthetic (seeded)",
+               "vs_baseline": None, "dtype": "u8 x s8 -> s32 (q4_k x q8_k), fp32 accum", "data": "synthetic (seeded)",
                "config": config_dict(args.config, cfg, R, {"parallelism": f"replicas x{ws}" if ws > 1 else "single",
                                                            "layer_hbm_frac": round(layer_frac, 4),
                                                            "unique_experts_per_step": loads / args.steps}),
@@ -438,6 +438,15 @@ def run_stack(args, cfg):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # kernels one step launches: the library's own count (graph replay on one GPU, per call with EP)
+    if use_ep:
+        l0 = ops.launches
+        step()
+        launches_per_step = ops.launches - l0
+    else:
+        step()
+        launches_per_step = g.last_stats()["kernels_launched"]
+    torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -481,13 +490,41 @@ def run_stack(args, cfg):
                 "frac": ach / 4500.0, "traffic": None,
                 "peak_src": "nominal dense int8 4.5 POPS (MEASURED_PEAKS.json holds no int8 figure)",
                 "algorithmic_ops_per_step": ops_step}
+    # end to end through the public API with host buffers: this rank's tokens copied in from pinned
+    # host memory, the whole stack, the result copied back, every step; wall clock, max over ranks
+    pinned = torch.empty((Tl, D), dtype=torch.float32, pin_memory=True)
+    pinned.numpy()[:] = x0
+    n_e2e = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        if not use_ep:
+            g.forward_stack(0, len(layers), pinned.numpy())
+            return
+        x.copy_(pinned, non_blocking=True)
+        step()
+        pinned.copy_(x, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_step()
+    if ws > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    if ws > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = T * n_e2e / e2e_s
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = stack_cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-               "vs_baseline": None, "dtype": "q4_k x q8_k int (dp4a), fp32 accum", "data": "synthetic (seeded)",
+               "vs_baseline": None, "dtype": "u8 x s8 -> s32 (q4_k x q8_k), fp32 accum", "data": "synthetic (seeded)",
                "config": {"workload": f"cfg{args.config}: {cfg['name']} ({n_dense} dense + {n_moe} lfm2moe FFN layers, "
                                       f"D={D} E={E} top-{K} I={I}, {T} tokens per step in total)",
                           "tokens_per_step": T, "layers": len(layers),
@@ -495,7 +532,9 @@ def run_stack(args, cfg):
                           if use_ep else ("single" if ws == 1 else f"replicas x{ws}"),
                           "l2": "the stack's weights exceed the 126 MB L2; every step streams them from HBM",
                           "unique_experts_per_moe_layer": loads / args.steps / n_moe},
-               "roofline": roof, "cpu_baseline": cpu, "gpu_launches": None, "clocks": clk}
+               "roofline": roof, "cpu_baseline": cpu,
+               "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
+               "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         print(json.dumps(out), flush=True)
     g.close()
     if ws > 1:

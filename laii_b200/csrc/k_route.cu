@@ -529,6 +529,13 @@ static size_t route_cluster_smem(const MoeLayerDev &L, uint32_t T, uint32_t *epc
     return bytes;
 }
 
+uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T) {
+    uint32_t epc = 0;
+    if (T == 0) return 0;
+    if (route_cluster_smem(L, T, &epc) > 0) return 1;
+    return L.dense ? 2u : 3u;
+}
+
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
                              cudaStream_t s, bool pdl) {
     if (T == 0) return cudaSuccess;

@@ -277,11 +277,11 @@ lfm_gpu_status_t check_layer_shape(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D,
     return LFM_GPU_OK;
 }
 
-/* Launch one kernel, bracketed by events when profiling is on. */
+/* Launch one step (`kernels` kernel launches), bracketed by events when profiling is on. */
 template <typename F>
-cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
+cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch, uint32_t kernels = 1) {
     if (!h->prof) {
-        ++h->stats.kernels_launched;
+        h->stats.kernels_launched += kernels;
         return launch();
     }
     ProfRec r{kid, nullptr, nullptr};
@@ -292,7 +292,7 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch) {
     if (e == cudaSuccess) e = cudaEventRecord(r.b, s);
     if (e == cudaSuccess) {
         h->recs.push_back(r);
-        ++h->stats.kernels_launched;
+        h->stats.kernels_launched += kernels;
     } else {
         if (r.a) cudaEventDestroy(r.a);
         if (r.b) cudaEventDestroy(r.b);
@@ -320,7 +320,7 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
             cudaError_t e = lfm_launch_umma_plan(w.rt, L.I, nt, w.utiles_gu, w.utbs, w.ucounts, mgu, mtb, s);
             return e == cudaSuccess ? lfm_launch_umma_plan(w.rt, L.D, nt, w.utiles_dn, w.utbs, w.ucounts + 2, mdn, mtb, s)
                                     : e;
-        }));
+        }, 2));
         LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
             return lfm_launch_q4k_umma(L.gate, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.rt.err, grid, s);
@@ -340,7 +340,7 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
         LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
             cudaError_t e = lfm_launch_gemm_plan(w.rt, L.I, w.tiles_gu, w.n_tiles, w.max_tiles_gu, s);
             return e == cudaSuccess ? lfm_launch_gemm_plan(w.rt, L.D, w.tiles_dn, w.n_tiles + 1, w.max_tiles_dn, s) : e;
-        }));
+        }, 2));
         LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
             return lfm_launch_q4k_gemm(L.gate, L.I, L.D, xq, w.rt.perm, K, w.tiles_gu, w.n_tiles, w.h, w.rt.err, grid, s);
         }));
@@ -377,7 +377,8 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
         LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
         return LFM_GPU_OK;
     }
-    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); },
+                      lfm_route_kernels(L, T)));
     return run_experts(h, L, x, T, xq, s, pdl);
 }
 
@@ -1010,6 +1011,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_route(lfm_gpu_moe_t *h, uint32_t layer, 
     Q8Rows xq = w.xq; xq.cols = L.D;
     RouteTables rt = w.rt;
     rt.loads = nullptr; /* expert loads are counted where the experts run (lfm_gpu_moe_ep_experts) */
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+    h->stats.kernels_launched = lfm_route_kernels(L, T) + 1;
     LFM_CUDA(h, lfm_launch_route(L, x, T, xq, rt, s, false));
     LFM_CUDA(h, cudaMemcpyAsync(idx_out, w.rt.idx, sizeof(int32_t) * T * L.K, cudaMemcpyDeviceToDevice, s));
     LFM_CUDA(h, cudaMemcpyAsync(w_out, w.rt.w, sizeof(float) * T * L.K, cudaMemcpyDeviceToDevice, s));
@@ -1040,6 +1044,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     Workspace &w = h->ws;
     Q8Rows xq = w.xq; xq.cols = Lx.D;
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = n_rows;
+    h->stats.kernels_launched = 3; /* + those of run_experts */
     LFM_CUDA(h, lfm_launch_gguf_to_q8(static_cast<const uint8_t *>(q8_in), n_rows, xq, s));
     LFM_CUDA(h, lfm_launch_ep_prepare(expert_ids, n_rows, first, count, w.rt, s));
     LFM_CUDA(h, lfm_launch_dispatch(Lx, n_rows, w.rt, s));
@@ -1055,6 +1062,9 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer
     if (T == 0) return LFM_GPU_OK;
     if (!x || !w || !y) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null buffer");
     DeviceGuard g(h->device);
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+    h->stats.kernels_launched = 1;
     LFM_CUDA(h, lfm_launch_ep_combine(x, T, S->dev.D, S->dev.K, w, y, static_cast<cudaStream_t>(stream)));
     return LFM_GPU_OK;
 }

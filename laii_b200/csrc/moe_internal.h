@@ -81,6 +81,8 @@ cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16);
 cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
                              cudaStream_t s, bool pdl);
+/* kernel launches lfm_launch_route makes for (L, T) */
+uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T);
 
 /* k_expert.cu */
 size_t lfm_gemv_smem(uint32_t cols, uint32_t mats);

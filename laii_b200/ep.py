@@ -114,6 +114,10 @@ class GpuOps:
         self.moe = moe
         self.D = D
         self.K = K
+        self.launches = 0  # CUDA kernels launched by the library through these calls
+
+    def _count(self):
+        self.launches += self.moe.last_stats()["kernels_launched"]
 
     def _stream(self) -> int:
         return torch.cuda.current_stream().cuda_stream
@@ -125,6 +129,7 @@ class GpuOps:
         w = torch.empty((T, self.K), dtype=torch.float32, device=dev)
         q8 = torch.empty((T, self.D // 256 * Q8K_BYTES), dtype=torch.uint8, device=dev)
         self.moe.ep_route(layer, x.data_ptr(), T, idx.data_ptr(), w.data_ptr(), q8.data_ptr(), self._stream())
+        self._count()
         return idx, w, q8
 
     def experts(self, layer: int, q8: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
@@ -135,8 +140,10 @@ class GpuOps:
         for a in range(0, n, self.MAX_ROWS):
             m = min(self.MAX_ROWS, n - a)
             self.moe.ep_experts(layer, q8[a:].data_ptr(), m, ids[a:].data_ptr(), y[a:].data_ptr(), self._stream())
+            self._count()
         return y
 
     def combine(self, layer: int, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
         self.moe.ep_combine(layer, x.data_ptr(), x.shape[0], w.contiguous().data_ptr(), y.contiguous().data_ptr(),
                             self._stream())
+        self._count()
