@@ -279,7 +279,7 @@ def run_ours(args, cfg):
     stq = g.last_stats()
     ploads = stq["expert_loads"] - stp["expert_loads"]
     # dominant kernel among those whose algorithmic work is counted below
-    known = [k for k in prof if k in ("gateup", "down", "moe_layer", "gemm_gate", "gemm_up", "gemm_down")]
+    known = [k for k in prof if k in ("gateup", "down", "moe_layer", "gemm_gate", "gemm_up", "gemm_down", "gemm_gateup")]
     dom = max(known or list(prof), key=lambda k: prof[k][1])
     n_launch, tot_ms = prof[dom]
     gu_bytes = 2 * I * (D // 256) * Q4K
@@ -292,7 +292,8 @@ def run_ours(args, cfg):
     tensor_bound = dom.startswith("gemm_")
     if tensor_bound:
         # int8 ops of one GEMM launch: 2 * (T*K rows) * rows_out * cols (each matrix once)
-        gemm_ops = {"gemm_gate": 2.0 * T * K * I * D, "gemm_up": 2.0 * T * K * I * D, "gemm_down": 2.0 * T * K * D * I}
+        gemm_ops = {"gemm_gate": 2.0 * T * K * I * D, "gemm_up": 2.0 * T * K * I * D, "gemm_down": 2.0 * T * K * D * I,
+                    "gemm_gateup": 4.0 * T * K * I * D}
         ach = gemm_ops[dom] / (tot_ms / n_launch / 1e3) / 1e12
     else:
         ach = per_launch_bytes.get(dom, 0.0) / (tot_ms / n_launch / 1e3) / 1e9

@@ -37,8 +37,48 @@ struct RouteSmem {
     int cur[LFM_GPU_MAX_EXPERTS_DEV];
     int act[LFM_GPU_MAX_EXPERTS_DEV]; /* active experts, in id order */
     int pb[LFM_GPU_MAX_EXPERTS_DEV];  /* first work pair of each active expert */
-    int uniq;
+    int tbb[LFM_GPU_MAX_EXPERTS_DEV + 1]; /* first token block of each active expert (tcgen05 plan) */
+    int uniq, bad;
 };
+
+/* The tcgen05 GEMMs' tile plans from the counts just formed (token blocks of
+ * <= nt slots per active expert; tiles with the token blocks fastest, so the
+ * CTAs that share a weight block run together and share it through L2). */
+__device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
+    const UmmaPlanOut &P = rt.plan;
+    const int nt = (int)P.nt, nrg = (int)P.rows_gu / 128, nrd = (int)P.rows_dn / 128;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    __syncthreads();
+    const int U = s.uniq;
+    if (threadIdx.x == 0) {
+        int a = 0;
+        for (int u = 0; u < U; ++u) {
+            s.tbb[u] = a;
+            a += (s.cnt[s.act[u]] + nt - 1) / nt;
+        }
+        s.tbb[U] = a;
+        s.bad = (uint32_t)a > P.max_tb || (uint32_t)(2 * a * nrg) > P.max_gu || (uint32_t)(a * nrd) > P.max_dn;
+        if (s.bad) atomicOr(rt.err, LFM_DEVERR_SEGMENT);
+        P.counts[0] = s.bad ? 0 : 2 * a * nrg;
+        P.counts[1] = s.bad ? 0 : a;
+        P.counts[2] = s.bad ? 0 : a * nrd;
+        P.counts[3] = s.bad ? 0 : a;
+    }
+    __syncthreads();
+    if (s.bad) return;
+    for (int u = warp; u < U; u += nwarps) {
+        const int e = s.act[u], cnt = s.cnt[e], off = s.off[e], t0 = s.tbb[u], n = s.tbb[u + 1] - t0;
+        for (int i = lane; i < n; i += 32) P.tbs[t0 + i] = LfmUTokBlock{off + i * nt, min(nt, cnt - i * nt)};
+        for (int q = lane; q < 2 * n * nrg; q += 32) { /* gate and up tiles of a block side by side */
+            const int m = q & 1, rb = (q >> 1) / n, i = (q >> 1) - rb * n;
+            P.tiles_gu[2 * t0 * nrg + q] = LfmUTile{e, t0 + i, rb * 128, m};
+        }
+        for (int q = lane; q < n * nrd; q += 32) {
+            const int rb = q / n, i = q - rb * n;
+            P.tiles_dn[t0 * nrd + q] = LfmUTile{e, t0 + i, rb * 128, 0};
+        }
+    }
+}
 
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
@@ -112,6 +152,7 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
             rt.inv[a] = -1;
         }
     }
+    if (rt.plan.nt) route_plan(rt, s);
 }
 
 /* Top-K of token t from its E logits (global memory written by other blocks,

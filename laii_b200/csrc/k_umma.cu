@@ -105,12 +105,8 @@ constexpr int kThreads = UCfg<false>::kThreads;
  * B s8 (10-12 = 1), both K-major, M >> 4 at bits 24-28; N >> 3 goes to 17-22. */
 constexpr uint32_t kIdescBase = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(kM >> 4) << 24);
 
-struct UTile {
-    int32_t expert, tb, row0, pad;
-};
-struct UTokBlock {
-    int32_t slot0, ntok;
-};
+using UTile = LfmUTile;
+using UTokBlock = LfmUTokBlock;
 
 struct UmmaArgs {
     const uint8_t *W;     /* expert tensors [E][rows][nb] Q4_K */
@@ -121,7 +117,7 @@ struct UmmaArgs {
     const UTile *tiles;
     const UTokBlock *tbs;
     const int32_t *n_tiles;
-    float *Y;             /* [slots][rows] */
+    float *Y[2];          /* [slots][rows] per matrix */
     uint32_t *err;
 };
 
@@ -234,7 +230,8 @@ __device__ __forceinline__ bool uwait(uint64_t *bar, uint32_t parity, volatile i
 }
 
 template <bool kDec>
-__global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw, UmmaArgs A) {
+__global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw0,
+                                                          const __grid_constant__ CUtensorMap tmw1, UmmaArgs A) {
     using C = UCfg<kDec>;
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ UmmaBars bars;
@@ -407,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
                 }
             }
             if (!ok) break;
-            float *yb = A.Y + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
+            float *yb = A.Y[tile.mat] + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
 #pragma unroll
             for (int t = 0; t < kCols; ++t)
                 if (t < nv) yb[(size_t)t * A.rows] = S[t];
@@ -425,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
             const UTile tile = tile_at(gg / nb);
             uint64_t *bar = &bars.r_full[gg % C::kSR];
             lfm_mbar_arrive_tx(bar, kRawSlot);
-            lfm_tma_load_2d(sR + (gg % C::kSR) * kRawSlot, &tmw, (gg % nb) * kRaw,
+            lfm_tma_load_2d(sR + (gg % C::kSR) * kRawSlot, tile.mat ? &tmw1 : &tmw0, (gg % nb) * kRaw,
                             (uint32_t)tile.expert * A.rows + tile.row0, bar);
         };
         bool ok = true;
@@ -625,54 +622,6 @@ __global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm
     }
 }
 
-/* Tile plan from the dispatch tables: token blocks of <= nt slots per active
- * expert, then tiles = (expert, 128-row block, token block) with the token
- * blocks fastest, so CTAs that share a weight block run together and share it
- * through L2.  One block; counts[0] = tiles, counts[1] = token blocks. */
-__global__ void k_umma_plan(RouteTables rt, uint32_t rows, uint32_t nt, UTile *tiles, UTokBlock *tbs,
-                            int32_t *counts, uint32_t max_tiles, uint32_t max_tb) {
-    __shared__ int s_e[LFM_GPU_MAX_EXPERTS_DEV], s_cnt[LFM_GPU_MAX_EXPERTS_DEV], s_off[LFM_GPU_MAX_EXPERTS_DEV];
-    __shared__ int s_tb[LFM_GPU_MAX_EXPERTS_DEV + 1], s_ti[LFM_GPU_MAX_EXPERTS_DEV + 1];
-    __shared__ int s_bad;
-    const int U = __ldcg(rt.summary + 0);
-    const int nrb = (int)rows / kM;
-    for (int u = threadIdx.x; u < U; u += blockDim.x) {
-        const int e = __ldcg(rt.act + u);
-        s_e[u] = e;
-        s_cnt[u] = __ldcg(rt.counts + e);
-        s_off[u] = __ldcg(rt.offsets + e);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int a = 0, b = 0;
-        for (int u = 0; u < U; ++u) {
-            const int n = (s_cnt[u] + (int)nt - 1) / (int)nt;
-            s_tb[u] = a;
-            s_ti[u] = b;
-            a += n;
-            b += n * nrb;
-        }
-        s_bad = (uint32_t)a > max_tb || (uint32_t)b > max_tiles;
-        if (s_bad) {
-            atomicOr(rt.err, LFM_DEVERR_SEGMENT);
-            a = b = 0;
-        }
-        counts[0] = b;
-        counts[1] = a;
-    }
-    __syncthreads();
-    if (s_bad) return;
-    for (int u = 0; u < U; ++u) {
-        const int n = (s_cnt[u] + (int)nt - 1) / (int)nt;
-        for (int q = threadIdx.x; q < n; q += blockDim.x)
-            tbs[s_tb[u] + q] = UTokBlock{s_off[u] + q * (int)nt, min((int)nt, s_cnt[u] - q * (int)nt)};
-        for (int q = threadIdx.x; q < n * nrb; q += blockDim.x) {
-            const int rb = q / n, i = q - rb * n;
-            tiles[s_ti[u] + q] = UTile{s_e[u], s_tb[u] + i, rb * kM, 0};
-        }
-    }
-}
-
 }  // namespace
 
 bool lfm_umma_ok(uint32_t rows) { return rows % kM == 0; }
@@ -686,17 +635,7 @@ size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts, uint32_t nt) { return (
 size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint32_t nt) {
     return (size_t)(rows / kM) * lfm_umma_tb_max(slots, experts, nt);
 }
-size_t lfm_umma_tile_bytes() { return sizeof(UTile); }
-size_t lfm_umma_tb_bytes() { return sizeof(UTokBlock); }
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt) { return max_tb * nb * (size_t)xt_sb_bytes(nt); }
-
-cudaError_t lfm_launch_umma_plan(const RouteTables &rt, uint32_t rows, uint32_t nt, void *tiles, void *tbs,
-                                 int32_t *counts, uint32_t max_tiles, uint32_t max_tb, cudaStream_t s) {
-    if (nt % 16 || nt == 0 || nt > (uint32_t)kN) return cudaErrorInvalidValue;
-    k_umma_plan<<<1, 256, 0, s>>>(rt, rows, nt, static_cast<UTile *>(tiles), static_cast<UTokBlock *>(tbs), counts,
-                                  max_tiles, max_tb);
-    return cudaGetLastError();
-}
 
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
@@ -734,31 +673,32 @@ bool lfm_tmap_2d(CUtensorMap *tm, CUtensorMapDataType type, uint32_t elem_bytes,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t experts, uint32_t rows, uint32_t cols, const uint8_t *xt,
-                                uint32_t nt, const void *tiles, const void *tbs, const int32_t *n_tiles, float *Y,
-                                uint32_t *err, int grid, cudaStream_t s) {
+cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
+                                const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
+                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s) {
     if (rows % kM || cols % 256 || experts == 0 || nt % 16 || nt == 0 || nt > (uint32_t)kN)
         return cudaErrorInvalidValue;
-    /* the expert tensor as a 2-D byte matrix [experts * rows][nb * 144] */
-    CUtensorMap tm;
+    /* each expert tensor as a 2-D byte matrix [experts * rows][nb * 144] */
+    CUtensorMap tm0, tm1;
     const uint64_t row_bytes = (uint64_t)(cols / 256) * kRaw;
-    if (!lfm_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, row_bytes, (uint64_t)experts * rows, row_bytes, kRaw, kM))
+    if (!lfm_tmap_2d(&tm0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W0, row_bytes, (uint64_t)experts * rows, row_bytes, kRaw, kM) ||
+        !lfm_tmap_2d(&tm1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W1, row_bytes, (uint64_t)experts * rows, row_bytes, kRaw, kM))
         return cudaErrorInvalidValue;
     const bool dec = nt <= kNtDecode;
     uint32_t nsb = min((uint32_t)kMaxSB, (uint32_t)(dec ? UCfg<true>::kBBytes : UCfg<false>::kBBytes) / (nt * kHalf));
     if (dec) nsb &= ~1u; /* one B ring per half super-block */
-    UmmaArgs a{W, rows, cols / 256, xt, nt, nsb, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
-               n_tiles, Y, err};
+    UmmaArgs a{W0, rows, cols / 256, xt, nt, nsb, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
+               n_tiles, {Y0, Y1}, err};
     if (dec) {
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<true>, UCfg<true>::kSmem, cache);
         if (e != cudaSuccess) return e;
-        k_q4k_umma<true><<<grid, kThreads, UCfg<true>::kSmem, s>>>(tm, a);
+        k_q4k_umma<true><<<grid, kThreads, UCfg<true>::kSmem, s>>>(tm0, tm1, a);
     } else {
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<false>, UCfg<false>::kSmem, cache);
         if (e != cudaSuccess) return e;
-        k_q4k_umma<false><<<grid, kThreads, UCfg<false>::kSmem, s>>>(tm, a);
+        k_q4k_umma<false><<<grid, kThreads, UCfg<false>::kSmem, s>>>(tm0, tm1, a);
     }
     return cudaGetLastError();
 }

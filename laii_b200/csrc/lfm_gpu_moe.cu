@@ -51,7 +51,8 @@ struct Workspace {
     int32_t *n_tiles = nullptr; /* [2] */
     uint32_t max_tiles_gu = 0, max_tiles_dn = 0;
     /* tcgen05 GEMM path (k_umma.cu): 128-row tile plans, token blocks, pre-gathered tokens */
-    void *utiles_gu = nullptr, *utiles_dn = nullptr, *utbs = nullptr;
+    LfmUTile *utiles_gu = nullptr, *utiles_dn = nullptr;
+    LfmUTokBlock *utbs = nullptr;
     int32_t *ucounts = nullptr; /* [4]: tiles gu, blocks, tiles dn, blocks */
     uint8_t *xt = nullptr;
     uint32_t umax_gu = 0, umax_dn = 0, umax_tb = 0;
@@ -61,10 +62,10 @@ struct Workspace {
 
 namespace {
 enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D,
-                K_XT, K_COUNT };
+                K_XT, K_GEMM_GU, K_COUNT };
 const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer",
                                            "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down",
-                                           "xt_gather"};
+                                           "xt_gather", "gemm_gateup"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -201,12 +202,12 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_nt = take(sizeof(int32_t) * 2);
     /* tcgen05 GEMM scratch for the smallest token block (the most blocks) and the largest (the most bytes) */
     const size_t umax_tb = lfm_umma_tb_max((uint32_t)TK, E, 16);
-    const size_t umax_gu = lfm_umma_tiles_max(I, (uint32_t)TK, E, 16), umax_dn = lfm_umma_tiles_max(D, (uint32_t)TK, E, 16);
+    const size_t umax_gu = 2 * lfm_umma_tiles_max(I, (uint32_t)TK, E, 16), umax_dn = lfm_umma_tiles_max(D, (uint32_t)TK, E, 16);
     const uint32_t nbx = (D > I ? D : I) / 256;
     const size_t xt16 = lfm_umma_xt_bytes(umax_tb, nbx, 16), xt128 = lfm_umma_xt_bytes(lfm_umma_tb_max((uint32_t)TK, E, 128), nbx, 128);
-    const size_t o_utgu = take(lfm_umma_tile_bytes() * umax_gu);
-    const size_t o_utdn = take(lfm_umma_tile_bytes() * umax_dn);
-    const size_t o_utbs = take(lfm_umma_tb_bytes() * umax_tb);
+    const size_t o_utgu = take(sizeof(LfmUTile) * umax_gu);
+    const size_t o_utdn = take(sizeof(LfmUTile) * umax_dn);
+    const size_t o_utbs = take(sizeof(LfmUTokBlock) * umax_tb);
     const size_t o_ucnt = take(sizeof(int32_t) * 4);
     const size_t o_xt = take(xt16 > xt128 ? xt16 : xt128);
     void *base = nullptr;
@@ -253,9 +254,9 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.n_tiles = reinterpret_cast<int32_t *>(b + o_nt);
     w.max_tiles_gu = (uint32_t)mt_gu;
     w.max_tiles_dn = (uint32_t)mt_dn;
-    w.utiles_gu = b + o_utgu;
-    w.utiles_dn = b + o_utdn;
-    w.utbs = b + o_utbs;
+    w.utiles_gu = reinterpret_cast<LfmUTile *>(b + o_utgu);
+    w.utiles_dn = reinterpret_cast<LfmUTile *>(b + o_utdn);
+    w.utbs = reinterpret_cast<LfmUTokBlock *>(b + o_utbs);
     w.ucounts = reinterpret_cast<int32_t *>(b + o_ucnt);
     w.xt = b + o_xt;
     w.umax_gu = (uint32_t)umax_gu;
@@ -304,34 +305,45 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch, uint32_
  * T > 16: grouped GEMMs on the tensor cores -- tcgen05 (k_umma.cu, token
  * blocks sized to the tokens per expert) where rows % 128 == 0, else mma.sync
  * (k_gemm.cu) for prefill-sized loads; otherwise the grouped GEMVs. */
+/* The tcgen05 tile plans a forward of T tokens on L needs, for the dispatch
+ * step to build (nt == 0 when the tcgen05 GEMMs are not the path). */
+UmmaPlanOut umma_plan_for(lfm_gpu_moe_t *h, const MoeLayerDev &L, uint32_t T) {
+    UmmaPlanOut p{};
+    if (!(h->use_gemm && h->use_umma && T > LFM_FUSED_MAX_T && lfm_umma_ok(L.I) && lfm_umma_ok(L.D))) return p;
+    Workspace &w = h->ws;
+    const uint32_t TK = T * lfm_layer_K(L), E = lfm_layer_E(L);
+    p.nt = lfm_umma_nt(TK, E);
+    p.rows_gu = L.I;
+    p.rows_dn = L.D;
+    p.tiles_gu = w.utiles_gu;
+    p.tiles_dn = w.utiles_dn;
+    p.tbs = w.utbs;
+    p.counts = w.ucounts;
+    p.max_tb = (uint32_t)lfm_umma_tb_max(TK, E, p.nt);
+    p.max_gu = 2 * (uint32_t)lfm_umma_tiles_max(L.I, TK, E, p.nt); /* gate and up */
+    p.max_dn = (uint32_t)lfm_umma_tiles_max(L.D, TK, E, p.nt);
+    return p;
+}
+
 lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, uint32_t T, Q8Rows xq,
-                             cudaStream_t s, bool pdl) {
+                             cudaStream_t s, bool pdl, const UmmaPlanOut &plan) {
     Workspace &w = h->ws;
     Q8Rows hq = w.hq; hq.cols = L.I;
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);
     const bool prefill = h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L);
-    if (h->use_gemm && h->use_umma && T > LFM_FUSED_MAX_T && lfm_umma_ok(L.I) && lfm_umma_ok(L.D)) {
-        const uint32_t TK = T * K, E = lfm_layer_E(L);
-        const uint32_t nt = lfm_umma_nt(TK, E);
-        const uint32_t mtb = (uint32_t)lfm_umma_tb_max(TK, E, nt);
-        const uint32_t mgu = (uint32_t)lfm_umma_tiles_max(L.I, TK, E, nt), mdn = (uint32_t)lfm_umma_tiles_max(L.D, TK, E, nt);
-        LFM_CUDA(h, timed(h, K_PLAN, s, [&] {
-            cudaError_t e = lfm_launch_umma_plan(w.rt, L.I, nt, w.utiles_gu, w.utbs, w.ucounts, mgu, mtb, s);
-            return e == cudaSuccess ? lfm_launch_umma_plan(w.rt, L.D, nt, w.utiles_dn, w.utbs, w.ucounts + 2, mdn, mtb, s)
-                                    : e;
-        }, 2));
+    if (plan.nt) { /* the dispatch step built the tile plans */
+        const uint32_t TK = T * K, E = lfm_layer_E(L), nt = plan.nt, mtb = plan.max_tb;
         LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
-        LFM_CUDA(h, timed(h, K_GEMM_G, s, [&] {
-            return lfm_launch_q4k_umma(L.gate, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.rt.err, grid, s);
-        }));
-        LFM_CUDA(h, timed(h, K_GEMM_U, s, [&] {
-            return lfm_launch_q4k_umma(L.up, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.u, w.rt.err, grid, s);
+        LFM_CUDA(h, timed(h, K_GEMM_GU, s, [&] { /* gate and up in one launch */
+            return lfm_launch_q4k_umma(L.gate, L.up, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
+                                       w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, TK, L.I, hq, s); }));
         LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(hq, nullptr, 1, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
-            return lfm_launch_q4k_umma(L.down, E, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.rt.err, grid, s);
+            return lfm_launch_q4k_umma(L.down, L.down, E, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.y,
+                                       w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
         return LFM_GPU_OK;
@@ -377,9 +389,11 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
         LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
         return LFM_GPU_OK;
     }
-    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, w.rt, s, pdl); },
+    RouteTables rt = w.rt;
+    rt.plan = umma_plan_for(h, L, T);
+    LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, xq, rt, s, pdl); },
                       lfm_route_kernels(L, T)));
-    return run_experts(h, L, x, T, xq, s, pdl);
+    return run_experts(h, L, x, T, xq, s, pdl, rt.plan);
 }
 
 lfm_gpu_status_t read_device_error(lfm_gpu_moe_t *h) {
@@ -1049,9 +1063,11 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer
     h->stats.kernels_launched = 3; /* + those of run_experts */
     LFM_CUDA(h, lfm_launch_gguf_to_q8(static_cast<const uint8_t *>(q8_in), n_rows, xq, s));
     LFM_CUDA(h, lfm_launch_ep_prepare(expert_ids, n_rows, first, count, w.rt, s));
-    LFM_CUDA(h, lfm_launch_dispatch(Lx, n_rows, w.rt, s));
+    RouteTables rt = w.rt;
+    rt.plan = umma_plan_for(h, Lx, n_rows);
+    LFM_CUDA(h, lfm_launch_dispatch(Lx, n_rows, rt, s));
     LFM_CUDA(h, cudaMemsetAsync(y_out, 0, sizeof(float) * n_rows * Lx.D, s));
-    return run_experts(h, Lx, y_out, n_rows, xq, s, false); /* y_out = fma(1, y, 0) = y */
+    return run_experts(h, Lx, y_out, n_rows, xq, s, false, rt.plan); /* y_out = fma(1, y, 0) = y */
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,

@@ -38,6 +38,27 @@ struct Q8Rows {
     uint32_t cols;
 };
 
+/* tcgen05 GEMM work (k_umma.cu): a tile is weight rows [row0, row0 + 128) of
+ * `expert` in matrix `mat` (0: gate or down, 1: up) against token block `tb`;
+ * a token block is dispatch slots [slot0, slot0 + ntok), ntok <= nt. */
+struct LfmUTile {
+    int32_t expert, tb, row0, mat;
+};
+struct LfmUTokBlock {
+    int32_t slot0, ntok;
+};
+/* Tile plans the dispatch step writes for the tcgen05 GEMMs (nt == 0: none):
+ * token blocks of <= nt slots per active expert, then tiles (expert, 128-row
+ * block, token block, matrix) with the matrix and then the token blocks
+ * fastest: one plan covers gate and up together, one the down rows.
+ * counts = {tiles gu, blocks, tiles dn, blocks}. */
+struct UmmaPlanOut {
+    LfmUTile *tiles_gu, *tiles_dn;
+    LfmUTokBlock *tbs;
+    int32_t *counts;
+    uint32_t rows_gu, rows_dn, nt, max_gu, max_dn, max_tb;
+};
+
 /* Routing / dispatch tables for one forward (all device pointers). */
 struct RouteTables {
     int32_t *idx;        /* [T*K] expert id of assignment a = t*K + k                   */
@@ -55,6 +76,7 @@ struct RouteTables {
     float *rms;          /* [T]   1/rms of x (the prefill router's two passes)            */
     uint32_t *err;       /* device error word                                            */
     unsigned long long *loads; /* [2] running sum of unique experts, MoE layer runs      */
+    UmmaPlanOut plan;    /* tcgen05 GEMM tile plans to build with the dispatch (nt == 0: none) */
 };
 
 struct MoeLayerDev {
@@ -132,17 +154,14 @@ bool lfm_umma_ok(uint32_t rows);
 uint32_t lfm_umma_nt(uint32_t slots, uint32_t experts);
 size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts, uint32_t nt);
 size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint32_t nt);
-size_t lfm_umma_tile_bytes();
-size_t lfm_umma_tb_bytes();
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt);
-cudaError_t lfm_launch_umma_plan(const RouteTables &rt, uint32_t rows, uint32_t nt, void *tiles, void *tbs,
-                                 int32_t *counts, uint32_t max_tiles, uint32_t max_tb, cudaStream_t s);
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
-/* W: `experts` tensors [rows][cols/256] Q4_K back to back */
-cudaError_t lfm_launch_q4k_umma(const uint8_t *W, uint32_t experts, uint32_t rows, uint32_t cols, const uint8_t *xt,
-                                uint32_t nt, const void *tiles, const void *tbs, const int32_t *n_tiles, float *Y,
-                                uint32_t *err, int grid, cudaStream_t s);
+/* W0, W1: `experts` tensors [rows][cols/256] Q4_K back to back (tiles of
+ * matrix m read Wm and write Ym; W1/Y1 may repeat W0/Y0 when every tile has m = 0) */
+cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
+                                const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
+                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s);
 
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
