@@ -622,6 +622,71 @@ __global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm
     }
 }
 
+/* Q8_K of one 256-value block held 8 per lane (elements 8*lane..) -- the
+ * quantiser of lfm_quant_block_warp, value for value -- written as token t of
+ * a pre-gathered block (the layout k_xt_gather writes). */
+__device__ __forceinline__ void quant_block_xt(const float v[8], uint8_t *dst, uint32_t nt, uint32_t t) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = lfm_warp_max(amax);
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int part = 0;
+    if (amax != 0.0f) {
+        const float s = __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { q[i] = __float2int_rn(__fmul_rn(v[i], s)); part += q[i]; }
+    }
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[i])) << (8 * i);
+        hi |= (uint32_t)(uint8_t)(int8_t)max(-128, min(127, q[4 + i])) << (8 * i);
+    }
+    /* elements 8*lane..8*lane+7: half (8*lane)/128, 16-byte K chunk ((8*lane) % 128) / 16, bytes 8*(lane & 1).. */
+    const uint32_t k = 8u * lane;
+    *reinterpret_cast<uint2 *>(dst + (k >> 7) * nt * kHalf + ((k & 127) >> 4) * 16 * nt + 16 * t + (k & 15)) =
+        make_uint2(lo, hi);
+    /* sub-block sums (32 codes, unsaturated): lanes 4j..4j+3; pairs (2i, 2i+1) packed per word */
+    int sum4 = part + __shfl_xor_sync(LFM_FULL_MASK, part, 1);
+    sum4 += __shfl_xor_sync(LFM_FULL_MASK, sum4, 2);
+    const int odd = __shfl_down_sync(LFM_FULL_MASK, sum4, 4);
+    if ((lane & 7) == 0)
+        reinterpret_cast<uint32_t *>(dst + 2 * nt * kHalf + nt * 4 + 16 * t)[lane >> 3] =
+            (uint32_t)(uint16_t)sum4 | ((uint32_t)(uint16_t)odd << 16);
+    if (lane == 0) reinterpret_cast<float *>(dst + 2 * nt * kHalf)[t] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
+}
+
+/* h = (g / (1 + exp(-g))) * u (tools/lfm2_decode_1x4.c:976-985), quantised to
+ * Q8_K per 256 and written straight into the down GEMM's pre-gathered token
+ * blocks (the slots of a block are consecutive); one warp per (token, 256
+ * block), eight tokens of a token block per CTA. */
+__global__ void __launch_bounds__(256) k_swiglu_xt(const float *__restrict__ G, const float *__restrict__ U,
+                                                   uint32_t cols, const UTokBlock *tbs, const int32_t *n_tb,
+                                                   uint32_t nt, uint8_t *xt) {
+    const int tb = blockIdx.x / (nt / 8);
+    if (tb >= __ldcg(n_tb)) return;
+    const uint32_t sb = blockIdx.y, nb = cols / 256;
+    const UTokBlock blk = tbs[tb];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *dst = xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt);
+    {
+        const uint32_t t = (blockIdx.x % (nt / 8)) * 8 + warp;
+        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if ((int)t < blk.ntok) {
+            const size_t o = (size_t)(blk.slot0 + t) * cols + 256 * sb + 8 * lane;
+            const float4 g0 = __ldcg(reinterpret_cast<const float4 *>(G + o)), g1 = __ldcg(reinterpret_cast<const float4 *>(G + o) + 1);
+            const float4 u0 = __ldcg(reinterpret_cast<const float4 *>(U + o)), u1 = __ldcg(reinterpret_cast<const float4 *>(U + o) + 1);
+            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, lfm_expf(-g[i]))), u[i]);
+        }
+        quant_block_xt(v, dst, nt, t);
+    }
+}
+
 }  // namespace
 
 bool lfm_umma_ok(uint32_t rows) { return rows % kM == 0; }
@@ -671,6 +736,14 @@ bool lfm_tmap_2d(CUtensorMap *tm, CUtensorMapDataType type, uint32_t elem_bytes,
     return encode(tm, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
+    const uint32_t nb = cols / 256;
+    if (max_tb == 0 || nb == 0) return cudaSuccess;
+    k_swiglu_xt<<<dim3(max_tb * (nt / 8), nb), 256, 0, s>>>(G, U, cols, static_cast<const UTokBlock *>(tbs), n_tb, nt, xt);
+    return cudaGetLastError();
 }
 
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,

@@ -339,8 +339,7 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
             return lfm_launch_q4k_umma(L.gate, L.up, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
                                        w.rt.err, grid, s);
         }));
-        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, TK, L.I, hq, s); }));
-        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(hq, nullptr, 1, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
             return lfm_launch_q4k_umma(L.down, L.down, E, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.y,
                                        w.rt.err, grid, s);

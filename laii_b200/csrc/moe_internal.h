@@ -157,6 +157,9 @@ size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint3
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt);
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+/* SwiGLU of the gate|up outputs, Q8_K, written as the down GEMM's token blocks */
+cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
 /* W0, W1: `experts` tensors [rows][cols/256] Q4_K back to back (tiles of
  * matrix m read Wm and write Ym; W1/Y1 may repeat W0/Y0 when every tile has m = 0) */
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
