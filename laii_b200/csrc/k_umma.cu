@@ -17,23 +17,23 @@
  * Tile: 128 weight rows (MMA M) x nt tokens (MMA N, nt = 16..128 chosen per
  * call from the tokens per expert) of one expert; K walked in half
  * super-blocks (128 bytes).  One CTA per SM, persistent over the tile
- * list, warp-specialised:
- *   warps 0-7   epilogue: TMEM -> registers (tcgen05.ld 32x32b), the fp32
- *               update above into <= 64 running sums per thread (thread =
- *               row, warp pair = the tile's two token halves), Y at the end;
- *   warps 8-11  producers: the tile's 128 Q4_K rows of a super-block arrive
- *               by one 2-D tensor copy (TMA tile 144 bytes x 128 rows, ring of
- *               3 super-blocks); thread p expands row p's nibbles into A1/A2 in
- *               the UMMA canonical K-major layout (8-row x 16-byte core
- *               matrices) and publishes d, dmin, m_j;
- *   warp 12     TMEM allocation and the MMA issue (one thread): per half
- *               super-block 4 K-steps x (A1 -> D1, A2 -> D2), commits release
- *               the shared-memory stages and hand a finished accumulator pair
- *               to the epilogue.  D1/D2 are double buffered (2 x 256 columns),
- *               so super-block b+1 multiplies while b drains;
- *   warp 13     loader (one thread): the tokens' codes and scales for each
- *               half super-block, pre-gathered by k_xt_gather into the same
- *               canonical layout, one bulk copy each.
+ * list, warp-specialised (counts per arrangement in UCfg below):
+ *   epilogue    TMEM -> registers (tcgen05.ld 32x32b), the fp32 update above
+ *               into running sums (thread = row; the warps of a TMEM lane
+ *               quarter split the tile's tokens), Y at the end;
+ *   producers   the tile's 128 Q4_K rows of a super-block arrive by one 2-D
+ *               tensor copy (TMA tile 144 bytes x 128 rows, a ring of
+ *               super-blocks); a thread expands its row's nibbles into the
+ *               UMMA canonical K-major layout (8-row x 16-byte core matrices)
+ *               and publishes d, dmin and the 6-bit scales and mins;
+ *   2 MMA warps TMEM allocation (the first) and the MMA issue (one thread
+ *               each, independent accumulators); commits release the stages
+ *               and hand a finished accumulator buffer to the epilogue.
+ *               Accumulators are double buffered, so super-block b+1
+ *               multiplies while b drains;
+ *   loader      one thread: the tokens' codes and scales for each half
+ *               super-block, pre-gathered (k_xt_gather, k_swiglu_xt) into the
+ *               same canonical layout, one bulk copy each.
  * Every mbarrier wait is bounded; on a timeout the CTA raises the device error
  * word, every role leaves its loop, the CTA waits out copies and MMAs in
  * flight and frees its tensor memory before it exits.
@@ -65,9 +65,10 @@ constexpr uint32_t kTmemCols = 512;
 /* Two arrangements of the same pipeline.
  *  prefill (kDec = false, nt > 32): A1 = b*q4 and A2 = a*q4 in shared memory,
  *    acc = D1 + 16*D2 accumulated over the super-block by the tensor core
- *    (16 MMAs a super-block); 8 epilogue warps (two per TMEM lane quarter,
- *    half of the tokens each), 4 producer warps (one row each, both halves of
- *    a super-block); TMEM: D1/D2 for nt <= 128, double buffered.
+ *    (16 MMAs a super-block, the two MMA warps issuing A1 and A2); 16
+ *    epilogue warps (four per TMEM lane quarter, a quarter of the tokens
+ *    each), 4 producer warps (one row each, both halves of a super-block);
+ *    TMEM: D1/D2 for nt <= 128, double buffered.
  *  decode (kDec = true, nt <= 32): A = the raw nibbles as bytes and one
  *    accumulator per sub-block, D_j = q4 . q8 over its 32 K, so a super-block
  *    takes 8 MMAs; the epilogue forms acc = sum_j sc_j * D_j (exact).  At few
@@ -77,7 +78,7 @@ constexpr uint32_t kTmemCols = 512;
  *    raw-weight ring; TMEM: 8 accumulators x 32 columns, double buffered. */
 template <bool kDec>
 struct UCfg {
-    static constexpr int kEpi = kDec ? 4 : 8;
+    static constexpr int kEpi = kDec ? 4 : 16;
     static constexpr int kProd = kDec ? 8 : 4;
     static constexpr int kSR = kDec ? 5 : 3;                   /* raw weight ring (super-blocks)      */
     static constexpr int kSA = kDec ? 4 : 3;  /* A stages: decode 2 per half super-block, prefill 3 shared */
@@ -98,8 +99,6 @@ struct UCfg {
 };
 constexpr uint32_t kNtDecode = 32; /* largest token block of the decode arrangement */
 static_assert(UCfg<false>::kSmem <= 227 * 1024 && UCfg<true>::kSmem <= 227 * 1024, "shared memory");
-static_assert(UCfg<false>::kThreads == UCfg<true>::kThreads, "one block size");
-constexpr int kThreads = UCfg<false>::kThreads;
 
 /* Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A u8 (7-9 = 0),
  * B s8 (10-12 = 1), both K-major, M >> 4 at bits 24-28; N >> 3 goes to 17-22. */
@@ -230,7 +229,7 @@ __device__ __forceinline__ bool uwait(uint64_t *bar, uint32_t parity, volatile i
 }
 
 template <bool kDec>
-__global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw0,
+__global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw0,
                                                           const __grid_constant__ CUtensorMap tmw1, UmmaArgs A) {
     using C = UCfg<kDec>;
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -320,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
 
     if (warp < C::kEpi) {
         /* ---------------- epilogue ---------------- */
-        constexpr int kCols = kDec ? (int)kNtDecode : kN / 2; /* most columns of one warp */
+        constexpr int kCols = kDec ? (int)kNtDecode : kN / (C::kEpi / 4); /* most columns of one warp */
         const int q4 = warp & 3, ch = warp >> 2;
         const int r = 32 * q4 + lane;
         const int half = (int)A.nt / (C::kEpi / 4); /* columns of this warp: [ch * half, ch * half + half) */
@@ -353,11 +352,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
 #pragma unroll
                     for (int j = 0; j < 8; ++j) sc[j] = (int)(((j < 4 ? r2.x : r2.y) >> (8 * (j & 3))) & 0xFFu);
                 }
+                constexpr int kStep = 8; /* columns per TMEM round trip */
 #pragma unroll
-                for (int c = 0; c < kCols / 8; ++c) {
-                    if (8 * c < nv) { /* warp-uniform */
-                        const uint32_t col = buf * C::kDbuf + (uint32_t)(ch * half) + 8u * c;
-                        int acc[8];
+                for (int c = 0; c < kCols / kStep; ++c) {
+                    if (kStep * c < nv) { /* warp-uniform */
+                        const uint32_t col = buf * C::kDbuf + (uint32_t)(ch * half) + (uint32_t)(kStep * c);
+                        int acc[kStep];
                         if constexpr (kDec) {
                             /* acc = sum_j sc_j * D_j, D_j at column block 32 j */
                             uint32_t v[8][8];
@@ -384,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
                         /* S = fma(d8*d, acc, fma(-(d8*dmin), mins, S)), two tokens a step; a d8 == 0
                          * block has acc = mins = 0 (all its codes are 0) and adds exact zeros */
 #pragma unroll
-                        for (int i = 0; i < 8; i += 2) {
-                            const int t = 8 * c + i;
+                        for (int i = 0; i < kStep; i += 2) {
+                            const int t = kStep * c + i;
                             const float2 d8 = *reinterpret_cast<const float2 *>(d8s + t);
                             const uint64_t d8p = pk2(d8.x, d8.y);
                             const int m0 = mins_of(bps[t], ri.z, ri.w), m1 = mins_of(bps[t + 1], ri.z, ri.w);
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_q4k_umma(const __grid_constant_
                 }
             }
             if (!ok) break;
-            float *yb = A.Y[tile.mat] + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
+            float *yb = (tile.mat ? A.Y[1] : A.Y[0]) + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
 #pragma unroll
             for (int t = 0; t < kCols; ++t)
                 if (t < nv) yb[(size_t)t * A.rows] = S[t];
@@ -766,12 +766,12 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<true>, UCfg<true>::kSmem, cache);
         if (e != cudaSuccess) return e;
-        k_q4k_umma<true><<<grid, kThreads, UCfg<true>::kSmem, s>>>(tm0, tm1, a);
+        k_q4k_umma<true><<<grid, UCfg<true>::kThreads, UCfg<true>::kSmem, s>>>(tm0, tm1, a);
     } else {
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<false>, UCfg<false>::kSmem, cache);
         if (e != cudaSuccess) return e;
-        k_q4k_umma<false><<<grid, kThreads, UCfg<false>::kSmem, s>>>(tm0, tm1, a);
+        k_q4k_umma<false><<<grid, UCfg<false>::kThreads, UCfg<false>::kSmem, s>>>(tm0, tm1, a);
     }
     return cudaGetLastError();
 }
