@@ -347,6 +347,8 @@ def run_ours(args, cfg):
                "gpu_launches": kernels_per_step * args.steps,
                "clocks": clk}
         print(json.dumps(out), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()  # no rank frees its arena while another may still write into it
     g.close()
     if ws > 1:
         torch.distributed.destroy_process_group()
@@ -392,7 +394,8 @@ def stack_cpu_baseline(cfg, seconds, threads=0):
 def run_stack(args, cfg):
     """Configs 4 and 5: a stack of FFN layers, T tokens in total per step (strong scaling over ranks).
     One GPU: the stack as one captured forward.  N GPUs with --ep: experts sharded across ranks,
-    each rank's T/N tokens routed and exchanged with NCCL all-to-all (laii_b200.ep)."""
+    each rank's T/N tokens routed and exchanged by the library's peer-memory kernels (--ep-comm p2p,
+    the default) or NCCL all-to-all driven from Python (--ep-comm nccl, laii_b200.ep.ep_forward)."""
     import torch
     ws, rank, local = dist_setup()
     torch.cuda.set_device(local)
@@ -419,11 +422,14 @@ def run_stack(args, cfg):
         else:
             g.synth_layer(l, D, E, K, I, layer_seeds(l))
     g.reserve(max(Tl * K if use_ep else Tl, Tl))
+    p2p = use_ep and args.ep_comm == "p2p"
+    if p2p:  # the library's own exchange kernels over peer memory; torch.distributed carries the IPC handles
+        ep.p2p_connect(g, Tl, D, E, K, I)
     x0 = synth.make_hidden(Tl, D, seed_offset=rank * Tl)
     x = torch.from_numpy(x0.copy()).cuda()
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
-    comm = ep.TorchComm() if use_ep else None
+    comm = ep.TorchComm() if use_ep and not p2p else None
     ops = ep.GpuOps(g, D, K) if use_ep else None
 
     def step():
@@ -433,8 +439,12 @@ def run_stack(args, cfg):
         for kind, l in layers:
             if kind == "dense":
                 g.forward_device(l, x.data_ptr(), Tl, stream=sp)
+            elif p2p:
+                g.ep_p2p_forward(l, x.data_ptr(), Tl, sp)
             else:
                 ep.ep_forward(ops, comm, l, x, E, K)
+            if p2p:
+                ops.launches += g.last_stats()["kernels_launched"]
 
     for _ in range(args.warmup):
         step()
@@ -529,7 +539,8 @@ def run_stack(args, cfg):
                "config": {"workload": f"cfg{args.config}: {cfg['name']} ({n_dense} dense + {n_moe} lfm2moe FFN layers, "
                                       f"D={D} E={E} top-{K} I={I}, {T} tokens per step in total)",
                           "tokens_per_step": T, "layers": len(layers),
-                          "parallelism": f"expert-parallel x{ws} (E/{ws} experts per rank, NCCL all-to-all)"
+                          "parallelism": (f"expert-parallel x{ws} (E/{ws} experts per rank, "
+                                          + ("exchange kernels over NVLink peer memory)" if p2p else "NCCL all-to-all)"))
                           if use_ep else ("single" if ws == 1 else f"replicas x{ws}"),
                           "l2": "the stack's weights exceed the 126 MB L2; every step streams them from HBM",
                           "unique_experts_per_moe_layer": loads / args.steps / n_moe},
@@ -537,6 +548,8 @@ def run_stack(args, cfg):
                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
                "gpu_launches": launches_per_step * args.steps, "clocks": clk}
         print(json.dumps(out), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()  # no rank frees its arena while another may still write into it
     g.close()
     if ws > 1:
         torch.distributed.destroy_process_group()
@@ -549,6 +562,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--ep", action="store_true", help="configs 4/5 under torchrun: expert parallelism")
+    ap.add_argument("--ep-comm", default="p2p", choices=["p2p", "nccl"],
+                    help="--ep exchange: the library's peer-memory kernels (p2p) or torch all_to_all over NCCL")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ring", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -150,6 +150,54 @@ lfm_gpu_status_t lfm_gpu_moe_ep_experts(lfm_gpu_moe_t *h, uint32_t layer, const 
 lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T, const float *w,
                                         const float *y, void *stream);
 
+/* ---- expert parallelism over peer memory (NVLink / NVSwitch) -------------
+ * The same layer step as ep_route -> exchange -> ep_experts -> exchange ->
+ * ep_combine, with the two exchanges done by the library's own kernels
+ * through CUDA IPC mappings of every rank's exchange arena: no host
+ * synchronisation, no collective library call.  Per layer:
+ *   home rank: route, publish its per-expert counts to every rank;
+ *   expert rank: wait for every rank's counts (bounded), plan, gather the
+ *     Q8_K rows of its experts from the home ranks' memory, gate/up, SwiGLU,
+ *     down, store each output row into its home rank's arena, signal;
+ *   home rank: wait for every expert rank's signal (bounded), combine in the
+ *     reference's k order (tools/lfm2_moe_checkpoint.c:266-269).
+ * Every rank calls lfm_gpu_moe_ep_p2p_forward for the same layers in the same
+ * order (T may differ per rank, 0 included).  A wait that runs out sets
+ * LFM_GPU_ERR_TIMEOUT at the next lfm_gpu_moe_sync; the ranks are then out of
+ * step and must detach and attach again.  The layer must be the rank's shard:
+ * experts [first, first + n) with (first, n) as in the host-side shard_of
+ * (the first E % world ranks hold one expert more). */
+#define LFM_GPU_MOE_EP_MAX_RANKS 8
+#define LFM_GPU_MOE_IPC_HANDLE_BYTES 64
+
+/* Step 1 (every rank): allocate this rank's exchange arena for up to
+ * max_tokens tokens per rank and layers of shape D, E, K, I, and return its
+ * IPC handle (LFM_GPU_MOE_IPC_HANDLE_BYTES opaque bytes) for the other ranks.
+ * wait_ms bounds every device wait on another rank (0: 5000 ms).
+ * No counterpart in the reference (its MoE runs on one host). */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_attach(lfm_gpu_moe_t *h, int rank, int world, uint32_t max_tokens, uint32_t D,
+                                           uint32_t E, uint32_t K, uint32_t I, uint32_t wait_ms,
+                                           void *ipc_handle_out);
+
+/* Step 2 (every rank, after every rank's attach returned): map the other
+ * ranks' arenas; handles[r] is rank r's handle from step 1, in rank order. */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_connect(lfm_gpu_moe_t *h, const void *handles);
+
+/* x[T][D] += MoE(x) for this rank's tokens (device x), experts spread over
+ * the ranks.  Asynchronous on `stream`. */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T, void *stream);
+
+/* A check of the bounded-wait path: one device wait for a step that no rank
+ * will ever signal, bounded by attach's wait_ms.  The next lfm_gpu_moe_sync
+ * returns LFM_GPU_ERR_TIMEOUT and the handle stays usable (the step counter
+ * does not move).  Asynchronous on `stream`.  No counterpart in the reference. */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_wait_check(lfm_gpu_moe_t *h, void *stream);
+
+/* Unmap the peers and free the arena (after a device sync; every rank detaches
+ * before any rank frees the memory another still reads: the caller puts a
+ * barrier between the last forward and detach). */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_detach(lfm_gpu_moe_t *h);
+
 /* Reserve scratch for up to max_tokens tokens per forward (forward grows it on
  * demand; reserve first when the forward is to be captured in a CUDA graph). */
 lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens);

@@ -46,6 +46,11 @@ GPU_API = [
     ("lfm_gpu_moe_ep_route", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_ep_experts", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_ep_combine", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_attach", c_int, [c_vp, c_int, c_int, c_u32, c_u32, c_u32, c_u32, c_u32, c_u32, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_connect", c_int, [c_vp, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_wait_check", c_int, [c_vp, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_detach", c_int, [c_vp]),
     ("lfm_gpu_moe_reserve", c_int, [c_vp, c_u32]),
     ("lfm_gpu_moe_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_int, c_vp]),
     ("lfm_gpu_moe_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_int, c_vp]),

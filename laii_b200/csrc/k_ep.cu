@@ -1,0 +1,134 @@
+/*
+ * Expert parallelism over peer memory: the exchange kernels.
+ *
+ * One process per GPU; every rank's exchange arena is mapped into every other
+ * rank (CUDA IPC over NVLink / NVSwitch), so the two all-to-all steps of a
+ * layer are loads and stores of the kernels themselves:
+ *   k_ep_publish       home rank: its per-expert counts into every rank's
+ *                      count table, then its cnt_flag there (release);
+ *   (k_ep_plan, k_route.cu; k_xt_gather_ep, k_umma.cu: the expert rank lays
+ *    out the received slots and gathers their Q8_K rows from the home ranks)
+ *   k_ep_push          expert rank: each output row straight into its home
+ *                      rank's yhome[t*K + k]; the last CTA raises y_flag on
+ *                      every rank (release);
+ *   k_ep_combine_wait  home rank: acquire every y_flag, then
+ *                      x[t] = fma(w[t][k], yhome[t*K+k], x[t]) for k in order
+ *                      (tools/lfm2_moe_checkpoint.c:266-269).
+ * Flags hold the epoch of the layer step; waits compare wrap-safe and are
+ * bounded by EpStep::wait_ns (LFM_DEVERR_TIMEOUT, then the kernel returns).
+ * Buffer reuse needs no further handshake: a home rank overwrites its Q8_K
+ * rows, perm and count-table entries for step n+1 only after its combine of
+ * step n saw every expert rank's y_flag, which each raises after it gathered
+ * and computed step n; an expert rank writes yhome rows of step n+1 only after
+ * every home rank published step n+1, i.e. after that rank's combine of step
+ * n read them.  The count table alternates by epoch parity because a home rank
+ * can publish step n+1 while a slower expert rank still plans step n.
+ */
+#include "moe_device.cuh"
+#include "moe_internal.h"
+
+namespace {
+
+__global__ void __launch_bounds__(256) k_ep_publish(EpStep st, const int32_t *__restrict__ counts) {
+    const size_t row = ((size_t)(st.epoch & 1u) * LFM_EP_MAX_RANKS + st.rank) * st.E;
+    for (uint32_t q = threadIdx.x; q < st.world * st.E; q += blockDim.x) {
+        const uint32_t p = q / st.E, e = q - p * st.E;
+        st.table[p][row + e] = __ldcg(counts + e);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < st.world) lfm_st_release_sys(st.cnt_flag[threadIdx.x] + st.rank, st.epoch);
+}
+
+/* One warp per received row: D fp32 from this rank's y to the home rank's
+ * yhome row (peer stores, 16 bytes a lane, four in flight). */
+__global__ void __launch_bounds__(256) k_ep_push(EpStep st, const float *__restrict__ y) {
+    __shared__ float *yh[LFM_EP_MAX_RANKS];
+    if (threadIdx.x < LFM_EP_MAX_RANKS) yh[threadIdx.x] = threadIdx.x < st.world ? st.yhome[threadIdx.x] : nullptr;
+    __syncthreads();
+    const int n = __ldcg(st.self.n_recv);
+    const uint32_t lane = threadIdx.x & 31, D4 = st.D / 4;
+    const uint32_t nw = gridDim.x * (blockDim.x >> 5);
+    for (uint32_t j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < (uint32_t)n; j += nw) {
+        const uint32_t v = __ldcg(st.self.ret + j), r = v >> 24, a = v & 0xffffffu;
+        if (r >= st.world || a >= st.max_assign) {
+            if (lane == 0) atomicOr(st.err, LFM_DEVERR_SEGMENT);
+            continue;
+        }
+        const float4 *src = reinterpret_cast<const float4 *>(y + (size_t)j * st.D);
+        float4 *dst = reinterpret_cast<float4 *>(yh[r] + (size_t)a * st.D);
+        uint32_t c = lane;
+        for (; c + 96 < D4; c += 128) {
+            const float4 v0 = __ldcg(src + c), v1 = __ldcg(src + c + 32), v2 = __ldcg(src + c + 64),
+                         v3 = __ldcg(src + c + 96);
+            dst[c] = v0;
+            dst[c + 32] = v1;
+            dst[c + 64] = v2;
+            dst[c + 96] = v3;
+        }
+        for (; c < D4; c += 32) dst[c] = __ldcg(src + c);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(st.self.done, 1u);
+        if (prev == gridDim.x - 1) { /* every CTA's stores are fenced before its count */
+            atomicExch(st.self.done, 0u);
+            __threadfence_system();
+            for (uint32_t p = 0; p < st.world; ++p) lfm_st_release_sys(st.y_flag[p] + st.rank, st.epoch);
+        }
+    }
+}
+
+/* x[t][c..c+3] = fma(w[t][k], yhome[t*K+k][c..c+3], x) for k = 0..K-1 in order. */
+__global__ void __launch_bounds__(256) k_ep_combine_wait(EpStep st, float *__restrict__ x, uint32_t T,
+                                                         const float *__restrict__ w) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.y_flag, st.world, st.epoch, st.wait_ns, st.err) ? 1 : 0;
+    __syncthreads();
+    if (!ok) return;
+    const uint32_t D4 = st.D / 4, K = st.K;
+    const float *y = st.self.yhome;
+    const uint64_t n = (uint64_t)T * D4;
+    for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n; q += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t t = q / D4, c = q - t * D4;
+        float4 acc = reinterpret_cast<float4 *>(x)[q];
+        for (uint32_t k = 0; k < K; ++k) {
+            const float wk = __ldg(w + t * K + k);
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(y + (t * K + k) * st.D) + c);
+            acc.x = __fmaf_rn(wk, v.x, acc.x);
+            acc.y = __fmaf_rn(wk, v.y, acc.y);
+            acc.z = __fmaf_rn(wk, v.z, acc.z);
+            acc.w = __fmaf_rn(wk, v.w, acc.w);
+        }
+        reinterpret_cast<float4 *>(x)[q] = acc;
+    }
+}
+
+}  // namespace
+
+cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaStream_t s) {
+    if (st.world == 0 || st.world > LFM_EP_MAX_RANKS) return cudaErrorInvalidValue;
+    k_ep_publish<<<1, 256, 0, s>>>(st, counts);
+    return cudaGetLastError();
+}
+
+cudaError_t lfm_launch_ep_push(const EpStep &st, const float *y, uint32_t max_recv, int grid, cudaStream_t s) {
+    if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.D % 4) return cudaErrorInvalidValue;
+    uint32_t blocks = (max_recv + 7) / 8; /* eight rows (warps) per CTA */
+    const uint32_t cap = (uint32_t)grid * 4;
+    if (blocks > cap) blocks = cap;
+    if (blocks == 0) blocks = 1;
+    k_ep_push<<<blocks, 256, 0, s>>>(st, y);
+    return cudaGetLastError();
+}
+
+cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, cudaStream_t s) {
+    if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.D % 4) return cudaErrorInvalidValue;
+    const uint64_t n = (uint64_t)T * (st.D / 4);
+    uint64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks == 0) blocks = 1; /* T == 0 still waits: no rank runs ahead of the step */
+    k_ep_combine_wait<<<(unsigned)blocks, 256, 0, s>>>(st, x, T, w);
+    return cudaGetLastError();
+}

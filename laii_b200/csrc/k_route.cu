@@ -515,7 +515,88 @@ __global__ void __launch_bounds__(256) k_dispatch_only(MoeLayerDev L, uint32_t T
     route_dispatch(L, T, rt, s);
 }
 
+/* Expert parallelism, expert rank: wait for every home rank's per-expert
+ * counts, then lay out the received slots -- local expert el, then home rank
+ * r, then r's own slot order -- as the dispatch tables of the shard (counts,
+ * offsets, active experts, tcgen05 tile plans) plus rowmap[slot] = (r << 24)
+ * | r's slot, which the gather reads r's perm and Q8_K rows through.  The
+ * home rank's slot of its i-th assignment to expert e is its exclusive
+ * prefix of counts before e, plus i (route_dispatch's slot order). */
+__global__ void __launch_bounds__(1024) k_ep_plan(EpStep st, uint32_t first, uint32_t count, RouteTables rt) {
+    __shared__ RouteSmem s;
+    __shared__ int tab[LFM_EP_MAX_RANKS][LFM_GPU_MAX_EXPERTS_DEV];
+    __shared__ int pre[LFM_EP_MAX_RANKS][LFM_GPU_MAX_EXPERTS_DEV];  /* home ranks before r, per local expert */
+    __shared__ int hoff[LFM_EP_MAX_RANKS][LFM_GPU_MAX_EXPERTS_DEV]; /* r's first slot of expert first + el */
+    __shared__ int ok;
+    const UmmaPlanOut &P = rt.plan;
+    const uint32_t W = st.world, E = st.E;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.cnt_flag, W, st.epoch, st.wait_ns, st.err) ? 1 : 0;
+    __syncthreads();
+    if (!ok) {
+        if (threadIdx.x < 4) P.counts[threadIdx.x] = 0;
+        if (threadIdx.x == 0) *st.self.n_recv = 0;
+        return;
+    }
+    const int32_t *t0 = st.self.table + (size_t)(st.epoch & 1u) * LFM_EP_MAX_RANKS * E;
+    for (uint32_t q = threadIdx.x; q < W * E; q += blockDim.x) tab[q / E][q % E] = lfm_ld_relaxed_sys(t0 + q);
+    __syncthreads();
+    if (threadIdx.x < W) { /* home rank r's slot prefix up to each of this shard's experts */
+        const uint32_t r = threadIdx.x;
+        int acc = 0;
+        for (uint32_t e = 0; e < first; ++e) acc += tab[r][e];
+        for (uint32_t el = 0; el < count; ++el) {
+            hoff[r][el] = acc;
+            acc += tab[r][first + el];
+        }
+    }
+    if (threadIdx.x >= 32 && threadIdx.x - 32 < count) {
+        const uint32_t el = threadIdx.x - 32;
+        int acc = 0;
+        for (uint32_t r = 0; r < W; ++r) {
+            pre[r][el] = acc;
+            acc += tab[r][first + el];
+        }
+        s.cnt[el] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0, uniq = 0;
+        for (uint32_t el = 0; el < count; ++el) {
+            s.off[el] = acc;
+            acc += s.cnt[el];
+            if (s.cnt[el] > 0) s.act[uniq++] = (int)el;
+        }
+        s.off[count] = acc;
+        s.uniq = uniq;
+        s.bad = acc < 0 || (uint32_t)acc > st.max_recv;
+        if (s.bad) atomicOr(st.err, LFM_DEVERR_SEGMENT);
+        *st.self.n_recv = s.bad ? 0 : acc;
+        if (rt.loads) { rt.loads[0] += (unsigned long long)uniq; rt.loads[1] += 1ull; }
+    }
+    __syncthreads();
+    if (s.bad) {
+        if (threadIdx.x < 4) P.counts[threadIdx.x] = 0;
+        return;
+    }
+    for (uint32_t q = warp; q < count * W; q += nwarps) { /* (local expert, home rank) runs of slots */
+        const uint32_t el = q / W, r = q % W;
+        const int n = tab[r][first + el], dst = s.off[el] + pre[r][el], src = hoff[r][el];
+        for (int i = lane; i < n; i += 32) st.self.rowmap[dst + i] = (r << 24) | (uint32_t)(src + i);
+    }
+    route_plan(rt, s);
+}
+
 }  // namespace
+
+cudaError_t lfm_launch_ep_plan(const EpStep &st, uint32_t first, uint32_t count, const RouteTables &rt,
+                               cudaStream_t s) {
+    if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.E > LFM_GPU_MAX_EXPERTS_DEV || count > st.E ||
+        first + count > st.E || !rt.plan.nt)
+        return cudaErrorInvalidValue;
+    k_ep_plan<<<1, 1024, 0, s>>>(st, first, count, rt);
+    return cudaGetLastError();
+}
 
 cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s) {
     if (T == 0) return cudaSuccess;

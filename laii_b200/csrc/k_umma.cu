@@ -582,37 +582,35 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
  * tokens, token t's 16 bytes at chunk*16*nt + 16*t (= 8-token groups of 128
  * bytes); then d8 per token and the sub-block sums bsum[2j] + bsum[2j+1]
  * packed two per word (j = 0..7).  Tokens past the block's count are zero. */
-__global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const UTokBlock *tbs,
-                                                   const int32_t *n_tb, uint32_t nb, uint32_t nt, uint8_t *xt) {
-    __shared__ int xr[kN];
-    const int tb = blockIdx.x;
-    if (tb >= __ldcg(n_tb)) return;
-    const uint32_t sb = blockIdx.y;
-    const UTokBlock blk = tbs[tb];
-    if (threadIdx.x < kN) {
-        const int t = threadIdx.x;
-        xr[t] = t < blk.ntok ? (perm ? __ldcg(perm + blk.slot0 + t) / (int)K : blk.slot0 + t) : -1;
-    }
-    __syncthreads();
-    uint8_t *dst = xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt);
+struct XtRow {
+    const int8_t *qs; /* the token's Q8_K row: values, scales, sums */
+    const float *d;
+    const int16_t *bs;
+};
+
+/* Copy super-block sb of the block's ntok tokens (row pointers in shared
+ * memory) into the block's pre-gathered layout. */
+__device__ __forceinline__ void xt_copy_block(const XtRow *rows, int ntok, uint32_t sb, uint32_t nt, uint8_t *dst) {
     for (uint32_t q = threadIdx.x; q < nt * 16; q += blockDim.x) {
         const uint32_t c = q / nt, t = q % nt;
-        const int row = xr[t];
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row >= 0) v = __ldcg(reinterpret_cast<const uint4 *>(X.qs + (size_t)row * X.cols + 256 * sb + 16 * c));
+        if ((int)t < ntok) v = __ldcg(reinterpret_cast<const uint4 *>(rows[t].qs + 256 * sb + 16 * c));
         *reinterpret_cast<uint4 *>(dst + (c >> 3) * nt * kHalf + (c & 7) * 16 * nt + 16 * t) = v;
     }
     if (threadIdx.x < nt) {
-        const int t = threadIdx.x, row = xr[t];
+        const int t = threadIdx.x;
         float d8 = 0.0f;
         uint4 pr = make_uint4(0u, 0u, 0u, 0u);
-        if (row >= 0) {
-            d8 = __ldcg(X.d + (size_t)row * nb + sb);
-            const int16_t *bs = X.bs + ((size_t)row * nb + sb) * 16;
+        if (t < ntok) {
+            d8 = __ldcg(rows[t].d + sb);
+            const uint4 *bp = reinterpret_cast<const uint4 *>(rows[t].bs + 16 * sb);
+            const uint4 b0 = __ldcg(bp), b1 = __ldcg(bp + 1);
+            const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
             uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int lo = bs[4 * i] + bs[4 * i + 1], hi = bs[4 * i + 2] + bs[4 * i + 3];
+            for (int i = 0; i < 4; ++i) { /* bsum pairs (4i, 4i+1) and (4i+2, 4i+3) */
+                const int lo = (int)(int16_t)(bw[2 * i] & 0xffffu) + (int)(int16_t)(bw[2 * i] >> 16);
+                const int hi = (int)(int16_t)(bw[2 * i + 1] & 0xffffu) + (int)(int16_t)(bw[2 * i + 1] >> 16);
                 w[i] = (uint32_t)(uint16_t)lo | ((uint32_t)(uint16_t)hi << 16);
             }
             pr = make_uint4(w[0], w[1], w[2], w[3]);
@@ -620,6 +618,51 @@ __global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm
         reinterpret_cast<float *>(dst + 2 * nt * kHalf)[t] = d8;
         reinterpret_cast<uint4 *>(dst + 2 * nt * kHalf + nt * 4)[t] = pr;
     }
+}
+
+__global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const UTokBlock *tbs,
+                                                   const int32_t *n_tb, uint32_t nb, uint32_t nt, uint8_t *xt) {
+    __shared__ XtRow rows[kN];
+    const int tb = blockIdx.x;
+    if (tb >= __ldcg(n_tb)) return;
+    const uint32_t sb = blockIdx.y;
+    const UTokBlock blk = tbs[tb];
+    if (threadIdx.x < kN && (int)threadIdx.x < blk.ntok) {
+        const int t = threadIdx.x;
+        const size_t row = perm ? (size_t)(__ldcg(perm + blk.slot0 + t) / (int)K) : (size_t)(blk.slot0 + t);
+        rows[t] = XtRow{X.qs + row * X.cols, X.d + row * nb, X.bs + row * nb * 16};
+    }
+    __syncthreads();
+    xt_copy_block(rows, blk.ntok, sb, nt, xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt));
+}
+
+/* Expert parallelism: the block's received slots name their home rank and
+ * the home rank's slot; the Q8_K rows are read from the home rank's memory
+ * (peer loads over NVLink).  The sb == 0 CTAs also record each slot's
+ * assignment t*K+k at home, where the output row will go. */
+__global__ void __launch_bounds__(256) k_xt_gather_ep(EpGather g, const UTokBlock *tbs, const int32_t *n_tb,
+                                                      uint32_t nb, uint32_t nt, uint8_t *xt) {
+    __shared__ XtRow rows[kN];
+    const int tb = blockIdx.x;
+    if (tb >= __ldcg(n_tb)) return;
+    const uint32_t sb = blockIdx.y, cols = nb * 256;
+    const UTokBlock blk = tbs[tb];
+    if (threadIdx.x < kN && (int)threadIdx.x < blk.ntok) {
+        const int t = threadIdx.x;
+        const uint32_t v = __ldcg(g.rowmap + blk.slot0 + t);
+        uint32_t r = v >> 24, a = 0;
+        if (r < g.world && (v & 0xffffffu) < g.max_assign) a = (uint32_t)__ldcg(g.perm[r] + (v & 0xffffffu));
+        if (r >= g.world || a >= g.max_assign) { /* a plan or perm entry out of range: read row 0 of rank 0 */
+            atomicOr(g.err, LFM_DEVERR_SEGMENT);
+            r = 0;
+            a = 0;
+        }
+        const size_t row = a / g.K;
+        rows[t] = XtRow{g.qs[r] + row * cols, g.d[r] + row * nb, g.bs[r] + row * nb * 16};
+        if (sb == 0) g.ret[blk.slot0 + t] = (r << 24) | a;
+    }
+    __syncthreads();
+    xt_copy_block(rows, blk.ntok, sb, nt, xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt));
 }
 
 /* Q8_K of one 256-value block held 8 per lane (elements 8*lane..) -- the
@@ -707,6 +750,14 @@ cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, cons
     const uint32_t nb = X.cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
     k_xt_gather<<<dim3(max_tb, nb), 256, 0, s>>>(X, perm, K, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
+    return cudaGetLastError();
+}
+
+cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
+                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
+    const uint32_t nb = cols / 256;
+    if (max_tb == 0 || nb == 0) return cudaSuccess;
+    k_xt_gather_ep<<<dim3(max_tb, nb), 256, 0, s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
     return cudaGetLastError();
 }
 

@@ -33,6 +33,7 @@ struct LayerSlot {
 
 struct Workspace {
     uint32_t T = 0, D = 0, E = 0, K = 0, I = 0;
+    size_t TK = 0;            /* (token, expert) rows covered          */
     void *base = nullptr;
     size_t bytes = 0;
     size_t counters_bytes = 0; /* leading zero-kept counter region      */
@@ -62,10 +63,10 @@ struct Workspace {
 
 namespace {
 enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D,
-                K_XT, K_GEMM_GU, K_COUNT };
+                K_XT, K_GEMM_GU, K_EP_PUBLISH, K_EP_PLAN, K_EP_PUSH, K_COUNT };
 const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer",
                                            "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down",
-                                           "xt_gather", "gemm_gateup"};
+                                           "xt_gather", "gemm_gateup", "ep_publish", "ep_plan", "ep_push"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -78,6 +79,25 @@ struct GraphEntry {
     cudaGraphExec_t exec;
 };
 constexpr size_t kMaxGraphs = 64;
+}  // namespace
+
+namespace {
+/* Expert parallelism over peer memory: this rank's exchange arena (CUDA IPC
+ * exportable) and every rank's mapping of it. */
+struct EpP2P {
+    bool attached = false, connected = false;
+    uint32_t rank = 0, world = 1, T_max = 0, D = 0, E = 0, K = 0, I = 0;
+    uint64_t wait_ns = 0;
+    uint32_t epoch = 0;
+    uint8_t *arena = nullptr;
+    size_t bytes = 0;
+    uint8_t *peer[LFM_EP_MAX_RANKS] = {};  /* peer[rank] == arena */
+    bool opened[LFM_EP_MAX_RANKS] = {};    /* mapped through cudaIpcOpenMemHandle */
+    /* byte offsets of the arena's parts (the same on every rank) */
+    size_t o_cnt = 0, o_y = 0, o_done = 0, o_tab = 0, o_qs = 0, o_qd = 0, o_qb = 0, o_perm = 0, o_yhome = 0,
+           o_rowmap = 0, o_ret = 0, o_nrecv = 0;
+    uint32_t max_recv() const { return world * T_max * K; }
+};
 }  // namespace
 
 struct lfm_gpu_moe {
@@ -97,6 +117,7 @@ struct lfm_gpu_moe {
     bool use_gemm = true;    /* tensor-core grouped GEMMs for prefill-sized T */
     bool use_umma = true;    /* ... on tcgen05 (k_umma.cu) where rows % 128 == 0, else mma.sync (k_gemm.cu) */
     std::vector<GraphEntry> graphs;
+    EpP2P ep;
 };
 
 namespace {
@@ -159,12 +180,15 @@ void drop_graphs(lfm_gpu_moe_t *h) {
  * region; kernels return every counter to zero when they finish with it. */
 lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint32_t E, uint32_t K, uint32_t I) {
     Workspace &w = h->ws;
-    if (w.base && T <= w.T && D <= w.D && E <= w.E && K <= w.K && I <= w.I) return LFM_GPU_OK;
+    /* tokens (T) and (token, expert) assignments (TK) are sized apart: the
+     * expert-parallel step needs many rows at K = 1 next to few tokens at K */
+    const size_t tk_req = (size_t)T * (K ? K : 1u);
+    if (w.base && T <= w.T && tk_req <= w.TK && D <= w.D && E <= w.E && I <= w.I) return LFM_GPU_OK;
     T = T > w.T ? T : w.T; D = D > w.D ? D : w.D; E = E > w.E ? E : w.E;
     K = K > w.K ? K : w.K; I = I > w.I ? I : w.I;
     if (E < 1) E = 1;
     if (K < 1) K = 1;
-    const size_t TK = (size_t)T * K;
+    const size_t TK = tk_req > w.TK ? tk_req : w.TK;
     const size_t n_pairs = E + (TK + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
@@ -222,7 +246,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     drop_graphs(h);
     uint8_t *b = static_cast<uint8_t *>(base);
     w.base = base; w.bytes = off; w.counters_bytes = counters_end;
-    w.T = T; w.D = D; w.E = E; w.K = K; w.I = I;
+    w.T = T; w.D = D; w.E = E; w.K = K; w.I = I; w.TK = TK;
     w.x = reinterpret_cast<float *>(b + o_x);
     w.xq = Q8Rows{reinterpret_cast<int8_t *>(b + o_xq), reinterpret_cast<float *>(b + o_xd),
                   reinterpret_cast<int16_t *>(b + o_xb), 0};
@@ -440,6 +464,10 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
     return LFM_GPU_OK;
 }
 
+namespace {
+void ep_release(lfm_gpu_moe_t *h); /* expert-parallel arena and peer mappings (below) */
+}  // namespace
+
 LFM_API void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h) {
     if (!h) return;
     DeviceGuard g(h->device);
@@ -450,6 +478,10 @@ LFM_API void lfm_gpu_moe_destroy(lfm_gpu_moe_t *h) {
     if (h->dev_err) cudaFree(h->dev_err);
     if (h->loads) cudaFree(h->loads);
     for (ProfRec &r : h->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    if (h->ep.attached) {
+        cudaDeviceSynchronize();
+        ep_release(h);
+    }
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
 }
@@ -1081,5 +1113,266 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer
     h->stats.tokens = T;
     h->stats.kernels_launched = 1;
     LFM_CUDA(h, lfm_launch_ep_combine(x, T, S->dev.D, S->dev.K, w, y, static_cast<cudaStream_t>(stream)));
+    return LFM_GPU_OK;
+}
+
+/* ---- expert parallelism over peer memory ----------------------------------
+ * Home and expert roles of every rank in one call per layer; the exchange
+ * kernels live in k_ep.cu (publish, push, combine), k_route.cu (plan) and
+ * k_umma.cu (gather). */
+
+namespace {
+
+void ep_layout(EpP2P &p) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    const size_t T = p.T_max, TK = (size_t)p.T_max * p.K, nb = p.D / 256, R = p.max_recv();
+    p.o_cnt = take(sizeof(uint32_t) * LFM_EP_MAX_RANKS);
+    p.o_y = take(sizeof(uint32_t) * LFM_EP_MAX_RANKS);
+    p.o_done = take(sizeof(uint32_t));
+    p.o_tab = take(sizeof(int32_t) * 2 * LFM_EP_MAX_RANKS * p.E);
+    p.o_qs = take(T * p.D);
+    p.o_qd = take(sizeof(float) * T * nb);
+    p.o_qb = take(sizeof(int16_t) * T * nb * 16);
+    p.o_perm = take(sizeof(int32_t) * TK);
+    p.o_yhome = take(sizeof(float) * TK * p.D);
+    p.o_rowmap = take(sizeof(uint32_t) * R);
+    p.o_ret = take(sizeof(uint32_t) * R);
+    p.o_nrecv = take(sizeof(int32_t));
+    p.bytes = off;
+}
+
+EpArena ep_arena_view(const EpP2P &p, uint8_t *b) {
+    EpArena a{};
+    a.cnt_flag = reinterpret_cast<uint32_t *>(b + p.o_cnt);
+    a.y_flag = reinterpret_cast<uint32_t *>(b + p.o_y);
+    a.done = reinterpret_cast<uint32_t *>(b + p.o_done);
+    a.table = reinterpret_cast<int32_t *>(b + p.o_tab);
+    a.xq = Q8Rows{reinterpret_cast<int8_t *>(b + p.o_qs), reinterpret_cast<float *>(b + p.o_qd),
+                  reinterpret_cast<int16_t *>(b + p.o_qb), p.D};
+    a.perm = reinterpret_cast<int32_t *>(b + p.o_perm);
+    a.yhome = reinterpret_cast<float *>(b + p.o_yhome);
+    a.rowmap = reinterpret_cast<uint32_t *>(b + p.o_rowmap);
+    a.ret = reinterpret_cast<uint32_t *>(b + p.o_ret);
+    a.n_recv = reinterpret_cast<int32_t *>(b + p.o_nrecv);
+    return a;
+}
+
+void ep_release(lfm_gpu_moe_t *h) {
+    EpP2P &p = h->ep;
+    for (uint32_t r = 0; r < LFM_EP_MAX_RANKS; ++r) {
+        if (p.opened[r] && p.peer[r]) cudaIpcCloseMemHandle(p.peer[r]);
+        p.opened[r] = false;
+        p.peer[r] = nullptr;
+    }
+    if (p.arena) cudaFree(p.arena);
+    p = EpP2P{};
+}
+
+}  // namespace
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_attach(lfm_gpu_moe_t *h, int rank, int world, uint32_t max_tokens,
+                                                   uint32_t D, uint32_t E, uint32_t K, uint32_t I, uint32_t wait_ms,
+                                                   void *ipc_handle_out) {
+    if (!h || !ipc_handle_out) return LFM_GPU_ERR_INVALID_ARG;
+    if (h->ep.attached) return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_attach: already attached (detach first)");
+    if (world < 1 || world > LFM_EP_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_attach: rank %d of world %d (1..%d ranks)", rank, world,
+                    LFM_EP_MAX_RANKS);
+    lfm_gpu_status_t st = check_layer_shape(h, 0, D, E, K, I);
+    if (st != LFM_GPU_OK) return st;
+    if ((uint32_t)world > E) return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_attach: %d ranks for %u experts", world, E);
+    if (max_tokens == 0 || max_tokens > 65535)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_attach: max_tokens=%u not in 1..65535", max_tokens);
+    if (!(lfm_umma_ok(I) && lfm_umma_ok(D)))
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "ep_p2p_attach: D=%u, I=%u need multiples of 128 rows", D, I);
+    static_assert(sizeof(cudaIpcMemHandle_t) <= LFM_GPU_MOE_IPC_HANDLE_BYTES, "IPC handle size");
+    DeviceGuard g(h->device);
+    EpP2P &p = h->ep;
+    p = EpP2P{};
+    p.rank = (uint32_t)rank;
+    p.world = (uint32_t)world;
+    p.T_max = max_tokens;
+    p.D = D; p.E = E; p.K = K; p.I = I;
+    p.wait_ns = (uint64_t)(wait_ms ? wait_ms : 5000u) * 1000000ull;
+    ep_layout(p);
+    /* scratch for both roles now, so no forward reallocates it mid-step:
+     * routing max_tokens tokens at K, and the shard's experts on every row
+     * the ranks can send (at K = 1) */
+    st = ensure_workspace(h, max_tokens, D, E, K, I);
+    if (st == LFM_GPU_OK) st = ensure_workspace(h, p.max_recv(), D, E, 1, I);
+    if (st != LFM_GPU_OK) { p = EpP2P{}; return st; }
+    void *base = nullptr;
+    cudaError_t e = cudaMalloc(&base, p.bytes);
+    if (e != cudaSuccess) { p = EpP2P{}; return cuda_fail(h, e, "ep_p2p_attach: arena cudaMalloc"); }
+    p.arena = static_cast<uint8_t *>(base);
+    e = cudaMemset(base, 0, p.bytes);
+    cudaIpcMemHandle_t ipc{};
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&ipc, base);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { ep_release(h); return cuda_fail(h, e, "ep_p2p_attach: arena setup"); }
+    memset(ipc_handle_out, 0, LFM_GPU_MOE_IPC_HANDLE_BYTES);
+    memcpy(ipc_handle_out, &ipc, sizeof ipc);
+    p.peer[p.rank] = p.arena;
+    p.attached = true;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_connect(lfm_gpu_moe_t *h, const void *handles) {
+    if (!h || !handles) return LFM_GPU_ERR_INVALID_ARG;
+    EpP2P &p = h->ep;
+    if (!p.attached) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_connect: attach first");
+    if (p.connected) return LFM_GPU_OK;
+    DeviceGuard g(h->device);
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (uint32_t r = 0; r < p.world; ++r) {
+        if (r == p.rank) continue;
+        cudaIpcMemHandle_t ipc;
+        memcpy(&ipc, hb + (size_t)r * LFM_GPU_MOE_IPC_HANDLE_BYTES, sizeof ipc);
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < r; ++q)
+                if (p.opened[q]) { cudaIpcCloseMemHandle(p.peer[q]); p.opened[q] = false; p.peer[q] = nullptr; }
+            return fail(h, LFM_GPU_ERR_COMM, "ep_p2p_connect: opening rank %u's arena: %s", r, cudaGetErrorString(e));
+        }
+        p.peer[r] = static_cast<uint8_t *>(ptr);
+        p.opened[r] = true;
+    }
+    p.connected = true;
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_detach(lfm_gpu_moe_t *h) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    if (!h->ep.attached) return LFM_GPU_OK;
+    DeviceGuard g(h->device);
+    const cudaError_t e = cudaDeviceSynchronize();
+    ep_release(h);
+    if (e != cudaSuccess) return cuda_fail(h, e, "ep_p2p_detach: sync");
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                                    void *stream) {
+    const LayerSlot *S = nullptr;
+    lfm_gpu_status_t st = ep_layer(h, layer, &S);
+    if (st != LFM_GPU_OK) return st;
+    EpP2P &p = h->ep;
+    if (!p.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_forward: attach and connect first");
+    const MoeLayerDev &L = S->dev;
+    const uint32_t first = lfm_ep_first(p.rank, p.E, p.world),
+                   count = lfm_ep_first(p.rank + 1, p.E, p.world) - first;
+    if (L.D != p.D || L.E != p.E || L.K != p.K || L.I != p.I)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: layer %u is %ux%ux%ux%u, the arena %ux%ux%ux%u", layer,
+                    L.D, L.E, L.K, L.I, p.D, p.E, p.K, p.I);
+    if (S->ep_first != first || (S->ep_count ? S->ep_count : L.E) != count)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: layer %u holds experts [%u, %u), rank %u owns [%u, %u)",
+                    layer, S->ep_first, S->ep_first + (S->ep_count ? S->ep_count : L.E), p.rank, first, first + count);
+    if (T > p.T_max) return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: T=%u above max_tokens %u", T, p.T_max);
+    if (T && (!x || (reinterpret_cast<uintptr_t>(x) & 15u)))
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: device x must be 16-byte aligned");
+    DeviceGuard g(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Workspace &w = h->ws;
+    const int grid = h->sm_count;
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+
+    EpStep es{};
+    es.rank = p.rank; es.world = p.world; es.E = p.E; es.K = p.K; es.D = p.D;
+    es.epoch = ++p.epoch;
+    es.max_assign = p.T_max * p.K;
+    es.max_recv = p.max_recv();
+    es.wait_ns = p.wait_ns;
+    es.err = h->dev_err;
+    es.self = ep_arena_view(p, p.arena);
+    EpGather eg{};
+    eg.rowmap = es.self.rowmap;
+    eg.ret = es.self.ret;
+    eg.err = h->dev_err;
+    eg.K = p.K;
+    eg.world = p.world;
+    eg.max_assign = es.max_assign;
+    for (uint32_t r = 0; r < p.world; ++r) {
+        const EpArena a = ep_arena_view(p, p.peer[r]);
+        es.table[r] = a.table;
+        es.cnt_flag[r] = a.cnt_flag;
+        es.y_flag[r] = a.y_flag;
+        es.yhome[r] = a.yhome;
+        eg.perm[r] = a.perm;
+        eg.qs[r] = a.xq.qs;
+        eg.d[r] = a.xq.d;
+        eg.bs[r] = a.xq.bs;
+    }
+
+    /* home role: route this rank's tokens into the arena (Q8_K rows, slots) and publish the counts */
+    RouteTables rt = w.rt;
+    rt.perm = es.self.perm;
+    rt.loads = nullptr;
+    rt.plan = UmmaPlanOut{};
+    if (T) {
+        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, false); },
+                          lfm_route_kernels(L, T)));
+    } else {
+        LFM_CUDA(h, cudaMemsetAsync(rt.counts, 0, sizeof(int32_t) * p.E, s));
+    }
+    LFM_CUDA(h, timed(h, K_EP_PUBLISH, s, [&] { return lfm_launch_ep_publish(es, rt.counts, s); }));
+
+    /* expert role: the rows every rank routed to this shard, token blocks sized to the expected load */
+    MoeLayerDev Lx = L;
+    Lx.E = count;
+    Lx.K = 1;
+    UmmaPlanOut plan{};
+    plan.nt = lfm_umma_nt(T ? T * p.K : p.K, count); /* T*K rows expected per shard on average */
+    plan.rows_gu = L.I;
+    plan.rows_dn = L.D;
+    plan.tiles_gu = w.utiles_gu;
+    plan.tiles_dn = w.utiles_dn;
+    plan.tbs = w.utbs;
+    plan.counts = w.ucounts;
+    const uint32_t R = es.max_recv;
+    plan.max_tb = (uint32_t)lfm_umma_tb_max(R, count, plan.nt);
+    plan.max_gu = 2 * (uint32_t)lfm_umma_tiles_max(L.I, R, count, plan.nt);
+    plan.max_dn = (uint32_t)lfm_umma_tiles_max(L.D, R, count, plan.nt);
+    if (plan.max_tb > w.umax_tb || plan.max_gu > w.umax_gu || plan.max_dn > w.umax_dn)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: tile plan capacity (internal)");
+    RouteTables rx = w.rt;
+    rx.plan = plan;
+    const uint32_t nt = plan.nt, mtb = plan.max_tb;
+    LFM_CUDA(h, timed(h, K_EP_PLAN, s, [&] { return lfm_launch_ep_plan(es, first, count, rx, s); }));
+    LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather_ep(eg, L.D, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
+    LFM_CUDA(h, timed(h, K_GEMM_GU, s, [&] {
+        return lfm_launch_q4k_umma(Lx.gate, Lx.up, count, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
+                                   h->dev_err, grid, s);
+    }));
+    LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
+    LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
+        return lfm_launch_q4k_umma(Lx.down, Lx.down, count, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y,
+                                   w.y, h->dev_err, grid, s);
+    }));
+    LFM_CUDA(h, timed(h, K_EP_PUSH, s, [&] { return lfm_launch_ep_push(es, w.y, R, grid, s); }));
+
+    /* home role: combine the outputs the expert ranks stored here */
+    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, s); }));
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_wait_check(lfm_gpu_moe_t *h, void *stream) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    EpP2P &p = h->ep;
+    if (!p.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_wait_check: attach and connect first");
+    DeviceGuard g(h->device);
+    EpStep es{};
+    es.rank = p.rank; es.world = p.world; es.E = p.E; es.K = p.K; es.D = p.D;
+    es.epoch = p.epoch + 2u; /* no rank signals a step beyond the next one */
+    es.max_assign = p.T_max * p.K;
+    es.max_recv = p.max_recv();
+    es.wait_ns = p.wait_ns;
+    es.err = h->dev_err;
+    es.self = ep_arena_view(p, p.arena);
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.kernels_launched = 1;
+    LFM_CUDA(h, lfm_launch_ep_combine_wait(es, nullptr, 0, nullptr, static_cast<cudaStream_t>(stream)));
     return LFM_GPU_OK;
 }

@@ -105,6 +105,38 @@ __device__ __forceinline__ bool lfm_mbar_wait(uint64_t *bar, uint32_t parity, ui
     return true;
 }
 
+/* Flags another GPU writes (expert parallelism over peer memory). */
+__device__ __forceinline__ uint32_t lfm_ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void lfm_st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t lfm_ld_relaxed_sys(const int32_t *p) {
+    int32_t v;
+    asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+/* One thread: wait until flags[0..n) all reach `epoch` (wrap-safe), for at
+ * most wait_ns in total.  On timeout: set the error bit and return false. */
+__device__ __forceinline__ bool lfm_wait_flags(const uint32_t *flags, uint32_t n, uint32_t epoch, uint64_t wait_ns,
+                                               uint32_t *err) {
+    const uint64_t t0 = lfm_globaltimer();
+    for (uint32_t p = 0; p < n; ++p) {
+        while ((int32_t)(lfm_ld_acquire_sys(flags + p) - epoch) < 0) {
+            if (lfm_globaltimer() - t0 > wait_ns) {
+                atomicOr(err, LFM_DEVERR_TIMEOUT);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
 /* L2 policy for data read exactly once (expert weights). */
 __device__ __forceinline__ uint64_t lfm_policy_evict_first() {
     uint64_t p;

@@ -132,6 +132,70 @@ cudaError_t lfm_launch_ep_combine(float *x, uint32_t T, uint32_t D, uint32_t K, 
                                   cudaStream_t s);
 cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cudaStream_t s);
 
+/* ---- expert parallelism over peer memory (k_ep.cu, k_route.cu, k_umma.cu) ----
+ * Every rank's exchange arena has the same layout; the host maps the other
+ * ranks' arenas (CUDA IPC) so kernels read and write them directly.  Flags
+ * carry the epoch of the layer step (wrap-safe compare); the count table is
+ * double-buffered by epoch parity. */
+#define LFM_EP_MAX_RANKS 8
+struct EpArena {
+    uint32_t *cnt_flag; /* [LFM_EP_MAX_RANKS] epoch of home rank r's published counts (written by r)   */
+    uint32_t *y_flag;   /* [LFM_EP_MAX_RANKS] epoch of expert rank r's stored outputs (written by r)    */
+    uint32_t *done;     /* [1] output-store CTAs finished (this rank only; kept at 0)                    */
+    int32_t *table;     /* [2][LFM_EP_MAX_RANKS][E] per-expert counts of every home rank                 */
+    Q8Rows xq;          /* [max_tokens] this rank's Q8_K rows of x (read by the expert ranks)            */
+    int32_t *perm;      /* [max_tokens*K] slot -> assignment t*K+k, slots grouped by expert (read by them)*/
+    float *yhome;       /* [max_tokens*K][D] expert output of assignment t*K+k (written by them)         */
+    uint32_t *rowmap;   /* [max_recv] received slot -> (home rank << 24) | home slot (this rank only)    */
+    uint32_t *ret;      /* [max_recv] received slot -> (home rank << 24) | t*K+k     (this rank only)    */
+    int32_t *n_recv;    /* [1] rows received in this step (this rank only)                               */
+};
+/* What the exchange kernels of one step need: this rank's arena and every rank's view of its own. */
+struct EpStep {
+    uint32_t rank, world, E, K, D, epoch;
+    uint32_t max_assign; /* T*K capacity of every home rank's yhome / perm */
+    uint32_t max_recv;   /* received-slot capacity of this rank          */
+    uint64_t wait_ns;
+    uint32_t *err;
+    EpArena self;
+    int32_t *table[LFM_EP_MAX_RANKS];     /* peer views */
+    uint32_t *cnt_flag[LFM_EP_MAX_RANKS];
+    uint32_t *y_flag[LFM_EP_MAX_RANKS];
+    float *yhome[LFM_EP_MAX_RANKS];
+};
+/* The received rows for k_xt_gather: slot -> home rank's Q8_K row (peer views). */
+struct EpGather {
+    const uint32_t *rowmap;
+    uint32_t *ret;
+    uint32_t *err;
+    uint32_t K, world, max_assign; /* max_assign: T*K capacity of a home rank */
+    const int32_t *perm[LFM_EP_MAX_RANKS];
+    const int8_t *qs[LFM_EP_MAX_RANKS];
+    const float *d[LFM_EP_MAX_RANKS];
+    const int16_t *bs[LFM_EP_MAX_RANKS];
+};
+/* Owning rank of expert e when E experts are split over `world` ranks, the
+ * first E % world ranks holding one more. */
+__host__ __device__ inline uint32_t lfm_ep_owner(uint32_t e, uint32_t E, uint32_t world) {
+    const uint32_t base = E / world, rem = E % world, big = rem * (base + 1);
+    return e < big ? e / (base + 1) : rem + (e - big) / base;
+}
+__host__ __device__ inline uint32_t lfm_ep_first(uint32_t r, uint32_t E, uint32_t world) {
+    const uint32_t base = E / world, rem = E % world;
+    return r * base + (r < rem ? r : rem);
+}
+/* home rank: publish rt.counts[E] into every rank's table, then its cnt_flag */
+cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaStream_t s);
+/* expert rank: wait for every rank's counts, then the received slots' layout
+ * (rowmap, n_recv) and the tcgen05 tile plans of the local experts
+ * [first, first + count) */
+cudaError_t lfm_launch_ep_plan(const EpStep &st, uint32_t first, uint32_t count, const RouteTables &rt,
+                               cudaStream_t s);
+/* expert rank: y[slot][D] -> its home rank's yhome row; the last CTA raises y_flag on every rank */
+cudaError_t lfm_launch_ep_push(const EpStep &st, const float *y, uint32_t max_recv, int grid, cudaStream_t s);
+/* home rank: wait for every expert rank's y_flag, then x[t] += w . yhome[t] in k order */
+cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, cudaStream_t s);
+
 /* k_gemm.cu: prefill grouped GEMM (tensor cores) */
 size_t lfm_gemm_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);
 size_t lfm_gemm_tile_bytes();
@@ -157,6 +221,9 @@ size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint3
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt);
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+/* the same from other ranks' Q8_K rows (expert parallelism, g.rowmap set); X.cols gives D */
+cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
+                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
 /* SwiGLU of the gate|up outputs, Q8_K, written as the down GEMM's token blocks */
 cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);

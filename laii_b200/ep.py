@@ -16,9 +16,17 @@ E/G experts (``shard_of``).  One layer step on a rank's own T tokens:
      x[t] = fma(w[t, k], y[t, k], x[t]) (tools/lfm2_moe_checkpoint.c:266-269),
      so the result equals the single-GPU layer bit for bit.
 
-The exchanges use ``torch.distributed.all_to_all_single`` (NCCL over NVLink
-between GPUs; gloo for the host-side tests).  The compute is the CUDA
-library's ``lfm_gpu_moe_ep_*`` entry points (``GpuOps``).
+Two ways to run it:
+  * ``ep_forward`` with a comm object: the exchanges are
+    ``torch.distributed.all_to_all_single`` (NCCL over NVLink between GPUs;
+    gloo for the host-side tests) and the compute is the CUDA library's
+    ``lfm_gpu_moe_ep_*`` entry points (``GpuOps``).  The split sizes come to
+    the host every layer.
+  * ``p2p_connect`` + ``GpuMoE.ep_p2p_forward``: the whole layer step in the
+    library, the exchanges done by its own kernels through CUDA IPC mappings
+    of every rank's exchange arena (peer loads and stores over NVLink), with
+    no host synchronisation; torch.distributed only carries the IPC handles
+    once at setup.
 """
 from __future__ import annotations
 
@@ -147,3 +155,24 @@ class GpuOps:
         self.moe.ep_combine(layer, x.data_ptr(), x.shape[0], w.contiguous().data_ptr(), y.contiguous().data_ptr(),
                             self._stream())
         self._count()
+
+
+def p2p_connect(moe, max_tokens: int, D: int, E: int, K: int, I: int, group=None, wait_ms: int = 0):
+    """Attach moe's exchange arena for up to max_tokens tokens per rank and map
+    every other rank's (one process per GPU, torch.distributed initialised;
+    without it, a world of one).  Returns (rank, world).  Collective: every
+    rank calls it, then ``moe.ep_p2p_forward`` for the same layers in order."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+    else:
+        world, rank = 1, 0
+    handle = moe.ep_p2p_attach(rank, world, max_tokens, D, E, K, I, wait_ms)
+    if world == 1:
+        moe.ep_p2p_connect([handle])
+        return rank, world
+    handles: List[Optional[bytes]] = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    moe.ep_p2p_connect(handles)
+    dist.barrier(group=group)  # no rank writes into an arena before its owner has mapped every peer
+    return rank, world

@@ -129,6 +129,34 @@ class GpuMoE:
         self._check(self._lib.lfm_gpu_moe_ep_combine(self._h, layer, ctypes.c_void_p(x_ptr), T, ctypes.c_void_p(w_ptr),
                                                      ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or None)))
 
+    # -- expert parallelism over peer memory (one process per GPU) --------
+    IPC_HANDLE_BYTES = 64
+
+    def ep_p2p_attach(self, rank: int, world: int, max_tokens: int, D: int, E: int, K: int, I: int,
+                      wait_ms: int = 0) -> bytes:
+        """Allocate this rank's exchange arena; returns its IPC handle for the other ranks."""
+        buf = ctypes.create_string_buffer(self.IPC_HANDLE_BYTES)
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_attach(self._h, rank, world, max_tokens, D, E, K, I, wait_ms, buf))
+        return buf.raw
+
+    def ep_p2p_connect(self, handles) -> None:
+        """Map the other ranks' arenas; handles[r] = rank r's attach result."""
+        blob = b"".join(bytes(h) for h in handles)
+        if len(blob) != self.IPC_HANDLE_BYTES * len(handles):
+            raise ValueError("every IPC handle is %d bytes" % self.IPC_HANDLE_BYTES)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_connect(self._h, buf))
+
+    def ep_p2p_forward(self, layer: int, x_ptr: int, T: int, stream: int = 0):
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_forward(self._h, layer, ctypes.c_void_p(x_ptr or None), T,
+                                                         ctypes.c_void_p(stream or None)))
+
+    def ep_p2p_wait_check(self, stream: int = 0):
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_wait_check(self._h, ctypes.c_void_p(stream or None)))
+
+    def ep_p2p_detach(self):
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_detach(self._h))
+
     def reserve(self, max_tokens: int):
         self._check(self._lib.lfm_gpu_moe_reserve(self._h, max_tokens))
 

@@ -230,3 +230,146 @@ def test_ep_nccl_two_gpus_match_single_gpu_forward(tmp_path):
         want = g.forward(0, synth.make_hidden(world * T, 2048, seed_offset=61))
     assert rel_l2(got, want) <= REL_L2
     assert float(np.abs(got - want).max()) <= MAX_ABS
+
+
+# ---- expert parallelism over peer memory (lfm_gpu_moe_ep_p2p_*) ----------
+
+P2P_SHAPE = (2048, 32, 4, 1792)
+
+
+def _p2p_layers(g, n_layers, first, count):
+    import bench
+    D_, E_, K_, I_ = P2P_SHAPE
+    for l in range(n_layers):
+        if count == E_:
+            g.synth_layer_shard(l, D_, E_, K_, I_, bench.layer_seeds(l + 40), 0, E_)
+        else:
+            g.synth_layer_shard(l, D_, E_, K_, I_, bench.layer_seeds(l + 40), first, count)
+
+
+def _p2p_want(xs, n_layers):
+    """Every step of the test through the one-GPU forward of the full layers."""
+    import bench
+    from laii_b200.moe import GpuMoE
+    D_, E_, K_, I_ = P2P_SHAPE
+    out = []
+    with GpuMoE(0) as g:
+        for l in range(n_layers):
+            g.synth_layer(l, D_, E_, K_, I_, bench.layer_seeds(l + 40))
+        for x in xs:
+            y = np.array(x, copy=True)
+            for l in range(n_layers):
+                if y.shape[0]:
+                    y = g.forward(l, y)
+            out.append(y)
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Ts", [(8, 24, 0, 300), (64, 1)])
+def test_ep_p2p_world_of_one_matches_forward(Ts):
+    """The peer-memory layer step as a world of one (every exchange to itself), two layers a step,
+    against the regular forward: the same grouped GEMMs and k-ordered combine, so bit-exact."""
+    import torch
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    D_, E_, K_, I_ = P2P_SHAPE
+    xs = [synth.make_hidden(T, D_, seed_offset=77 + T) if T else np.zeros((0, D_), np.float32) for T in Ts]
+    want = _p2p_want(xs, 2)
+    with GpuMoE(0) as g:
+        _p2p_layers(g, 2, 0, E_)
+        assert ep.p2p_connect(g, max(Ts), D_, E_, K_, I_) == (0, 1)
+        for x, wnt in zip(xs, want):
+            xd = torch.from_numpy(np.array(x, copy=True)).cuda()
+            s = torch.cuda.current_stream().cuda_stream
+            for l in range(2):
+                g.ep_p2p_forward(l, xd.data_ptr() if xd.numel() else 0, xd.shape[0], s)
+            torch.cuda.synchronize()
+            g.sync()
+            got = xd.cpu().numpy()
+            assert np.array_equal(got, wnt)
+        g.ep_p2p_detach()
+
+
+@pytest.mark.gpu
+def test_ep_p2p_bounded_wait_reports_timeout_and_recovers():
+    """A wait on a step no rank signals runs out after wait_ms: TIMEOUT at the next sync, the context
+    stays usable and the next layer step is still right."""
+    import time
+    import torch
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE, MoEError
+    D_, E_, K_, I_ = P2P_SHAPE
+    x = synth.make_hidden(24, D_, seed_offset=5)
+    want = _p2p_want([x], 1)[0]
+    with GpuMoE(0) as g:
+        _p2p_layers(g, 1, 0, E_)
+        ep.p2p_connect(g, 24, D_, E_, K_, I_, wait_ms=200)
+        g.ep_p2p_wait_check(torch.cuda.current_stream().cuda_stream)
+        t0 = time.perf_counter()
+        with pytest.raises(MoEError) as ei:
+            g.sync()
+        assert ei.value.status == -9
+        assert time.perf_counter() - t0 < 10.0
+        xd = torch.from_numpy(np.array(x, copy=True)).cuda()
+        g.ep_p2p_forward(0, xd.data_ptr(), 24, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        g.sync()
+        assert np.array_equal(xd.cpu().numpy(), want)
+
+
+P2P_STEPS = [(40, 7), (0, 33), (200, 200)]  # tokens of rank 0, rank 1 per step
+
+
+def _p2p_rank(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120))
+    try:
+        D_, E_, K_, I_ = P2P_SHAPE
+        first, count = ep.shard_of(E_, world, rank)
+        g = GpuMoE(rank)
+        _p2p_layers(g, 2, first, count)
+        Tmax = max(max(s) for s in P2P_STEPS)
+        ep.p2p_connect(g, Tmax, D_, E_, K_, I_, wait_ms=10000)
+        for i, Ts in enumerate(P2P_STEPS):
+            T = Ts[rank]
+            x = synth.make_hidden(T, D_, seed_offset=1000 * i + 100 * rank) if T else np.zeros((0, D_), np.float32)
+            xd = torch.from_numpy(np.array(x, copy=True)).cuda()
+            s = torch.cuda.current_stream().cuda_stream
+            for l in range(2):
+                g.ep_p2p_forward(l, xd.data_ptr() if T else 0, T, s)
+            torch.cuda.synchronize()
+            g.sync()
+            np.save(os.path.join(out_dir, f"p2p_{i}_{rank}.npy"), xd.cpu().numpy())
+        dist.barrier()
+        g.ep_p2p_detach()
+        g.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_p2p_two_gpus_match_single_gpu_forward(tmp_path):
+    """Two processes, one GPU each, experts split 16/16: uneven and empty token counts per rank,
+    two layers a step, three steps; each rank's tokens against the one-GPU forward, bit-exact."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from laii_b200 import synth
+    world = 2
+    mp.spawn(_p2p_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    D_ = P2P_SHAPE[0]
+    for i, Ts in enumerate(P2P_STEPS):
+        xs = [synth.make_hidden(T, D_, seed_offset=1000 * i + 100 * r) if T else np.zeros((0, D_), np.float32)
+              for r, T in enumerate(Ts)]
+        want = _p2p_want(xs, 2)
+        for r in range(world):
+            got = np.load(tmp_path / f"p2p_{i}_{r}.npy")
+            assert np.array_equal(got, want[r]), (i, r)
