@@ -8,9 +8,9 @@
  *                      count table, then its cnt_flag there (release);
  *   (k_ep_plan, k_route.cu; k_xt_gather_ep, k_umma.cu: the expert rank lays
  *    out the received slots and gathers their Q8_K rows from the home ranks)
- *   k_ep_push          expert rank: each output row straight into its home
- *                      rank's yhome[t*K + k]; the last CTA raises y_flag on
- *                      every rank (release);
+ *   (the down GEMM, k_umma.cu, stores each output row straight into its home
+ *    rank's yhome[t*K + k] from its epilogue; its last CTA raises y_flag on
+ *    every rank (release));
  *   k_ep_combine_wait  home rank: acquire every y_flag, then
  *                      x[t] = fma(w[t][k], yhome[t*K+k], x[t]) for k in order
  *                      (tools/lfm2_moe_checkpoint.c:266-269).
@@ -38,46 +38,6 @@ __global__ void __launch_bounds__(256) k_ep_publish(EpStep st, const int32_t *__
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x < st.world) lfm_st_release_sys(st.cnt_flag[threadIdx.x] + st.rank, st.epoch);
-}
-
-/* One warp per received row: D fp32 from this rank's y to the home rank's
- * yhome row (peer stores, 16 bytes a lane, four in flight). */
-__global__ void __launch_bounds__(256) k_ep_push(EpStep st, const float *__restrict__ y) {
-    __shared__ float *yh[LFM_EP_MAX_RANKS];
-    if (threadIdx.x < LFM_EP_MAX_RANKS) yh[threadIdx.x] = threadIdx.x < st.world ? st.yhome[threadIdx.x] : nullptr;
-    __syncthreads();
-    const int n = __ldcg(st.self.n_recv);
-    const uint32_t lane = threadIdx.x & 31, D4 = st.D / 4;
-    const uint32_t nw = gridDim.x * (blockDim.x >> 5);
-    for (uint32_t j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < (uint32_t)n; j += nw) {
-        const uint32_t v = __ldcg(st.self.ret + j), r = v >> 24, a = v & 0xffffffu;
-        if (r >= st.world || a >= st.max_assign) {
-            if (lane == 0) atomicOr(st.err, LFM_DEVERR_SEGMENT);
-            continue;
-        }
-        const float4 *src = reinterpret_cast<const float4 *>(y + (size_t)j * st.D);
-        float4 *dst = reinterpret_cast<float4 *>(yh[r] + (size_t)a * st.D);
-        uint32_t c = lane;
-        for (; c + 96 < D4; c += 128) {
-            const float4 v0 = __ldcg(src + c), v1 = __ldcg(src + c + 32), v2 = __ldcg(src + c + 64),
-                         v3 = __ldcg(src + c + 96);
-            dst[c] = v0;
-            dst[c + 32] = v1;
-            dst[c + 64] = v2;
-            dst[c + 96] = v3;
-        }
-        for (; c < D4; c += 32) dst[c] = __ldcg(src + c);
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(st.self.done, 1u);
-        if (prev == gridDim.x - 1) { /* every CTA's stores are fenced before its count */
-            atomicExch(st.self.done, 0u);
-            __threadfence_system();
-            for (uint32_t p = 0; p < st.world; ++p) lfm_st_release_sys(st.y_flag[p] + st.rank, st.epoch);
-        }
-    }
 }
 
 /* x[t][c..c+3] = fma(w[t][k], yhome[t*K+k][c..c+3], x) for k = 0..K-1 in order. */
@@ -110,16 +70,6 @@ __global__ void __launch_bounds__(256) k_ep_combine_wait(EpStep st, float *__res
 cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaStream_t s) {
     if (st.world == 0 || st.world > LFM_EP_MAX_RANKS) return cudaErrorInvalidValue;
     k_ep_publish<<<1, 256, 0, s>>>(st, counts);
-    return cudaGetLastError();
-}
-
-cudaError_t lfm_launch_ep_push(const EpStep &st, const float *y, uint32_t max_recv, int grid, cudaStream_t s) {
-    if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.D % 4) return cudaErrorInvalidValue;
-    uint32_t blocks = (max_recv + 7) / 8; /* eight rows (warps) per CTA */
-    const uint32_t cap = (uint32_t)grid * 4;
-    if (blocks > cap) blocks = cap;
-    if (blocks == 0) blocks = 1;
-    k_ep_push<<<blocks, 256, 0, s>>>(st, y);
     return cudaGetLastError();
 }
 

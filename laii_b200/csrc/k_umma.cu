@@ -228,15 +228,18 @@ __device__ __forceinline__ bool uwait(uint64_t *bar, uint32_t parity, volatile i
     return true;
 }
 
-template <bool kDec>
+template <bool kDec, bool kEp>
 __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __grid_constant__ CUtensorMap tmw0,
-                                                          const __grid_constant__ CUtensorMap tmw1, UmmaArgs A) {
+                                                          const __grid_constant__ CUtensorMap tmw1, UmmaArgs A,
+                                                          const __grid_constant__ UmmaEpOut ep) {
     using C = UCfg<kDec>;
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ UmmaBars bars;
     __shared__ UTile s_tile[kCtaTiles];    /* this CTA's tiles, in walking order */
     __shared__ UTokBlock s_blk[kCtaTiles]; /* and their token blocks           */
+    __shared__ float *s_yh[LFM_EP_MAX_RANKS];  /* home ranks' output rows (expert parallelism) */
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (kEp && tid < LFM_EP_MAX_RANKS) s_yh[tid] = ep.yhome[tid];
     if (tid == 0) {
         /* decode: each half super-block feeds one MMA stream; prefill: both streams read every stage */
         for (int i = 0; i < C::kSA; ++i) {
@@ -404,10 +407,23 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
                 }
             }
             if (!ok) break;
-            float *yb = (tile.mat ? A.Y[1] : A.Y[0]) + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
+            if constexpr (kEp) { /* the row of slot j belongs to a token of home rank ret[j] >> 24 */
+                const uint32_t *rt = ep.ret + blk.slot0 + ch * half;
 #pragma unroll
-            for (int t = 0; t < kCols; ++t)
-                if (t < nv) yb[(size_t)t * A.rows] = S[t];
+                for (int t = 0; t < kCols; ++t)
+                    if (t < nv) {
+                        const uint32_t v = __ldg(rt + t), hr = v >> 24, a = v & 0xffffffu;
+                        if (hr < ep.world && a < ep.max_assign)
+                            s_yh[hr][(size_t)a * A.rows + tile.row0 + r] = S[t];
+                        else
+                            atomicOr(A.err, LFM_DEVERR_SEGMENT);
+                    }
+            } else {
+                float *yb = (tile.mat ? A.Y[1] : A.Y[0]) + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
+#pragma unroll
+                for (int t = 0; t < kCols; ++t)
+                    if (t < nv) yb[(size_t)t * A.rows] = S[t];
+            }
         }
         if (!ok) *abort = 1;
     } else if (warp < C::kWarpMma) {
@@ -563,6 +579,7 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
         }
     }
 
+    if (kEp) __threadfence_system(); /* this thread's peer stores, before the CTA counts itself done */
     __syncthreads();
     if (*abort) {
         /* copies and MMAs already issued complete within microseconds: let them land */
@@ -574,6 +591,12 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+    if (kEp && tid == 0 && atomicAdd(ep.done, 1u) == gridDim.x - 1) {
+        /* the last CTA: every row of this rank is stored at its home rank */
+        atomicExch(ep.done, 0u);
+        __threadfence_system();
+        for (uint32_t p = 0; p < ep.world; ++p) lfm_st_release_sys(ep.y_flag[p] + ep.rank, ep.epoch);
     }
 }
 
@@ -590,12 +613,22 @@ struct XtRow {
 
 /* Copy super-block sb of the block's ntok tokens (row pointers in shared
  * memory) into the block's pre-gathered layout. */
+constexpr uint32_t kXtThreads = 256;
 __device__ __forceinline__ void xt_copy_block(const XtRow *rows, int ntok, uint32_t sb, uint32_t nt, uint8_t *dst) {
-    for (uint32_t q = threadIdx.x; q < nt * 16; q += blockDim.x) {
-        const uint32_t c = q / nt, t = q % nt;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if ((int)t < ntok) v = __ldcg(reinterpret_cast<const uint4 *>(rows[t].qs + 256 * sb + 16 * c));
-        *reinterpret_cast<uint4 *>(dst + (c >> 3) * nt * kHalf + (c & 7) * 16 * nt + 16 * t) = v;
+    /* all loads first, then the stores: the rows may sit on another GPU, where
+     * a load takes microseconds, so every thread keeps all of its in flight */
+    constexpr uint32_t kIt = kN * 16 / kXtThreads;
+    uint4 v[kIt];
+#pragma unroll
+    for (uint32_t i = 0; i < kIt; ++i) {
+        const uint32_t q = threadIdx.x + i * kXtThreads, c = q / nt, t = q % nt;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (q < nt * 16 && (int)t < ntok) v[i] = __ldcg(reinterpret_cast<const uint4 *>(rows[t].qs + 256 * sb + 16 * c));
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kIt; ++i) {
+        const uint32_t q = threadIdx.x + i * kXtThreads, c = q / nt, t = q % nt;
+        if (q < nt * 16) *reinterpret_cast<uint4 *>(dst + (c >> 3) * nt * kHalf + (c & 7) * 16 * nt + 16 * t) = v[i];
     }
     if (threadIdx.x < nt) {
         const int t = threadIdx.x;
@@ -620,7 +653,7 @@ __device__ __forceinline__ void xt_copy_block(const XtRow *rows, int ntok, uint3
     }
 }
 
-__global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const UTokBlock *tbs,
+__global__ void __launch_bounds__(kXtThreads) k_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const UTokBlock *tbs,
                                                    const int32_t *n_tb, uint32_t nb, uint32_t nt, uint8_t *xt) {
     __shared__ XtRow rows[kN];
     const int tb = blockIdx.x;
@@ -640,7 +673,7 @@ __global__ void __launch_bounds__(256) k_xt_gather(Q8Rows X, const int32_t *perm
  * the home rank's slot; the Q8_K rows are read from the home rank's memory
  * (peer loads over NVLink).  The sb == 0 CTAs also record each slot's
  * assignment t*K+k at home, where the output row will go. */
-__global__ void __launch_bounds__(256) k_xt_gather_ep(EpGather g, const UTokBlock *tbs, const int32_t *n_tb,
+__global__ void __launch_bounds__(kXtThreads) k_xt_gather_ep(EpGather g, const UTokBlock *tbs, const int32_t *n_tb,
                                                       uint32_t nb, uint32_t nt, uint8_t *xt) {
     __shared__ XtRow rows[kN];
     const int tb = blockIdx.x;
@@ -749,7 +782,7 @@ cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, cons
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
     const uint32_t nb = X.cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
-    k_xt_gather<<<dim3(max_tb, nb), 256, 0, s>>>(X, perm, K, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
+    k_xt_gather<<<dim3(max_tb, nb), kXtThreads, 0, s>>>(X, perm, K, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
     return cudaGetLastError();
 }
 
@@ -757,7 +790,7 @@ cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void
                                     uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
     const uint32_t nb = cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
-    k_xt_gather_ep<<<dim3(max_tb, nb), 256, 0, s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
+    k_xt_gather_ep<<<dim3(max_tb, nb), kXtThreads, 0, s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
     return cudaGetLastError();
 }
 
@@ -797,11 +830,24 @@ cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, 
     return cudaGetLastError();
 }
 
+template <bool kDec, bool kEp>
+static cudaError_t launch_umma(const CUtensorMap &tm0, const CUtensorMap &tm1, const UmmaArgs &a,
+                               const UmmaEpOut &ep, int grid, cudaStream_t s) {
+    using C = UCfg<kDec>;
+    static size_t cache[16];
+    const cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<kDec, kEp>, C::kSmem, cache);
+    if (e != cudaSuccess) return e;
+    k_q4k_umma<kDec, kEp><<<grid, C::kThreads, C::kSmem, s>>>(tm0, tm1, a, ep);
+    return cudaGetLastError();
+}
+
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
                                 const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
-                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s) {
+                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s,
+                                const UmmaEpOut *ep) {
     if (rows % kM || cols % 256 || experts == 0 || nt % 16 || nt == 0 || nt > (uint32_t)kN)
         return cudaErrorInvalidValue;
+    if (ep && (!ep->ret || !ep->done || ep->world == 0 || ep->world > LFM_EP_MAX_RANKS)) return cudaErrorInvalidValue;
     /* each expert tensor as a 2-D byte matrix [experts * rows][nb * 144] */
     CUtensorMap tm0, tm1;
     const uint64_t row_bytes = (uint64_t)(cols / 256) * kRaw;
@@ -813,16 +859,8 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
     if (dec) nsb &= ~1u; /* one B ring per half super-block */
     UmmaArgs a{W0, rows, cols / 256, xt, nt, nsb, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
                n_tiles, {Y0, Y1}, err};
-    if (dec) {
-        static size_t cache[16];
-        cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<true>, UCfg<true>::kSmem, cache);
-        if (e != cudaSuccess) return e;
-        k_q4k_umma<true><<<grid, UCfg<true>::kThreads, UCfg<true>::kSmem, s>>>(tm0, tm1, a);
-    } else {
-        static size_t cache[16];
-        cudaError_t e = lfm_smem_attr((const void *)k_q4k_umma<false>, UCfg<false>::kSmem, cache);
-        if (e != cudaSuccess) return e;
-        k_q4k_umma<false><<<grid, UCfg<false>::kThreads, UCfg<false>::kSmem, s>>>(tm0, tm1, a);
-    }
-    return cudaGetLastError();
+    const UmmaEpOut eo = ep ? *ep : UmmaEpOut{};
+    if (dec)
+        return ep ? launch_umma<true, true>(tm0, tm1, a, eo, grid, s) : launch_umma<true, false>(tm0, tm1, a, eo, grid, s);
+    return ep ? launch_umma<false, true>(tm0, tm1, a, eo, grid, s) : launch_umma<false, false>(tm0, tm1, a, eo, grid, s);
 }

@@ -63,10 +63,10 @@ struct Workspace {
 
 namespace {
 enum KernelId { K_ROUTE, K_GATEUP, K_QUANT_H, K_DOWN, K_COMBINE, K_LAYER, K_PLAN, K_GEMM_G, K_GEMM_U, K_SWIGLU, K_GEMM_D,
-                K_XT, K_GEMM_GU, K_EP_PUBLISH, K_EP_PLAN, K_EP_PUSH, K_COUNT };
+                K_XT, K_GEMM_GU, K_EP_PUBLISH, K_EP_PLAN, K_COUNT };
 const char *const kKernelNames[K_COUNT] = {"route", "gateup", "quant_h", "down", "combine", "moe_layer",
                                            "gemm_plan", "gemm_gate", "gemm_up", "swiglu_q8", "gemm_down",
-                                           "xt_gather", "gemm_gateup", "ep_publish", "ep_plan", "ep_push"};
+                                           "xt_gather", "gemm_gateup", "ep_publish", "ep_plan"};
 struct ProfRec {
     int kid;
     cudaEvent_t a, b;
@@ -1347,11 +1347,23 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t l
                                    h->dev_err, grid, s);
     }));
     LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
+    /* down: every output row stored at its home rank from the epilogue (peer stores over NVLink),
+     * y_flag raised on every rank by the last CTA */
+    UmmaEpOut eo{};
+    eo.ret = es.self.ret;
+    for (uint32_t r = 0; r < p.world; ++r) {
+        eo.yhome[r] = es.yhome[r];
+        eo.y_flag[r] = es.y_flag[r];
+    }
+    eo.done = es.self.done;
+    eo.world = p.world;
+    eo.rank = p.rank;
+    eo.epoch = es.epoch;
+    eo.max_assign = es.max_assign;
     LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
         return lfm_launch_q4k_umma(Lx.down, Lx.down, count, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y,
-                                   w.y, h->dev_err, grid, s);
+                                   w.y, h->dev_err, grid, s, &eo);
     }));
-    LFM_CUDA(h, timed(h, K_EP_PUSH, s, [&] { return lfm_launch_ep_push(es, w.y, R, grid, s); }));
 
     /* home role: combine the outputs the expert ranks stored here */
     LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, s); }));

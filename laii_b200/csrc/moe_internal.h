@@ -191,8 +191,17 @@ cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaS
  * [first, first + count) */
 cudaError_t lfm_launch_ep_plan(const EpStep &st, uint32_t first, uint32_t count, const RouteTables &rt,
                                cudaStream_t s);
-/* expert rank: y[slot][D] -> its home rank's yhome row; the last CTA raises y_flag on every rank */
-cudaError_t lfm_launch_ep_push(const EpStep &st, const float *y, uint32_t max_recv, int grid, cudaStream_t s);
+/* Where an expert rank's down GEMM stores its output rows: the row of slot j
+ * goes to home rank (ret[j] >> 24)'s yhome row ret[j] & 0xffffff (a peer
+ * store over NVLink, or local); the GEMM's last CTA then raises y_flag[rank]
+ * on every rank (release, after a system-scope fence of every CTA's stores). */
+struct UmmaEpOut {
+    const uint32_t *ret;
+    float *yhome[LFM_EP_MAX_RANKS];
+    uint32_t *y_flag[LFM_EP_MAX_RANKS];
+    uint32_t *done;
+    uint32_t world, rank, epoch, max_assign;
+};
 /* home rank: wait for every expert rank's y_flag, then x[t] += w . yhome[t] in k order */
 cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, cudaStream_t s);
 
@@ -228,10 +237,13 @@ cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void
 cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
 /* W0, W1: `experts` tensors [rows][cols/256] Q4_K back to back (tiles of
- * matrix m read Wm and write Ym; W1/Y1 may repeat W0/Y0 when every tile has m = 0) */
+ * matrix m read Wm and write Ym; W1/Y1 may repeat W0/Y0 when every tile has m = 0).
+ * ep (expert parallelism, down GEMM): store each row at its home rank instead of Y. */
+struct UmmaEpOut;
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
                                 const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
-                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s);
+                                const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s,
+                                const UmmaEpOut *ep = nullptr);
 
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
