@@ -80,6 +80,20 @@ __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
     }
 }
 
+/* Expert parallelism: this block's counts (s.cnt) into every rank's count
+ * table, then its cnt_flag there.  Every thread fences its own writes (the
+ * Q8_K rows and slots the expert ranks read next) before the flag. */
+__device__ void route_publish(const EpPublish &pub, const RouteSmem &s) {
+    const size_t row = ((size_t)(pub.epoch & 1u) * LFM_EP_MAX_RANKS + pub.rank) * pub.E;
+    for (uint32_t q = threadIdx.x; q < pub.world * pub.E; q += blockDim.x) {
+        const uint32_t p = q / pub.E, e = q - p * pub.E;
+        pub.table[p][row + e] = s.cnt[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, pub.epoch);
+}
+
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
     const uint32_t n = T * K;
@@ -236,7 +250,7 @@ __device__ __forceinline__ void cluster_sync_release_acquire() {
 
 __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L, const float *__restrict__ x,
                                                                    uint32_t T, uint32_t epc, Q8Rows xq,
-                                                                   RouteTables rt) {
+                                                                   RouteTables rt, EpPublish pub) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ RouteSmem s;
     __shared__ float s_inv[kClusterMaxT];
@@ -325,6 +339,10 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
         for (uint32_t q = threadIdx.x; q < T * E; q += kClusterThreads) rt.logits[q] = lg[q];
     __syncthreads();
     route_dispatch(L, T, rt, s);
+    if (pub.world) {
+        __syncthreads();
+        route_publish(pub, s);
+    }
 }
 
 /*
@@ -504,9 +522,13 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
     }
 }
 
-__global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt) {
+__global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt, EpPublish pub) {
     __shared__ RouteSmem s;
     route_dispatch(L, T, rt, s);
+    if (pub.world) {
+        __syncthreads();
+        route_publish(pub, s);
+    }
 }
 
 /* Dispatch tables alone, for rows whose experts are given (expert parallelism). */
@@ -623,7 +645,7 @@ static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uin
 
 /* T > 16: normalise + quantise, score (all experts per CTA), dispatch. */
 static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
-                                        const RouteTables &rt, cudaStream_t s) {
+                                        const RouteTables &rt, cudaStream_t s, const EpPublish &pub) {
     const size_t nsmem = sizeof(float) * kNormWarps * L.D;
     static size_t cache[16];
     cudaError_t e = lfm_smem_attr((const void *)k_norm_q8, nsmem, cache);
@@ -637,7 +659,7 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
         else e = launch_router_tiles<4, 1>(L, x, T, rt, s);
         if (e != cudaSuccess) return e;
     }
-    k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt);
+    k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt, pub);
     return cudaGetLastError();
 }
 
@@ -659,8 +681,10 @@ uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T) {
 }
 
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
-                             cudaStream_t s, bool pdl) {
+                             cudaStream_t s, bool pdl, const EpPublish *pub_in) {
     if (T == 0) return cudaSuccess;
+    const EpPublish pub = pub_in ? *pub_in : EpPublish{};
+    if (pub.world > LFM_EP_MAX_RANKS || (pub.world && L.E > LFM_GPU_MAX_EXPERTS_DEV)) return cudaErrorInvalidValue;
     uint32_t epc = 0;
     const size_t csmem = route_cluster_smem(L, T, &epc);
     if (csmem > 0) {
@@ -682,7 +706,7 @@ cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q
         attr[1].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        return cudaLaunchKernelEx(&cfg, k_route_cluster, L, x, T, epc, xq, rt);
+        return cudaLaunchKernelEx(&cfg, k_route_cluster, L, x, T, epc, xq, rt, pub);
     }
-    return launch_route_prefill(L, x, T, xq, rt, s);
+    return launch_route_prefill(L, x, T, xq, rt, s, pub);
 }

@@ -671,16 +671,33 @@ __global__ void __launch_bounds__(kXtThreads) k_xt_gather(Q8Rows X, const int32_
 
 /* Expert parallelism: the block's received slots name their home rank and
  * the home rank's slot; the Q8_K rows are read from the home rank's memory
- * (peer loads over NVLink).  The sb == 0 CTAs also record each slot's
- * assignment t*K+k at home, where the output row will go. */
+ * (over NVLink) with one bulk copy per token and super-block (256 code bytes,
+ * 32 bytes of sums) into shared memory, then laid out like k_xt_gather.  The
+ * sb == 0 CTAs also record each slot's assignment t*K+k at home, where the
+ * down GEMM stores the output row. */
+constexpr uint32_t kGxRow = 256 + 16; /* padded smem row: 16-byte chunks of consecutive tokens hit distinct banks */
+struct GatherSmem {
+    uint8_t qs[kN * kGxRow];
+    int16_t bs[kN * 16];
+    float d8[kN];
+    uint64_t bar;
+    int ok;
+};
 __global__ void __launch_bounds__(kXtThreads) k_xt_gather_ep(EpGather g, const UTokBlock *tbs, const int32_t *n_tb,
-                                                      uint32_t nb, uint32_t nt, uint8_t *xt) {
-    __shared__ XtRow rows[kN];
+                                                             uint32_t nb, uint32_t nt, uint8_t *xt) {
+    extern __shared__ __align__(128) uint8_t gx_raw[];
+    GatherSmem &S = *reinterpret_cast<GatherSmem *>(gx_raw);
     const int tb = blockIdx.x;
     if (tb >= __ldcg(n_tb)) return;
     const uint32_t sb = blockIdx.y, cols = nb * 256;
     const UTokBlock blk = tbs[tb];
-    if (threadIdx.x < kN && (int)threadIdx.x < blk.ntok) {
+    const int ntok = blk.ntok;
+    if (threadIdx.x == 0) {
+        lfm_mbar_init(&S.bar, 1);
+        lfm_fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x < kN && (int)threadIdx.x < ntok) {
         const int t = threadIdx.x;
         const uint32_t v = __ldcg(g.rowmap + blk.slot0 + t);
         uint32_t r = v >> 24, a = 0;
@@ -691,11 +708,46 @@ __global__ void __launch_bounds__(kXtThreads) k_xt_gather_ep(EpGather g, const U
             a = 0;
         }
         const size_t row = a / g.K;
-        rows[t] = XtRow{g.qs[r] + row * cols, g.d[r] + row * nb, g.bs[r] + row * nb * 16};
         if (sb == 0) g.ret[blk.slot0 + t] = (r << 24) | a;
+        if (t == 0) lfm_mbar_arrive_tx(&S.bar, (uint32_t)ntok * (256u + 32u));
+        __syncwarp(__activemask()); /* the expected bytes are posted before any copy of warp 0 lands */
+        lfm_bulk_g2s_plain(S.qs + t * kGxRow, g.qs[r] + row * cols + 256 * sb, 256u, &S.bar);
+        lfm_bulk_g2s_plain(S.bs + t * 16, g.bs[r] + (row * nb + sb) * 16, 32u, &S.bar);
+        S.d8[t] = __ldcg(g.d[r] + row * nb + sb);
     }
+    if (threadIdx.x == 0) S.ok = ntok <= 0 || lfm_mbar_wait(&S.bar, 0, g.err) ? 1 : 0;
     __syncthreads();
-    xt_copy_block(rows, blk.ntok, sb, nt, xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt));
+    if (!S.ok) { /* copies in flight land within microseconds: let them before the CTA's memory goes */
+        const uint64_t t0 = lfm_globaltimer();
+        while (lfm_globaltimer() - t0 < 2000000ull) {
+        }
+        return;
+    }
+    uint8_t *dst = xt + ((size_t)tb * nb + sb) * xt_sb_bytes(nt);
+    for (uint32_t q = threadIdx.x; q < nt * 16; q += kXtThreads) {
+        const uint32_t c = q / nt, t = q % nt;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if ((int)t < ntok) v = *reinterpret_cast<const uint4 *>(S.qs + t * kGxRow + 16 * c);
+        *reinterpret_cast<uint4 *>(dst + (c >> 3) * nt * kHalf + (c & 7) * 16 * nt + 16 * t) = v;
+    }
+    if (threadIdx.x < nt) {
+        const int t = threadIdx.x;
+        float d8 = 0.0f;
+        uint4 pr = make_uint4(0u, 0u, 0u, 0u);
+        if (t < ntok) {
+            d8 = S.d8[t];
+            const int16_t *bs = S.bs + t * 16;
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int lo = bs[4 * i] + bs[4 * i + 1], hi = bs[4 * i + 2] + bs[4 * i + 3];
+                w[i] = (uint32_t)(uint16_t)lo | ((uint32_t)(uint16_t)hi << 16);
+            }
+            pr = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        reinterpret_cast<float *>(dst + 2 * nt * kHalf)[t] = d8;
+        reinterpret_cast<uint4 *>(dst + 2 * nt * kHalf + nt * 4)[t] = pr;
+    }
 }
 
 /* Q8_K of one 256-value block held 8 per lane (elements 8*lane..) -- the
@@ -790,7 +842,11 @@ cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void
                                     uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
     const uint32_t nb = cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
-    k_xt_gather_ep<<<dim3(max_tb, nb), kXtThreads, 0, s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
+    static size_t cache[16];
+    const cudaError_t e = lfm_smem_attr((const void *)k_xt_gather_ep, sizeof(GatherSmem), cache);
+    if (e != cudaSuccess) return e;
+    k_xt_gather_ep<<<dim3(max_tb, nb), kXtThreads, sizeof(GatherSmem), s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb,
+                                                                             nb, nt, xt);
     return cudaGetLastError();
 }
 

@@ -1311,13 +1311,22 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t l
     rt.perm = es.self.perm;
     rt.loads = nullptr;
     rt.plan = UmmaPlanOut{};
-    if (T) {
-        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, false); },
+    if (T) { /* the dispatch kernel publishes the counts */
+        EpPublish pub{};
+        for (uint32_t r = 0; r < p.world; ++r) {
+            pub.table[r] = es.table[r];
+            pub.cnt_flag[r] = es.cnt_flag[r];
+        }
+        pub.world = p.world;
+        pub.rank = p.rank;
+        pub.E = p.E;
+        pub.epoch = es.epoch;
+        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, false, &pub); },
                           lfm_route_kernels(L, T)));
     } else {
         LFM_CUDA(h, cudaMemsetAsync(rt.counts, 0, sizeof(int32_t) * p.E, s));
+        LFM_CUDA(h, timed(h, K_EP_PUBLISH, s, [&] { return lfm_launch_ep_publish(es, rt.counts, s); }));
     }
-    LFM_CUDA(h, timed(h, K_EP_PUBLISH, s, [&] { return lfm_launch_ep_publish(es, rt.counts, s); }));
 
     /* expert role: the rows every rank routed to this shard, token blocks sized to the expected load */
     MoeLayerDev Lx = L;

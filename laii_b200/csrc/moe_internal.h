@@ -101,8 +101,10 @@ cudaError_t lfm_smem_attr(const void *fn, size_t smem, size_t *cache16);
 /* k_route.cu */
 /* dispatch tables only, from rt.idx already filled (one block) */
 cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s);
+struct EpPublish;
+/* pub (expert parallelism): the dispatch step also publishes the per-expert counts to every rank */
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
-                             cudaStream_t s, bool pdl);
+                             cudaStream_t s, bool pdl, const EpPublish *pub = nullptr);
 /* kernel launches lfm_launch_route makes for (L, T) */
 uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T);
 
@@ -184,7 +186,15 @@ __host__ __device__ inline uint32_t lfm_ep_first(uint32_t r, uint32_t E, uint32_
     const uint32_t base = E / world, rem = E % world;
     return r * base + (r < rem ? r : rem);
 }
-/* home rank: publish rt.counts[E] into every rank's table, then its cnt_flag */
+/* A home rank's per-expert counts of one step, into every rank's table, then
+ * its cnt_flag there (release, after a system-scope fence of the writes that
+ * precede it: the Q8_K rows and slots the expert ranks read next). */
+struct EpPublish {
+    int32_t *table[LFM_EP_MAX_RANKS];
+    uint32_t *cnt_flag[LFM_EP_MAX_RANKS];
+    uint32_t world, rank, E, epoch; /* world == 0: nothing to publish */
+};
+/* publish rt.counts[E] on its own (a step with no tokens, where no dispatch runs) */
 cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaStream_t s);
 /* expert rank: wait for every rank's counts, then the received slots' layout
  * (rowmap, n_recv) and the tcgen05 tile plans of the local experts
