@@ -436,15 +436,15 @@ def run_stack(args, cfg):
         if not use_ep:
             g.forward_device(0, x.data_ptr(), Tl, stream=sp, n_layers=len(layers))
             return
+        if p2p:  # the whole stack in one call: a captured CUDA graph after the first step
+            g.ep_p2p_forward_stack(0, len(layers), x.data_ptr(), Tl, sp)
+            ops.launches += g.last_stats()["kernels_launched"]
+            return
         for kind, l in layers:
             if kind == "dense":
                 g.forward_device(l, x.data_ptr(), Tl, stream=sp)
-            elif p2p:
-                g.ep_p2p_forward(l, x.data_ptr(), Tl, sp)
             else:
                 ep.ep_forward(ops, comm, l, x, E, K)
-            if p2p:
-                ops.launches += g.last_stats()["kernels_launched"]
 
     for _ in range(args.warmup):
         step()

@@ -187,6 +187,14 @@ lfm_gpu_status_t lfm_gpu_moe_ep_p2p_connect(lfm_gpu_moe_t *h, const void *handle
  * the ranks.  Asynchronous on `stream`. */
 lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T, void *stream);
 
+/* Layers [first, first + n) in order on the same device x[T][D]: MoE layers as
+ * the step above, dense layers whole on this rank.  The launches of a (first,
+ * n, T, x) are captured into a CUDA graph on first use and replayed after
+ * (the step epoch lives in device memory, so a replay needs no new
+ * arguments).  Asynchronous on `stream`. */
+lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x,
+                                                  uint32_t T, void *stream);
+
 /* A check of the bounded-wait path: one device wait for a step that no rank
  * will ever signal, bounded by attach's wait_ms.  The next lfm_gpu_moe_sync
  * returns LFM_GPU_ERR_TIMEOUT and the handle stays usable (the step counter

@@ -49,6 +49,7 @@ GPU_API = [
     ("lfm_gpu_moe_ep_p2p_attach", c_int, [c_vp, c_int, c_int, c_u32, c_u32, c_u32, c_u32, c_u32, c_u32, c_vp]),
     ("lfm_gpu_moe_ep_p2p_connect", c_int, [c_vp, c_vp]),
     ("lfm_gpu_moe_ep_p2p_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp]),
+    ("lfm_gpu_moe_ep_p2p_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_vp]),
     ("lfm_gpu_moe_ep_p2p_wait_check", c_int, [c_vp, c_vp]),
     ("lfm_gpu_moe_ep_p2p_detach", c_int, [c_vp]),
     ("lfm_gpu_moe_reserve", c_int, [c_vp, c_u32]),

@@ -14,8 +14,10 @@
  *   k_ep_combine_wait  home rank: acquire every y_flag, then
  *                      x[t] = fma(w[t][k], yhome[t*K+k], x[t]) for k in order
  *                      (tools/lfm2_moe_checkpoint.c:266-269).
- * Flags hold the epoch of the layer step; waits compare wrap-safe and are
- * bounded by EpStep::wait_ns (LFM_DEVERR_TIMEOUT, then the kernel returns).
+ * Flags hold the epoch of the layer step, read from the rank's device-side
+ * step counter (the combine's last CTA advances it); waits compare wrap-safe
+ * and are bounded by EpStep::wait_ns (LFM_DEVERR_TIMEOUT, then the kernel
+ * returns).
  * Buffer reuse needs no further handshake: a home rank overwrites its Q8_K
  * rows, perm and count-table entries for step n+1 only after its combine of
  * step n saw every expert rank's y_flag, which each raises after it gathered
@@ -30,21 +32,31 @@
 namespace {
 
 __global__ void __launch_bounds__(256) k_ep_publish(EpStep st, const int32_t *__restrict__ counts) {
-    const size_t row = ((size_t)(st.epoch & 1u) * LFM_EP_MAX_RANKS + st.rank) * st.E;
+    const uint32_t epoch = __ldcg(st.self.step) + st.ahead;
+    const size_t row = ((size_t)(epoch & 1u) * LFM_EP_MAX_RANKS + st.rank) * st.E;
     for (uint32_t q = threadIdx.x; q < st.world * st.E; q += blockDim.x) {
         const uint32_t p = q / st.E, e = q - p * st.E;
         st.table[p][row + e] = __ldcg(counts + e);
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < st.world) lfm_st_release_sys(st.cnt_flag[threadIdx.x] + st.rank, st.epoch);
+    if (threadIdx.x < st.world) lfm_st_release_sys(st.cnt_flag[threadIdx.x] + st.rank, epoch);
 }
 
 /* x[t][c..c+3] = fma(w[t][k], yhome[t*K+k][c..c+3], x) for k = 0..K-1 in order. */
 __global__ void __launch_bounds__(256) k_ep_combine_wait(EpStep st, float *__restrict__ x, uint32_t T,
-                                                         const float *__restrict__ w) {
+                                                         const float *__restrict__ w, int advance) {
     __shared__ int ok;
-    if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.y_flag, st.world, st.epoch, st.wait_ns, st.err) ? 1 : 0;
+    if (threadIdx.x == 0) {
+        const uint32_t epoch = __ldcg(st.self.step) + st.ahead;
+        ok = lfm_wait_flags(st.self.y_flag, st.world, epoch, st.wait_ns, st.err) ? 1 : 0;
+        /* the step is over for this rank once every CTA has read its epoch: the last one advances it */
+        __threadfence();
+        if (advance && atomicAdd(st.self.cdone, 1u) == gridDim.x - 1) {
+            atomicExch(st.self.cdone, 0u);
+            atomicExch(st.self.step, epoch);
+        }
+    }
     __syncthreads();
     if (!ok) return;
     const uint32_t D4 = st.D / 4, K = st.K;
@@ -73,12 +85,13 @@ cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaS
     return cudaGetLastError();
 }
 
-cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, cudaStream_t s) {
+cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, bool advance,
+                                       cudaStream_t s) {
     if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.D % 4) return cudaErrorInvalidValue;
     const uint64_t n = (uint64_t)T * (st.D / 4);
     uint64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks == 0) blocks = 1; /* T == 0 still waits: no rank runs ahead of the step */
-    k_ep_combine_wait<<<(unsigned)blocks, 256, 0, s>>>(st, x, T, w);
+    k_ep_combine_wait<<<(unsigned)blocks, 256, 0, s>>>(st, x, T, w, advance ? 1 : 0);
     return cudaGetLastError();
 }

@@ -84,14 +84,15 @@ __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
  * table, then its cnt_flag there.  Every thread fences its own writes (the
  * Q8_K rows and slots the expert ranks read next) before the flag. */
 __device__ void route_publish(const EpPublish &pub, const RouteSmem &s) {
-    const size_t row = ((size_t)(pub.epoch & 1u) * LFM_EP_MAX_RANKS + pub.rank) * pub.E;
+    const uint32_t epoch = __ldcg(pub.step) + 1u;
+    const size_t row = ((size_t)(epoch & 1u) * LFM_EP_MAX_RANKS + pub.rank) * pub.E;
     for (uint32_t q = threadIdx.x; q < pub.world * pub.E; q += blockDim.x) {
         const uint32_t p = q / pub.E, e = q - p * pub.E;
         pub.table[p][row + e] = s.cnt[e];
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, pub.epoch);
+    if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, epoch);
 }
 
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
@@ -553,14 +554,15 @@ __global__ void __launch_bounds__(1024) k_ep_plan(EpStep st, uint32_t first, uin
     const UmmaPlanOut &P = rt.plan;
     const uint32_t W = st.world, E = st.E;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.cnt_flag, W, st.epoch, st.wait_ns, st.err) ? 1 : 0;
+    const uint32_t epoch = __ldcg(st.self.step) + st.ahead;
+    if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.cnt_flag, W, epoch, st.wait_ns, st.err) ? 1 : 0;
     __syncthreads();
     if (!ok) {
         if (threadIdx.x < 4) P.counts[threadIdx.x] = 0;
         if (threadIdx.x == 0) *st.self.n_recv = 0;
         return;
     }
-    const int32_t *t0 = st.self.table + (size_t)(st.epoch & 1u) * LFM_EP_MAX_RANKS * E;
+    const int32_t *t0 = st.self.table + (size_t)(epoch & 1u) * LFM_EP_MAX_RANKS * E;
     for (uint32_t q = threadIdx.x; q < W * E; q += blockDim.x) tab[q / E][q % E] = lfm_ld_relaxed_sys(t0 + q);
     __syncthreads();
     if (threadIdx.x < W) { /* home rank r's slot prefix up to each of this shard's experts */

@@ -596,7 +596,8 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
         /* the last CTA: every row of this rank is stored at its home rank */
         atomicExch(ep.done, 0u);
         __threadfence_system();
-        for (uint32_t p = 0; p < ep.world; ++p) lfm_st_release_sys(ep.y_flag[p] + ep.rank, ep.epoch);
+        const uint32_t epoch = __ldcg(ep.step) + 1u;
+        for (uint32_t p = 0; p < ep.world; ++p) lfm_st_release_sys(ep.y_flag[p] + ep.rank, epoch);
     }
 }
 
@@ -903,7 +904,7 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
                                 const UmmaEpOut *ep) {
     if (rows % kM || cols % 256 || experts == 0 || nt % 16 || nt == 0 || nt > (uint32_t)kN)
         return cudaErrorInvalidValue;
-    if (ep && (!ep->ret || !ep->done || ep->world == 0 || ep->world > LFM_EP_MAX_RANKS)) return cudaErrorInvalidValue;
+    if (ep && (!ep->ret || !ep->done || !ep->step || ep->world == 0 || ep->world > LFM_EP_MAX_RANKS)) return cudaErrorInvalidValue;
     /* each expert tensor as a 2-D byte matrix [experts * rows][nb * 144] */
     CUtensorMap tm0, tm1;
     const uint64_t row_bytes = (uint64_t)(cols / 256) * kRaw;

@@ -74,6 +74,7 @@ struct ProfRec {
 /* One captured forward: layers [first, first+n) on x for T tokens. */
 struct GraphEntry {
     uint32_t first, n, T;
+    bool ep;  /* MoE layers as expert-parallel steps over peer memory */
     float *x;
     uint32_t kernels;
     cudaGraphExec_t exec;
@@ -88,14 +89,13 @@ struct EpP2P {
     bool attached = false, connected = false;
     uint32_t rank = 0, world = 1, T_max = 0, D = 0, E = 0, K = 0, I = 0;
     uint64_t wait_ns = 0;
-    uint32_t epoch = 0;
     uint8_t *arena = nullptr;
     size_t bytes = 0;
     uint8_t *peer[LFM_EP_MAX_RANKS] = {};  /* peer[rank] == arena */
     bool opened[LFM_EP_MAX_RANKS] = {};    /* mapped through cudaIpcOpenMemHandle */
     /* byte offsets of the arena's parts (the same on every rank) */
     size_t o_cnt = 0, o_y = 0, o_done = 0, o_tab = 0, o_qs = 0, o_qd = 0, o_qb = 0, o_perm = 0, o_yhome = 0,
-           o_rowmap = 0, o_ret = 0, o_nrecv = 0;
+           o_rowmap = 0, o_ret = 0, o_nrecv = 0, o_step = 0, o_cdone = 0;
     uint32_t max_recv() const { return world * T_max * K; }
 };
 }  // namespace
@@ -667,19 +667,31 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_toke
     return ensure_workspace(h, max_tokens, D, E, K, I);
 }
 
+namespace {
+lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s);
+}  // namespace
+
+/* Layer l of a stack: expert-parallel step for a MoE shard when ep, else the regular forward. */
+static lfm_gpu_status_t stack_layer(lfm_gpu_moe_t *h, uint32_t l, float *x, uint32_t T, cudaStream_t s, bool ep) {
+    const LayerSlot &S = h->layers[l];
+    if (ep && !S.dev.dense) return ep_forward_layer(h, S, x, T, s);
+    if (T == 0) return LFM_GPU_OK;
+    return forward_layer(h, S, x, T, s);
+}
+
 /* Replay (capturing on first use) the graph of layers [first, first+n) on x.
  * Capture runs on the handle's own stream (never the caller's, which may be
  * the legacy default stream); the replay is launched on the caller's stream. */
 static lfm_gpu_status_t run_graph(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x, uint32_t T,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, bool ep = false) {
     GraphEntry *hit = nullptr;
     for (GraphEntry &g : h->graphs)
-        if (g.first == first && g.n == n && g.T == T && g.x == x) { hit = &g; break; }
+        if (g.first == first && g.n == n && g.T == T && g.x == x && g.ep == ep) { hit = &g; break; }
     if (!hit) {
         /* first call with this key: run eagerly (kernel attributes get set
          * outside any capture), then capture the same launches for replay */
         for (uint32_t l = first; l < first + n; ++l) {
-            lfm_gpu_status_t st = forward_layer(h, h->layers[l], x, T, s);
+            lfm_gpu_status_t st = stack_layer(h, l, x, T, s, ep);
             if (st != LFM_GPU_OK) return st;
         }
         if (h->graphs.size() >= kMaxGraphs) {
@@ -690,7 +702,7 @@ static lfm_gpu_status_t run_graph(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, 
         const uint32_t k0 = h->stats.kernels_launched;
         lfm_gpu_status_t st = LFM_GPU_OK;
         for (uint32_t l = first; l < first + n && st == LFM_GPU_OK; ++l)
-            st = forward_layer(h, h->layers[l], x, T, h->stream);
+            st = stack_layer(h, l, x, T, h->stream, ep);
         cudaGraph_t graph = nullptr;
         const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
         if (st != LFM_GPU_OK) { if (graph) cudaGraphDestroy(graph); return st; }
@@ -699,7 +711,7 @@ static lfm_gpu_status_t run_graph(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, 
         const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         if (ie != cudaSuccess) return cuda_fail(h, ie, "cudaGraphInstantiate");
-        h->graphs.push_back(GraphEntry{first, n, T, x, h->stats.kernels_launched - k0, exec});
+        h->graphs.push_back(GraphEntry{first, n, T, ep, x, h->stats.kernels_launched - k0, exec});
         h->stats.kernels_launched = k0;
         return LFM_GPU_OK;
     }
@@ -1139,6 +1151,8 @@ void ep_layout(EpP2P &p) {
     p.o_rowmap = take(sizeof(uint32_t) * R);
     p.o_ret = take(sizeof(uint32_t) * R);
     p.o_nrecv = take(sizeof(int32_t));
+    p.o_step = take(sizeof(uint32_t));
+    p.o_cdone = take(sizeof(uint32_t));
     p.bytes = off;
 }
 
@@ -1155,6 +1169,8 @@ EpArena ep_arena_view(const EpP2P &p, uint8_t *b) {
     a.rowmap = reinterpret_cast<uint32_t *>(b + p.o_rowmap);
     a.ret = reinterpret_cast<uint32_t *>(b + p.o_ret);
     a.n_recv = reinterpret_cast<int32_t *>(b + p.o_nrecv);
+    a.step = reinterpret_cast<uint32_t *>(b + p.o_step);
+    a.cdone = reinterpret_cast<uint32_t *>(b + p.o_cdone);
     return a;
 }
 
@@ -1248,79 +1264,74 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_detach(lfm_gpu_moe_t *h) {
     if (!h->ep.attached) return LFM_GPU_OK;
     DeviceGuard g(h->device);
     const cudaError_t e = cudaDeviceSynchronize();
+    drop_graphs(h); /* captured steps hold the peer mappings */
     ep_release(h);
     if (e != cudaSuccess) return cuda_fail(h, e, "ep_p2p_detach: sync");
     return LFM_GPU_OK;
 }
 
-LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
-                                                    void *stream) {
-    const LayerSlot *S = nullptr;
-    lfm_gpu_status_t st = ep_layer(h, layer, &S);
-    if (st != LFM_GPU_OK) return st;
-    EpP2P &p = h->ep;
-    if (!p.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_forward: attach and connect first");
-    const MoeLayerDev &L = S->dev;
-    const uint32_t first = lfm_ep_first(p.rank, p.E, p.world),
-                   count = lfm_ep_first(p.rank + 1, p.E, p.world) - first;
-    if (L.D != p.D || L.E != p.E || L.K != p.K || L.I != p.I)
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: layer %u is %ux%ux%ux%u, the arena %ux%ux%ux%u", layer,
-                    L.D, L.E, L.K, L.I, p.D, p.E, p.K, p.I);
-    if (S->ep_first != first || (S->ep_count ? S->ep_count : L.E) != count)
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: layer %u holds experts [%u, %u), rank %u owns [%u, %u)",
-                    layer, S->ep_first, S->ep_first + (S->ep_count ? S->ep_count : L.E), p.rank, first, first + count);
-    if (T > p.T_max) return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: T=%u above max_tokens %u", T, p.T_max);
-    if (T && (!x || (reinterpret_cast<uintptr_t>(x) & 15u)))
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: device x must be 16-byte aligned");
-    DeviceGuard g(h->device);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    Workspace &w = h->ws;
-    const int grid = h->sm_count;
-    h->stats = lfm_gpu_moe_stats_t{};
-    h->stats.tokens = T;
+namespace {
 
+/* The layer must be this rank's shard of an arena-shaped MoE layer. */
+lfm_gpu_status_t ep_check_layer(lfm_gpu_moe_t *h, uint32_t layer, const LayerSlot &S) {
+    const EpP2P &p = h->ep;
+    const MoeLayerDev &L = S.dev;
+    const uint32_t first = lfm_ep_first(p.rank, p.E, p.world), count = lfm_ep_first(p.rank + 1, p.E, p.world) - first;
+    if (L.dense || L.D != p.D || L.E != p.E || L.K != p.K || L.I != p.I)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p: layer %u is not a %ux%ux%ux%u MoE layer", layer, p.D, p.E,
+                    p.K, p.I);
+    if (S.ep_first != first || (S.ep_count ? S.ep_count : L.E) != count)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p: layer %u holds experts [%u, %u), rank %u owns [%u, %u)", layer,
+                    S.ep_first, S.ep_first + (S.ep_count ? S.ep_count : L.E), p.rank, first, first + count);
+    return LFM_GPU_OK;
+}
+
+/* This step's arguments: this rank's arena and every rank's mapping of its own. */
+EpStep ep_step_args(lfm_gpu_moe_t *h, uint32_t ahead) {
+    const EpP2P &p = h->ep;
     EpStep es{};
     es.rank = p.rank; es.world = p.world; es.E = p.E; es.K = p.K; es.D = p.D;
-    es.epoch = ++p.epoch;
+    es.ahead = ahead;
     es.max_assign = p.T_max * p.K;
     es.max_recv = p.max_recv();
     es.wait_ns = p.wait_ns;
     es.err = h->dev_err;
     es.self = ep_arena_view(p, p.arena);
-    EpGather eg{};
-    eg.rowmap = es.self.rowmap;
-    eg.ret = es.self.ret;
-    eg.err = h->dev_err;
-    eg.K = p.K;
-    eg.world = p.world;
-    eg.max_assign = es.max_assign;
     for (uint32_t r = 0; r < p.world; ++r) {
         const EpArena a = ep_arena_view(p, p.peer[r]);
         es.table[r] = a.table;
         es.cnt_flag[r] = a.cnt_flag;
         es.y_flag[r] = a.y_flag;
         es.yhome[r] = a.yhome;
-        eg.perm[r] = a.perm;
-        eg.qs[r] = a.xq.qs;
-        eg.d[r] = a.xq.d;
-        eg.bs[r] = a.xq.bs;
     }
+    return es;
+}
 
-    /* home role: route this rank's tokens into the arena (Q8_K rows, slots) and publish the counts */
+/* One expert-parallel layer step on stream s: launches only (no host
+ * synchronisation, no host-side step state), so it can be captured. */
+lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, uint32_t T, cudaStream_t s) {
+    const EpP2P &p = h->ep;
+    const MoeLayerDev &L = S.dev;
+    const uint32_t first = lfm_ep_first(p.rank, p.E, p.world), count = lfm_ep_first(p.rank + 1, p.E, p.world) - first;
+    Workspace &w = h->ws;
+    const int grid = h->sm_count;
+    const EpStep es = ep_step_args(h, 1);
+
+    /* home role: route this rank's tokens into the arena (Q8_K rows, slots); the dispatch publishes the counts */
     RouteTables rt = w.rt;
     rt.perm = es.self.perm;
     rt.loads = nullptr;
     rt.plan = UmmaPlanOut{};
-    if (T) { /* the dispatch kernel publishes the counts */
+    if (T) {
         EpPublish pub{};
         for (uint32_t r = 0; r < p.world; ++r) {
             pub.table[r] = es.table[r];
             pub.cnt_flag[r] = es.cnt_flag[r];
         }
+        pub.step = es.self.step;
         pub.world = p.world;
         pub.rank = p.rank;
         pub.E = p.E;
-        pub.epoch = es.epoch;
         LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, false, &pub); },
                           lfm_route_kernels(L, T)));
     } else {
@@ -1329,9 +1340,6 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t l
     }
 
     /* expert role: the rows every rank routed to this shard, token blocks sized to the expected load */
-    MoeLayerDev Lx = L;
-    Lx.E = count;
-    Lx.K = 1;
     UmmaPlanOut plan{};
     plan.nt = lfm_umma_nt(T ? T * p.K : p.K, count); /* T*K rows expected per shard on average */
     plan.rows_gu = L.I;
@@ -1345,14 +1353,28 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t l
     plan.max_gu = 2 * (uint32_t)lfm_umma_tiles_max(L.I, R, count, plan.nt);
     plan.max_dn = (uint32_t)lfm_umma_tiles_max(L.D, R, count, plan.nt);
     if (plan.max_tb > w.umax_tb || plan.max_gu > w.umax_gu || plan.max_dn > w.umax_dn)
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: tile plan capacity (internal)");
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p: tile plan capacity (internal)");
     RouteTables rx = w.rt;
     rx.plan = plan;
     const uint32_t nt = plan.nt, mtb = plan.max_tb;
+    EpGather eg{};
+    eg.rowmap = es.self.rowmap;
+    eg.ret = es.self.ret;
+    eg.err = h->dev_err;
+    eg.K = p.K;
+    eg.world = p.world;
+    eg.max_assign = es.max_assign;
+    for (uint32_t r = 0; r < p.world; ++r) {
+        const EpArena a = ep_arena_view(p, p.peer[r]);
+        eg.perm[r] = a.perm;
+        eg.qs[r] = a.xq.qs;
+        eg.d[r] = a.xq.d;
+        eg.bs[r] = a.xq.bs;
+    }
     LFM_CUDA(h, timed(h, K_EP_PLAN, s, [&] { return lfm_launch_ep_plan(es, first, count, rx, s); }));
     LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather_ep(eg, L.D, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
     LFM_CUDA(h, timed(h, K_GEMM_GU, s, [&] {
-        return lfm_launch_q4k_umma(Lx.gate, Lx.up, count, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
+        return lfm_launch_q4k_umma(L.gate, L.up, count, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
                                    h->dev_err, grid, s);
     }));
     LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
@@ -1365,35 +1387,84 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t l
         eo.y_flag[r] = es.y_flag[r];
     }
     eo.done = es.self.done;
+    eo.step = es.self.step;
     eo.world = p.world;
     eo.rank = p.rank;
-    eo.epoch = es.epoch;
     eo.max_assign = es.max_assign;
     LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
-        return lfm_launch_q4k_umma(Lx.down, Lx.down, count, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y,
+        return lfm_launch_q4k_umma(L.down, L.down, count, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y,
                                    w.y, h->dev_err, grid, s, &eo);
     }));
 
-    /* home role: combine the outputs the expert ranks stored here */
-    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, s); }));
+    /* home role: combine the outputs the expert ranks stored here; the step is done */
+    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, true, s); }));
     return LFM_GPU_OK;
+}
+
+}  // namespace
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
+                                                    void *stream) {
+    const LayerSlot *S = nullptr;
+    lfm_gpu_status_t st = ep_layer(h, layer, &S);
+    if (st != LFM_GPU_OK) return st;
+    if (!h->ep.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_forward: attach and connect first");
+    st = ep_check_layer(h, layer, *S);
+    if (st != LFM_GPU_OK) return st;
+    if (T > h->ep.T_max) return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: T=%u above max_tokens %u", T, h->ep.T_max);
+    if (T && (!x || (reinterpret_cast<uintptr_t>(x) & 15u)))
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward: device x must be 16-byte aligned");
+    DeviceGuard g(h->device);
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+    return ep_forward_layer(h, *S, x, T, static_cast<cudaStream_t>(stream));
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_wait_check(lfm_gpu_moe_t *h, void *stream) {
     if (!h) return LFM_GPU_ERR_INVALID_ARG;
-    EpP2P &p = h->ep;
-    if (!p.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_wait_check: attach and connect first");
+    if (!h->ep.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_wait_check: attach and connect first");
     DeviceGuard g(h->device);
-    EpStep es{};
-    es.rank = p.rank; es.world = p.world; es.E = p.E; es.K = p.K; es.D = p.D;
-    es.epoch = p.epoch + 2u; /* no rank signals a step beyond the next one */
-    es.max_assign = p.T_max * p.K;
-    es.max_recv = p.max_recv();
-    es.wait_ns = p.wait_ns;
-    es.err = h->dev_err;
-    es.self = ep_arena_view(p, p.arena);
+    const EpStep es = ep_step_args(h, 2); /* no rank signals a step beyond the next one */
     h->stats = lfm_gpu_moe_stats_t{};
     h->stats.kernels_launched = 1;
-    LFM_CUDA(h, lfm_launch_ep_combine_wait(es, nullptr, 0, nullptr, static_cast<cudaStream_t>(stream)));
+    LFM_CUDA(h, lfm_launch_ep_combine_wait(es, nullptr, 0, nullptr, false, static_cast<cudaStream_t>(stream)));
+    return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uint32_t n, float *x,
+                                                          uint32_t T, void *stream) {
+    if (!h) return LFM_GPU_ERR_INVALID_ARG;
+    if (!h->ep.connected) return fail(h, LFM_GPU_ERR_NOT_READY, "ep_p2p_forward_stack: attach and connect first");
+    if (n == 0 || first >= LFM_GPU_MOE_MAX_LAYERS || n > LFM_GPU_MOE_MAX_LAYERS - first)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer range [%u, %u+%u) invalid", first, first, n);
+    if (T > h->ep.T_max)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward_stack: T=%u above max_tokens %u", T, h->ep.T_max);
+    if (T && (!x || (reinterpret_cast<uintptr_t>(x) & 15u)))
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_forward_stack: device x must be 16-byte aligned");
+    uint32_t dI = 0;
+    for (uint32_t l = first; l < first + n; ++l) {
+        const LayerSlot &S = h->layers[l];
+        if (!S.present) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", l);
+        if (S.dev.D != h->ep.D) return fail(h, LFM_GPU_ERR_INVALID_ARG, "layer %u: D=%u, the arena's %u", l, S.dev.D, h->ep.D);
+        if (S.dev.dense) {
+            dI = S.dev.I > dI ? S.dev.I : dI;
+            continue;
+        }
+        lfm_gpu_status_t st = ep_check_layer(h, l, S);
+        if (st != LFM_GPU_OK) return st;
+    }
+    DeviceGuard g(h->device);
+    if (dI && T) { /* dense layers run whole on every rank */
+        lfm_gpu_status_t st = ensure_workspace(h, T, h->ep.D, 1, 1, dI);
+        if (st != LFM_GPU_OK) return st;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    h->stats = lfm_gpu_moe_stats_t{};
+    h->stats.tokens = T;
+    if (h->use_graphs && !h->prof) return run_graph(h, first, n, x, T, s, true);
+    for (uint32_t l = first; l < first + n; ++l) {
+        lfm_gpu_status_t st = stack_layer(h, l, x, T, s, true);
+        if (st != LFM_GPU_OK) return st;
+    }
     return LFM_GPU_OK;
 }

@@ -138,7 +138,9 @@ cudaError_t lfm_launch_gguf_to_q8(const uint8_t *in, uint32_t rows, Q8Rows q, cu
  * Every rank's exchange arena has the same layout; the host maps the other
  * ranks' arenas (CUDA IPC) so kernels read and write them directly.  Flags
  * carry the epoch of the layer step (wrap-safe compare); the count table is
- * double-buffered by epoch parity. */
+ * double-buffered by epoch parity.  The epoch lives in device memory (step:
+ * the last finished step, advanced by the combine's last CTA), so a captured
+ * CUDA graph replays step after step with the same kernel arguments. */
 #define LFM_EP_MAX_RANKS 8
 struct EpArena {
     uint32_t *cnt_flag; /* [LFM_EP_MAX_RANKS] epoch of home rank r's published counts (written by r)   */
@@ -151,10 +153,13 @@ struct EpArena {
     uint32_t *rowmap;   /* [max_recv] received slot -> (home rank << 24) | home slot (this rank only)    */
     uint32_t *ret;      /* [max_recv] received slot -> (home rank << 24) | t*K+k     (this rank only)    */
     int32_t *n_recv;    /* [1] rows received in this step (this rank only)                               */
+    uint32_t *step;     /* [1] epoch of this rank's last finished step (this rank only)                   */
+    uint32_t *cdone;    /* [1] combine CTAs finished (this rank only; kept at 0)                          */
 };
 /* What the exchange kernels of one step need: this rank's arena and every rank's view of its own. */
 struct EpStep {
-    uint32_t rank, world, E, K, D, epoch;
+    uint32_t rank, world, E, K, D;
+    uint32_t ahead;      /* the step's epoch is *self.step + ahead (1; the wait check uses 2)   */
     uint32_t max_assign; /* T*K capacity of every home rank's yhome / perm */
     uint32_t max_recv;   /* received-slot capacity of this rank          */
     uint64_t wait_ns;
@@ -192,7 +197,8 @@ __host__ __device__ inline uint32_t lfm_ep_first(uint32_t r, uint32_t E, uint32_
 struct EpPublish {
     int32_t *table[LFM_EP_MAX_RANKS];
     uint32_t *cnt_flag[LFM_EP_MAX_RANKS];
-    uint32_t world, rank, E, epoch; /* world == 0: nothing to publish */
+    const uint32_t *step;           /* epoch of the step = *step + 1 */
+    uint32_t world, rank, E;        /* world == 0: nothing to publish */
 };
 /* publish rt.counts[E] on its own (a step with no tokens, where no dispatch runs) */
 cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaStream_t s);
@@ -210,10 +216,13 @@ struct UmmaEpOut {
     float *yhome[LFM_EP_MAX_RANKS];
     uint32_t *y_flag[LFM_EP_MAX_RANKS];
     uint32_t *done;
-    uint32_t world, rank, epoch, max_assign;
+    const uint32_t *step;  /* epoch of the step = *step + 1 */
+    uint32_t world, rank, max_assign;
 };
-/* home rank: wait for every expert rank's y_flag, then x[t] += w . yhome[t] in k order */
-cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, cudaStream_t s);
+/* home rank: wait for every expert rank's y_flag, then x[t] += w . yhome[t] in k order;
+ * advance: then the rank's step counter moves to this step's epoch */
+cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, bool advance,
+                                       cudaStream_t s);
 
 /* k_gemm.cu: prefill grouped GEMM (tensor cores) */
 size_t lfm_gemm_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);

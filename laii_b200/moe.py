@@ -151,6 +151,11 @@ class GpuMoE:
         self._check(self._lib.lfm_gpu_moe_ep_p2p_forward(self._h, layer, ctypes.c_void_p(x_ptr or None), T,
                                                          ctypes.c_void_p(stream or None)))
 
+    def ep_p2p_forward_stack(self, first: int, n: int, x_ptr: int, T: int, stream: int = 0):
+        """Layers [first, first + n): MoE shards as peer-memory steps, dense layers whole (CUDA graph replay)."""
+        self._check(self._lib.lfm_gpu_moe_ep_p2p_forward_stack(self._h, first, n, ctypes.c_void_p(x_ptr or None), T,
+                                                               ctypes.c_void_p(stream or None)))
+
     def ep_p2p_wait_check(self, stream: int = 0):
         self._check(self._lib.lfm_gpu_moe_ep_p2p_wait_check(self._h, ctypes.c_void_p(stream or None)))
 

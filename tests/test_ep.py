@@ -347,6 +347,17 @@ def _p2p_rank(rank, world, port, out_dir):
             torch.cuda.synchronize()
             g.sync()
             np.save(os.path.join(out_dir, f"p2p_{i}_{rank}.npy"), xd.cpu().numpy())
+        # the same steps through the stack call: captured on first use, then graph replays
+        xbuf = torch.zeros((Tmax, D_), dtype=torch.float32, device="cuda")
+        for rep in range(3):
+            for i, Ts in enumerate(P2P_STEPS):
+                T = Ts[rank]
+                if T:
+                    xbuf[:T].copy_(torch.from_numpy(synth.make_hidden(T, D_, seed_offset=1000 * i + 100 * rank)))
+                g.ep_p2p_forward_stack(0, 2, xbuf.data_ptr() if T else 0, T, torch.cuda.current_stream().cuda_stream)
+                torch.cuda.synchronize()
+                g.sync()
+                np.save(os.path.join(out_dir, f"p2ps_{rep}_{i}_{rank}.npy"), xbuf[:T].cpu().numpy())
         dist.barrier()
         g.ep_p2p_detach()
         g.close()
@@ -373,3 +384,38 @@ def test_ep_p2p_two_gpus_match_single_gpu_forward(tmp_path):
         for r in range(world):
             got = np.load(tmp_path / f"p2p_{i}_{r}.npy")
             assert np.array_equal(got, want[r]), (i, r)
+            for rep in range(3):
+                got = np.load(tmp_path / f"p2ps_{rep}_{i}_{r}.npy")
+                assert np.array_equal(got, want[r]), ("stack", rep, i, r)
+
+
+@pytest.mark.gpu
+def test_ep_p2p_stack_world_of_one_with_dense_layer_replays():
+    """A dense layer and two MoE shard layers through the expert-parallel stack call (world of one):
+    first call eager + capture, later calls CUDA-graph replays with the device-side step counter,
+    against the regular stack forward."""
+    import torch
+    import bench
+    from laii_b200 import synth
+    from laii_b200.moe import GpuMoE
+    from conftest import cached_dense
+    D_, E_, K_, I_ = P2P_SHAPE
+    dense = cached_dense(D_, 7168)
+    x = synth.make_hidden(24, D_, seed_offset=9)
+    with GpuMoE(0) as ref:
+        ref.upload_dense(0, dense)
+        for l in (1, 2):
+            ref.synth_layer(l, D_, E_, K_, I_, bench.layer_seeds(l + 40))
+        want = ref.forward_stack(0, 3, np.array(x, copy=True))
+    with GpuMoE(0) as g:
+        g.upload_dense(0, dense)
+        for l in (1, 2):
+            g.synth_layer_shard(l, D_, E_, K_, I_, bench.layer_seeds(l + 40), 0, E_)
+        ep.p2p_connect(g, 24, D_, E_, K_, I_)
+        xbuf = torch.empty((24, D_), dtype=torch.float32, device="cuda")
+        for rep in range(4):
+            xbuf.copy_(torch.from_numpy(x))
+            g.ep_p2p_forward_stack(0, 3, xbuf.data_ptr(), 24, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            g.sync()
+            assert np.array_equal(xbuf.cpu().numpy(), want), rep
