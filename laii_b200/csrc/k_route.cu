@@ -95,12 +95,10 @@ __device__ void route_publish(const EpPublish &pub, const RouteSmem &s) {
     if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, epoch);
 }
 
-__device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteSmem &s);
-
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
     const uint32_t n = T * K;
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
     __syncthreads();
     /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
@@ -115,37 +113,6 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
         if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
     }
     __syncthreads();
-    route_tables(L, rt, s);
-    /* slots: a run of equal ids in a warp takes consecutive slots with one atomic */
-    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
-        const uint32_t a = b0 + threadIdx.x;
-        int e = -1;
-        if (a < n) {
-            e = __ldcg(rt.idx + a);
-            if ((unsigned)e >= E) e = -1;
-        }
-        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
-        const int leader = __ffs(m) - 1;
-        int base = 0;
-        if (e >= 0 && lane == leader) base = atomicAdd(&s.cur[e], __popc(m));
-        base = __shfl_sync(LFM_FULL_MASK, base, leader);
-        if (e >= 0) {
-            const int pos = s.off[e] + base + __popc(m & ((1u << lane) - 1u));
-            rt.perm[pos] = (int)a;
-            rt.inv[a] = pos;
-        } else if (a < n) {
-            rt.inv[a] = -1;
-        }
-    }
-    if (rt.plan.nt) route_plan(rt, s);
-}
-
-/* The dispatch tables from the per-expert counts in s.cnt: offsets, active
- * experts, GEMV work pairs, summary and load statistics (s.off, s.act,
- * s.uniq set for the slot pass and the tile plans). */
-__device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteSmem &s) {
-    const uint32_t E = L.dense ? 1u : L.E;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     if (threadIdx.x == 0) {
         int acc = 0, uniq = 0, mx = 0, pairs = 0;
         for (uint32_t e = 0; e < E; ++e) {
@@ -179,7 +146,28 @@ __device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteS
         const int nch = (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
         for (int c = lane; c < nch; c += 32) rt.pairs[s.pb[u] + c] = make_int2(u, c);
     }
-    __syncthreads();
+    /* slots: a run of equal ids in a warp takes consecutive slots with one atomic */
+    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
+        const uint32_t a = b0 + threadIdx.x;
+        int e = -1;
+        if (a < n) {
+            e = __ldcg(rt.idx + a);
+            if ((unsigned)e >= E) e = -1;
+        }
+        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+        const int leader = __ffs(m) - 1;
+        int base = 0;
+        if (e >= 0 && lane == leader) base = atomicAdd(&s.cur[e], __popc(m));
+        base = __shfl_sync(LFM_FULL_MASK, base, leader);
+        if (e >= 0) {
+            const int pos = s.off[e] + base + __popc(m & ((1u << lane) - 1u));
+            rt.perm[pos] = (int)a;
+            rt.inv[a] = pos;
+        } else if (a < n) {
+            rt.inv[a] = -1;
+        }
+    }
+    if (rt.plan.nt) route_plan(rt, s);
 }
 
 /* Top-K of token t from its E logits (global memory written by other blocks,
@@ -535,162 +523,6 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
     }
 }
 
-/*
- * k_route_fused (T > 16, D <= 2048): the whole route of a layer in one launch.
- * CTA (tile, g) holds tokens [tile*TT, +TT) and router rows [g*8, +8) in
- * shared memory (one bulk copy per row), forms each token's RMSNorm and xb
- * exactly as k_norm_q8 does (the g == 0 CTAs also write Q8_K of xb and 1/rms),
- * and runs the reference's 16 column chains per (token, expert) pair.  The
- * last CTA of a token tile to arrive (a counter per tile) takes the tile's
- * top-K and counts its assignments per expert with one global atomic each,
- * keeping the returned rank; the last tile to finish (one more counter) turns
- * the counts into the dispatch tables, places every assignment at its
- * expert's offset plus its rank (the order inside an expert segment does not
- * change any result), builds the tcgen05 tile plans and, for expert
- * parallelism, publishes the counts.  Counters and per-expert cursors return
- * to zero for the next launch.
- */
-constexpr int kRfExperts = 8;
-constexpr uint32_t kRfMaxD = 2048;
-
-template <int TT, int TPT, int EPT>
-__global__ void __launch_bounds__(256) k_route_fused(MoeLayerDev L, const float *__restrict__ x, uint32_t T,
-                                                     Q8Rows xq, RouteTables rt, EpPublish pub) {
-    static_assert((TT / TPT) * (kRfExperts / EPT) == 16, "16 groups of 16 chain lanes");
-    extern __shared__ __align__(128) uint8_t dsm[];
-    __shared__ RouteSmem s;
-    __shared__ uint64_t bar;
-    __shared__ float s_inv[TT];
-    __shared__ int s_flag;
-    const uint32_t D = L.D, E = L.E, K = L.K;
-    float *xs = reinterpret_cast<float *>(dsm);  /* [TT][D]: x, then xb */
-    float *ws = xs + (size_t)TT * D;             /* [8][D] router rows  */
-    const uint32_t tile = blockIdx.x, tok0 = tile * TT, e0 = blockIdx.y * kRfExperts;
-    const uint32_t nt = min((uint32_t)TT, T - tok0), ne = min((uint32_t)kRfExperts, E - e0);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
-        lfm_mbar_init(&bar, 1);
-        lfm_fence_mbar_init();
-        lfm_mbar_arrive_tx(&bar, (nt + ne) * D * 4u);
-        for (uint32_t t = 0; t < nt; ++t) lfm_bulk_g2s_plain(xs + (size_t)t * D, x + (size_t)(tok0 + t) * D, D * 4u, &bar);
-        for (uint32_t e = 0; e < ne; ++e)
-            lfm_bulk_g2s_plain(ws + (size_t)e * D, L.router_w + (size_t)(e0 + e) * D, D * 4u, &bar);
-        s_flag = lfm_mbar_wait(&bar, 0, rt.err) ? 1 : 0;
-    }
-    __syncthreads();
-    if (!s_flag) { /* copies in flight land within microseconds: let them before the CTA's memory goes */
-        const uint64_t t0 = lfm_globaltimer();
-        while (lfm_globaltimer() - t0 < 2000000ull) {
-        }
-        return;
-    }
-    /* RMSNorm: one warp per token, lanes 0-15 run the reference's 16 chains */
-    for (uint32_t t = warp; t < nt; t += 8) {
-        const float *xr = xs + (size_t)t * D;
-        float acc = 0.0f;
-        if (lane < 16)
-            for (uint32_t i = 0; i < D; i += 16) acc = __fmaf_rn(xr[i + lane], xr[i + lane], acc);
-        const float ss = lfm_hsum16_ref(acc);
-        const float inv = __shfl_sync(LFM_FULL_MASK, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps))), 0);
-        if (lane == 0) s_inv[t] = inv;
-        if (blockIdx.y == 0) {
-            if (lane == 0) rt.rms[tok0 + t] = inv;
-            for (uint32_t b = 0; b < D / 256; ++b) {
-                float v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t c = 256 * b + 8 * lane + i;
-                    const float n = __fmul_rn(xr[c], inv);
-                    v[i] = L.ffn_norm ? __fmul_rn(n, __ldg(L.ffn_norm + c)) : n;
-                }
-                lfm_quant_block_warp(v, xq, tok0 + t, b);
-            }
-        }
-    }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < nt * D; i += blockDim.x) {
-        const uint32_t t = i / D, c = i - t * D;
-        const float n = __fmul_rn(xs[i], s_inv[t]);
-        xs[i] = L.ffn_norm ? __fmul_rn(n, __ldg(L.ffn_norm + c)) : n;
-    }
-    __syncthreads();
-    {   /* chain l of TPT tokens x EPT experts */
-        const int l = threadIdx.x & 15, g = threadIdx.x >> 4;
-        const int tg = g % (TT / TPT), eg = g / (TT / TPT);
-        float acc[TPT][EPT];
-#pragma unroll
-        for (int j = 0; j < TPT; ++j)
-#pragma unroll
-            for (int k = 0; k < EPT; ++k) acc[j][k] = 0.0f;
-        const float *xb = xs + (size_t)(tg * TPT) * D + l;
-        const float *wb = ws + (size_t)(eg * EPT) * D + l;
-#pragma unroll 4
-        for (uint32_t i = 0; i < D; i += 16) {
-            float xv[TPT], wv[EPT];
-#pragma unroll
-            for (int j = 0; j < TPT; ++j) xv[j] = xb[(size_t)j * D + i];
-#pragma unroll
-            for (int k = 0; k < EPT; ++k) wv[k] = wb[(size_t)k * D + i];
-#pragma unroll
-            for (int j = 0; j < TPT; ++j)
-#pragma unroll
-                for (int k = 0; k < EPT; ++k) acc[j][k] = __fmaf_rn(wv[k], xv[j], acc[j][k]);
-        }
-#pragma unroll
-        for (int j = 0; j < TPT; ++j)
-#pragma unroll
-            for (int k = 0; k < EPT; ++k) {
-                const float z = lfm_hsum16_ref(acc[j][k]);
-                const uint32_t t = tg * TPT + j, e = eg * EPT + k;
-                if (l == 0 && t < nt && e < ne) rt.logits[(size_t)(tok0 + t) * E + e0 + e] = z;
-            }
-    }
-    /* the xq rows of this CTA and its logits, before it counts itself in */
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) s_flag = atomicAdd(rt.tok_count + tile, 1u) == gridDim.y - 1;
-    __syncthreads();
-    if (!s_flag) return;
-    /* the tile's last CTA: top-K of its tokens from every CTA's logits */
-    __threadfence();
-    if (threadIdx.x == 0) rt.tok_count[tile] = 0;
-    for (uint32_t t = warp; t < nt; t += 8) route_topk(L, tok0 + t, rt, rt.logits + (size_t)(tok0 + t) * E, true);
-    __syncthreads();
-    for (uint32_t q = threadIdx.x; q < nt * K; q += blockDim.x) {
-        const size_t a = (size_t)tok0 * K + q;
-        const int e = __ldcg(rt.idx + a);
-        if ((unsigned)e >= E) {
-            atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
-            rt.inv[a] = -1;
-        } else {
-            rt.inv[a] = atomicAdd(rt.ecur + e, 1); /* rank inside the expert's segment, for now */
-        }
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) s_flag = atomicAdd(rt.done, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!s_flag) return;
-    /* the last tile: dispatch tables, slots, tile plans, publication */
-    __threadfence();
-    if (threadIdx.x == 0) *rt.done = 0;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) s.cnt[e] = atomicExch(rt.ecur + e, 0);
-    __syncthreads();
-    route_tables(L, rt, s);
-    for (uint32_t a = threadIdx.x; a < T * K; a += blockDim.x) {
-        const int e = __ldcg(rt.idx + a), r = __ldcg(rt.inv + a);
-        if ((unsigned)e >= E || r < 0) continue;
-        const int pos = s.off[e] + r;
-        rt.perm[pos] = (int)a;
-        rt.inv[a] = pos;
-    }
-    if (rt.plan.nt) route_plan(rt, s);
-    if (pub.world) {
-        __syncthreads();
-        route_publish(pub, s);
-    }
-}
-
 __global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt, EpPublish pub) {
     __shared__ RouteSmem s;
     route_dispatch(L, T, rt, s);
@@ -813,30 +645,9 @@ static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uin
     return cudaGetLastError();
 }
 
-template <int TT, int TPT, int EPT>
-static cudaError_t launch_route_fused(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
-                                      const RouteTables &rt, cudaStream_t s, const EpPublish &pub) {
-    const size_t smem = sizeof(float) * (size_t)(TT + kRfExperts) * L.D;
-    static size_t cache[16];
-    cudaError_t e = lfm_smem_attr((const void *)k_route_fused<TT, TPT, EPT>, smem, cache);
-    if (e != cudaSuccess) return e;
-    const dim3 grid((T + TT - 1) / TT, (L.E + kRfExperts - 1) / kRfExperts);
-    k_route_fused<TT, TPT, EPT><<<grid, 256, smem, s>>>(L, x, T, xq, rt, pub);
-    return cudaGetLastError();
-}
-
-static bool route_fused_ok(const MoeLayerDev &L, uint32_t T) {
-    return !L.dense && L.D <= kRfMaxD && L.E <= LFM_GPU_MAX_EXPERTS_DEV && T <= 65535;
-}
-
 /* T > 16: normalise + quantise, score (all experts per CTA), dispatch. */
 static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
                                         const RouteTables &rt, cudaStream_t s, const EpPublish &pub) {
-    if (route_fused_ok(L, T)) {
-        if (T >= 512) return launch_route_fused<8, 2, 2>(L, x, T, xq, rt, s, pub);
-        if (T >= 128) return launch_route_fused<4, 1, 2>(L, x, T, xq, rt, s, pub);
-        return launch_route_fused<2, 1, 1>(L, x, T, xq, rt, s, pub);
-    }
     const size_t nsmem = sizeof(float) * kNormWarps * L.D;
     static size_t cache[16];
     cudaError_t e = lfm_smem_attr((const void *)k_norm_q8, nsmem, cache);
@@ -868,7 +679,6 @@ uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T) {
     uint32_t epc = 0;
     if (T == 0) return 0;
     if (route_cluster_smem(L, T, &epc) > 0) return 1;
-    if (route_fused_ok(L, T)) return 1;
     return L.dense ? 2u : 3u;
 }
 

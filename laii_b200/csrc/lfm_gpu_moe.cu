@@ -196,7 +196,6 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_tc = take(sizeof(uint32_t) * T);
     const size_t o_done = take(sizeof(uint32_t));
     const size_t o_gbar = take(sizeof(uint32_t) * 2);
-    const size_t o_ecur = take(sizeof(int32_t) * E);
     const size_t counters_end = off;
     const size_t o_x = take(sizeof(float) * T * D);
     const size_t o_xq = take((size_t)T * D);
@@ -262,7 +261,6 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.rt.summary = reinterpret_cast<int32_t *>(b + o_sum);
     w.rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
     w.rt.done = reinterpret_cast<uint32_t *>(b + o_done);
-    w.rt.ecur = reinterpret_cast<int32_t *>(b + o_ecur);
     w.rt.logits = reinterpret_cast<float *>(b + o_log);
     w.rt.rms = reinterpret_cast<float *>(b + o_rms);
     w.rt.err = h->dev_err;
@@ -952,8 +950,7 @@ static size_t noalloc_layout(uint32_t T, const MoeLayerDev &L, uint8_t *b, Works
     const size_t n_pairs = E + (TK + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK + 1;
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
-    const size_t o_tc = take(sizeof(uint32_t) * T), o_done = take(sizeof(uint32_t)),
-                 o_ecur = take(sizeof(int32_t) * E);
+    const size_t o_tc = take(sizeof(uint32_t) * T), o_done = take(sizeof(uint32_t));
     if (counters_end) *counters_end = off;
     const size_t o_xq = take((size_t)T * D), o_xd = take(sizeof(float) * T * (D / 256)),
                  o_xb = take(sizeof(int16_t) * T * (D / 256) * 16);
@@ -982,7 +979,6 @@ static size_t noalloc_layout(uint32_t T, const MoeLayerDev &L, uint8_t *b, Works
     w->rt.summary = reinterpret_cast<int32_t *>(b + o_sum);
     w->rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
     w->rt.done = reinterpret_cast<uint32_t *>(b + o_done);
-    w->rt.ecur = reinterpret_cast<int32_t *>(b + o_ecur);
     w->rt.logits = reinterpret_cast<float *>(b + o_log);
     w->rt.rms = reinterpret_cast<float *>(b + o_rms);
     w->h = reinterpret_cast<float *>(b + o_h);
