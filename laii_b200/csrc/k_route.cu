@@ -95,19 +95,43 @@ __device__ void route_publish(const EpPublish &pub, const RouteSmem &s) {
     if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, epoch);
 }
 
+/* Expert id of assignment a for the dispatch passes (-1: none or out of range). */
+__device__ __forceinline__ int dispatch_id(const RouteTables &rt, uint32_t a, uint32_t n, uint32_t E, bool flag) {
+    int e = -1;
+    if (a < n) {
+        e = __ldcg(rt.idx + a);
+        if ((unsigned)e >= E) {
+            if (flag) atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
+            e = -1;
+        }
+    }
+    return e;
+}
+
 __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
     const uint32_t n = T * K;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    /* up to kPre ids per thread are loaded once, all in flight together, and
+     * serve both passes; larger n falls back to loads in each pass */
+    constexpr int kPre = 16;
+    const uint32_t npass = (n + blockDim.x - 1) / blockDim.x;
+    const bool pre = npass <= (uint32_t)kPre;
+    int ev[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) ev[i] = pre ? dispatch_id(rt, threadIdx.x + i * blockDim.x, n, E, true) : -1;
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
     __syncthreads();
     /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
-    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
-        const uint32_t a = b0 + threadIdx.x;
+    for (uint32_t i = 0; i < npass; ++i) {
+        const uint32_t a = i * blockDim.x + threadIdx.x;
         int e = -1;
-        if (a < n) {
-            e = __ldcg(rt.idx + a);
-            if ((unsigned)e >= E) { atomicOr(rt.err, LFM_DEVERR_EXPERT_ID); e = -1; }
+        if (pre) {
+#pragma unroll
+            for (int j = 0; j < kPre; ++j)
+                if ((uint32_t)j == i) e = ev[j];
+        } else {
+            e = dispatch_id(rt, a, n, E, true);
         }
         const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
         if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
@@ -147,12 +171,15 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
         for (int c = lane; c < nch; c += 32) rt.pairs[s.pb[u] + c] = make_int2(u, c);
     }
     /* slots: a run of equal ids in a warp takes consecutive slots with one atomic */
-    for (uint32_t b0 = 0; b0 < n; b0 += blockDim.x) {
-        const uint32_t a = b0 + threadIdx.x;
+    for (uint32_t i = 0; i < npass; ++i) {
+        const uint32_t a = i * blockDim.x + threadIdx.x;
         int e = -1;
-        if (a < n) {
-            e = __ldcg(rt.idx + a);
-            if ((unsigned)e >= E) e = -1;
+        if (pre) {
+#pragma unroll
+            for (int j = 0; j < kPre; ++j)
+                if ((uint32_t)j == i) e = ev[j];
+        } else {
+            e = dispatch_id(rt, a, n, E, false);
         }
         const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
         const int leader = __ffs(m) - 1;
@@ -353,9 +380,9 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
  *                 reference's 16 chains + tree), then Q8_K of xb; 1/rms is kept
  *                 for the next pass.  Dense layers route every token to expert
  *                 0 with weight 1 here.
- *  k_router_tiles a CTA scores TT tokens against every expert from 256-column
- *                 slices of the router rows and of x (tensor copies, four
- *                 slices in flight), then takes each token's top-K.
+ *  k_router_tiles a CTA scores TT tokens against 32 experts from 256-column
+ *                 slices of the router rows and of x (tensor copies, two or
+ *                 four slices in flight), then the top-K of each token.
  *  k_dispatch_wide the dispatch tables from one 1024-thread block.
  */
 constexpr int kNormWarps = 4;
@@ -411,7 +438,6 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_norm_q8(MoeLayerDev L, cons
 
 constexpr int kRtSlice = 256;   /* columns per slice */
 constexpr int kRtExperts = 32;  /* experts per pass  */
-constexpr int kRtStages = 4;
 
 template <int TT, int TPT>
 struct RouterTile {
@@ -423,63 +449,62 @@ struct RouterTile {
     static constexpr int kEpt = kRtExperts / (kGroups / kTokGroups); /* experts per thread per pass */
 };
 
-/* A CTA scores TT tokens against every expert.  Per 256-column slice: the
- * router rows (box 256 x 32 of router_w, rows past E read as zero) and the
- * tokens' x (box 256 x TT) arrive by one tensor copy each, ffn_norm by a bulk
- * copy, kRtStages slices in flight; xb is rebuilt in place from x, 1/rms and
- * ffn_norm exactly as k_norm_q8 forms it; thread (chain l, group g) advances
- * chain l of TPT tokens x EPT experts through the slice -- each chain in the
- * reference's column order -- and after the last slice of a pass the 16-lane
- * tree gives the logits.  One warp per token then takes the top-K. */
-template <int TT, int TPT>
+/* CTA (tile, p) scores TT tokens against experts [32p, 32p + 32).  Per
+ * 256-column slice: the router rows (box 256 x 32 of router_w, rows past E
+ * read as zero) and the tokens' x (box 256 x TT) arrive by one tensor copy
+ * each, ffn_norm by a bulk copy, NS slices in flight; xb is rebuilt in place
+ * from x, 1/rms and ffn_norm exactly as k_norm_q8 forms it; thread (chain l,
+ * group g) advances chain l of TPT tokens x EPT experts through the slice --
+ * each chain in the reference's column order -- and after the last slice the
+ * 16-lane tree gives the logits.  One warp per token then takes the top-K:
+ * at once when E <= 32, else in the last of the tile's CTAs to arrive (a
+ * counter per tile), from the logits every CTA wrote to global memory. */
+template <int TT, int TPT, int NS>
 __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CUtensorMap tmw,
                                                       const __grid_constant__ CUtensorMap tmx, MoeLayerDev L,
                                                       uint32_t T, RouteTables rt) {
     using RT = RouterTile<TT, TPT>;
     constexpr int EPT = RT::kEpt;
     extern __shared__ __align__(128) uint8_t dsm[];
-    __shared__ uint64_t bars[kRtStages];
+    __shared__ uint64_t bars[NS];
     __shared__ float s_inv[TT];
+    __shared__ int s_last;
     const uint32_t D = L.D, E = L.E;
-    const uint32_t tok0 = blockIdx.x * TT;
+    const uint32_t tok0 = blockIdx.x * TT, pass = blockIdx.y;
     const uint32_t nt = min((uint32_t)TT, T - tok0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int l = threadIdx.x & 15, g = threadIdx.x >> 4;
     const int tg = g % RT::kTokGroups, eg = g / RT::kTokGroups;
-    float *lg = reinterpret_cast<float *>(dsm + kRtStages * RT::kStage); /* [TT][E] logits */
-    const uint32_t nsl = D / kRtSlice, npass = (E + kRtExperts - 1) / kRtExperts;
-    const uint32_t nq = nsl * npass;
+    float *lg = reinterpret_cast<float *>(dsm + NS * RT::kStage); /* [TT][E] logits */
+    const uint32_t nq = D / kRtSlice; /* slices of this CTA's pass */
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kRtStages; ++i) lfm_mbar_init(&bars[i], 1);
+        for (int i = 0; i < NS; ++i) lfm_mbar_init(&bars[i], 1);
         lfm_fence_mbar_init();
     }
     if (threadIdx.x < TT) s_inv[threadIdx.x] = threadIdx.x < nt ? __ldcg(rt.rms + tok0 + threadIdx.x) : 0.0f;
     __syncthreads();
-    auto issue = [&](uint32_t q) {
-        const uint32_t p = q / nsl, sl = q % nsl;
-        uint8_t *st = dsm + (q % kRtStages) * RT::kStage;
-        uint64_t *bar = &bars[q % kRtStages];
+    auto issue = [&](uint32_t sl) {
+        uint8_t *st = dsm + (sl % NS) * RT::kStage;
+        uint64_t *bar = &bars[sl % NS];
         lfm_mbar_arrive_tx(bar, RT::kW + RT::kX + (L.ffn_norm ? kRtSlice * 4 : 0));
-        lfm_tma_load_2d(st, &tmw, sl * kRtSlice, p * kRtExperts, bar);
+        lfm_tma_load_2d(st, &tmw, sl * kRtSlice, pass * kRtExperts, bar);
         lfm_tma_load_2d(st + RT::kW, &tmx, sl * kRtSlice, tok0, bar);
         if (L.ffn_norm) lfm_bulk_g2s_plain(st + RT::kW + RT::kX, L.ffn_norm + sl * kRtSlice, kRtSlice * 4, bar);
     };
     if (threadIdx.x == 0)
-        for (uint32_t q = 0; q < nq && q < kRtStages - 1; ++q) issue(q);
+        for (uint32_t q = 0; q < nq && q < NS - 1; ++q) issue(q);
     float acc[TPT][EPT];
+#pragma unroll
+    for (int j = 0; j < TPT; ++j)
+#pragma unroll
+        for (int k = 0; k < EPT; ++k) acc[j][k] = 0.0f;
     bool ok = true;
     for (uint32_t q = 0; q < nq; ++q) {
-        const uint32_t p = q / nsl, sl = q % nsl;
-        if (sl == 0) {
-#pragma unroll
-            for (int j = 0; j < TPT; ++j)
-#pragma unroll
-                for (int k = 0; k < EPT; ++k) acc[j][k] = 0.0f;
-        }
-        /* stage (q + 3) % 4 was last read in iteration q - 1, which every thread has left */
-        if (threadIdx.x == 0 && q + kRtStages - 1 < nq) issue(q + kRtStages - 1);
-        ok = ok && lfm_mbar_wait(&bars[q % kRtStages], (q / kRtStages) & 1u, rt.err);
-        float *st = reinterpret_cast<float *>(dsm + (q % kRtStages) * RT::kStage);
+        const uint32_t sl = q;
+        /* stage (q + NS - 1) % NS was last read in iteration q - 1, which every thread has left */
+        if (threadIdx.x == 0 && q + NS - 1 < nq) issue(q + NS - 1);
+        ok = ok && lfm_mbar_wait(&bars[q % NS], (q / NS) & 1u, rt.err);
+        float *st = reinterpret_cast<float *>(dsm + (q % NS) * RT::kStage);
         const float *ws = st;
         float *xs = st + kRtExperts * kRtSlice;
         const float *nw = xs + TT * kRtSlice;
@@ -504,23 +529,37 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
                 }
             }
         }
-        if (sl == nsl - 1) {
+        if (sl == nq - 1) {
 #pragma unroll
             for (int j = 0; j < TPT; ++j)
 #pragma unroll
                 for (int k = 0; k < EPT; ++k) {
                     const float z = lfm_hsum16_ref(acc[j][k]);
-                    const uint32_t t = tg * TPT + j, e = p * kRtExperts + eg * EPT + k;
-                    if (l == 0 && e < E) lg[t * E + e] = z;
+                    const uint32_t t = tg * TPT + j, e = eg * EPT + k;
+                    if (l == 0 && pass * kRtExperts + e < E) lg[t * kRtExperts + e] = z;
                 }
         }
         __syncthreads();
     }
     if (!ok) return;
-    for (uint32_t t = warp; t < nt; t += blockDim.x / 32) {
-        for (uint32_t e = lane; e < E; e += 32) rt.logits[(size_t)(tok0 + t) * E + e] = lg[t * E + e];
-        route_topk(L, tok0 + t, rt, lg + t * E, false);
+    const uint32_t ne = min((uint32_t)kRtExperts, E - pass * kRtExperts);
+    for (uint32_t t = warp; t < nt; t += blockDim.x / 32)
+        for (uint32_t e = lane; e < ne; e += 32)
+            rt.logits[(size_t)(tok0 + t) * E + pass * kRtExperts + e] = lg[t * kRtExperts + e];
+    if (gridDim.y == 1) {
+        for (uint32_t t = warp; t < nt; t += blockDim.x / 32) route_topk(L, tok0 + t, rt, lg + t * kRtExperts, false);
+        return;
     }
+    /* several passes: the tile's last CTA takes the top-K from every pass's logits */
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(rt.tok_count + blockIdx.x, 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) rt.tok_count[blockIdx.x] = 0;
+    for (uint32_t t = warp; t < nt; t += blockDim.x / 32)
+        route_topk(L, tok0 + t, rt, rt.logits + (size_t)(tok0 + t) * E, true);
 }
 
 __global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt, EpPublish pub) {
@@ -628,7 +667,7 @@ cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTab
     return cudaGetLastError();
 }
 
-template <int TT, int TPT>
+template <int TT, int TPT, int NS>
 static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uint32_t T, const RouteTables &rt,
                                        cudaStream_t s) {
     using RT = RouterTile<TT, TPT>;
@@ -637,11 +676,12 @@ static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uin
                      kRtExperts) ||
         !lfm_tmap_2d(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, L.D, T, (uint64_t)L.D * 4, kRtSlice, TT))
         return cudaErrorInvalidValue;
-    const size_t smem = kRtStages * RT::kStage + sizeof(float) * TT * L.E;
+    const size_t smem = NS * RT::kStage + sizeof(float) * TT * kRtExperts;
     static size_t cache[16];
-    cudaError_t e = lfm_smem_attr((const void *)k_router_tiles<TT, TPT>, smem, cache);
+    cudaError_t e = lfm_smem_attr((const void *)k_router_tiles<TT, TPT, NS>, smem, cache);
     if (e != cudaSuccess) return e;
-    k_router_tiles<TT, TPT><<<(T + TT - 1) / TT, 256, smem, s>>>(tmw, tmx, L, T, rt);
+    const dim3 grid((T + TT - 1) / TT, (L.E + kRtExperts - 1) / kRtExperts);
+    k_router_tiles<TT, TPT, NS><<<grid, 256, smem, s>>>(tmw, tmx, L, T, rt);
     return cudaGetLastError();
 }
 
@@ -656,9 +696,11 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (!L.dense) {
-        if (T >= 1024) e = launch_router_tiles<16, 2>(L, x, T, rt, s);
-        else if (T >= 256) e = launch_router_tiles<8, 1>(L, x, T, rt, s);
-        else e = launch_router_tiles<4, 1>(L, x, T, rt, s);
+        /* enough CTAs for the grid, two or more resident per SM below 4096 tokens */
+        if (T >= 4096) e = launch_router_tiles<16, 2, 4>(L, x, T, rt, s);
+        else if (T >= 1024) e = launch_router_tiles<8, 1, 2>(L, x, T, rt, s);
+        else if (T >= 256) e = launch_router_tiles<4, 1, 2>(L, x, T, rt, s);
+        else e = launch_router_tiles<2, 1, 2>(L, x, T, rt, s);
         if (e != cudaSuccess) return e;
     }
     k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt, pub);
