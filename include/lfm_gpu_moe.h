@@ -206,6 +206,38 @@ lfm_gpu_status_t lfm_gpu_moe_ep_p2p_wait_check(lfm_gpu_moe_t *h, void *stream);
  * barrier between the last forward and detach). */
 lfm_gpu_status_t lfm_gpu_moe_ep_p2p_detach(lfm_gpu_moe_t *h);
 
+/* ---- GGUF checkpoints -------------------------------------------------------
+ * The FFN tensors of an lfm2moe GGUF v2/v3 file, bound as the reference binds
+ * them (lfm2_bind_moe_layer, tools/lfm2_moe_checkpoint.c:70-102, on the
+ * tensors and keys its loader reads, tools/lfm2_loader.c:359-366, :537-602):
+ * block l is an lfm2moe layer when blk.l.ffn_gate_exps.weight exists (Q4_K
+ * experts, F32 ffn_gate_inp router, optional exp_probs_b(.bias), top-K from
+ * the ".expert_used_count" key, default 4), else a dense SwiGLU layer from
+ * blk.l.ffn_{gate,up,down}.weight; both take blk.l.ffn_norm.weight and the
+ * ".attention.layer_norm_rms_epsilon" key (default 1e-5). */
+typedef struct {
+    uint32_t kind;     /* 0: no FFN tensors, 1: dense SwiGLU, 2: lfm2moe */
+    uint32_t D, E, K, I;
+    float eps;
+    int has_bias, has_norm;
+} lfm_gpu_moe_gguf_block_t;
+
+/* Describe block `block` of the file (host only, no GPU needed); *n_blocks =
+ * the ".block_count" key or one past the highest blk.N in the file. */
+lfm_gpu_status_t lfm_gpu_moe_gguf_describe(const char *path, uint32_t block, lfm_gpu_moe_gguf_block_t *out,
+                                           uint32_t *n_blocks);
+/* Text of the last GGUF error of this process. */
+const char *lfm_gpu_moe_gguf_last_error(void);
+
+/* Upload blocks [first_block, first_block + n_blocks) (n_blocks 0: to the
+ * end) into layer slots 0, 1, ...: lfm2moe blocks whole (n_local == 0) or as
+ * the expert shard [expert_first, expert_first + n_local), dense blocks whole.
+ * The file is mapped, not read into host memory first. *n_uploaded counts the
+ * layers uploaded. */
+lfm_gpu_status_t lfm_gpu_moe_upload_gguf(lfm_gpu_moe_t *h, const char *path, uint32_t first_block,
+                                         uint32_t n_blocks, uint32_t expert_first, uint32_t n_local,
+                                         uint32_t *n_uploaded);
+
 /* Reserve scratch for up to max_tokens tokens per forward (forward grows it on
  * demand; reserve first when the forward is to be captured in a CUDA graph). */
 lfm_gpu_status_t lfm_gpu_moe_reserve(lfm_gpu_moe_t *h, uint32_t max_tokens);

@@ -25,6 +25,11 @@ class Stats(ctypes.Structure):
                 ("max_segment", c_u32), ("expert_loads", c_u64), ("layer_runs", c_u64)]
 
 
+class GgufBlock(ctypes.Structure):
+    _fields_ = [("kind", c_u32), ("D", c_u32), ("E", c_u32), ("K", c_u32), ("I", c_u32), ("eps", c_f32),
+                ("has_bias", c_int), ("has_norm", c_int)]
+
+
 class KernelTime(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("launches", c_u32), ("total_ms", ctypes.c_double)]
 
@@ -52,6 +57,9 @@ GPU_API = [
     ("lfm_gpu_moe_ep_p2p_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_vp]),
     ("lfm_gpu_moe_ep_p2p_wait_check", c_int, [c_vp, c_vp]),
     ("lfm_gpu_moe_ep_p2p_detach", c_int, [c_vp]),
+    ("lfm_gpu_moe_gguf_describe", c_int, [ctypes.c_char_p, c_u32, c_vp, ctypes.POINTER(c_u32)]),
+    ("lfm_gpu_moe_gguf_last_error", ctypes.c_char_p, []),
+    ("lfm_gpu_moe_upload_gguf", c_int, [c_vp, ctypes.c_char_p, c_u32, c_u32, c_u32, c_u32, ctypes.POINTER(c_u32)]),
     ("lfm_gpu_moe_reserve", c_int, [c_vp, c_u32]),
     ("lfm_gpu_moe_forward", c_int, [c_vp, c_u32, c_vp, c_u32, c_int, c_vp]),
     ("lfm_gpu_moe_forward_stack", c_int, [c_vp, c_u32, c_u32, c_vp, c_u32, c_int, c_vp]),

@@ -33,6 +33,19 @@ def _ptr(a: Optional[np.ndarray]):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
 
+def gguf_describe(path: str, block: int) -> Tuple[dict, int]:
+    """The FFN of GGUF block `block` as the library binds it, and the file's block count (no GPU needed)."""
+    lib = _native.load_gpu()
+    out = _native.GgufBlock()
+    n = ctypes.c_uint32()
+    st = lib.lfm_gpu_moe_gguf_describe(str(path).encode(), block, ctypes.byref(out), ctypes.byref(n))
+    if st != 0:
+        raise MoEError(st, lib.lfm_gpu_moe_gguf_last_error().decode(errors="replace"))
+    kind = {0: "none", 1: "dense", 2: "moe"}[out.kind]
+    return ({"kind": kind, "D": out.D, "E": out.E, "K": out.K, "I": out.I, "eps": out.eps,
+             "has_bias": bool(out.has_bias), "has_norm": bool(out.has_norm)}, n.value)
+
+
 class GpuMoE:
     """One handle on one CUDA device (owns weights and scratch in HBM)."""
 
@@ -161,6 +174,19 @@ class GpuMoE:
 
     def ep_p2p_detach(self):
         self._check(self._lib.lfm_gpu_moe_ep_p2p_detach(self._h))
+
+    def upload_gguf(self, path: str, first_block: int = 0, n_blocks: int = 0, expert_first: int = 0,
+                    n_local: int = 0) -> int:
+        """Blocks [first_block, +n_blocks) of a GGUF checkpoint into layer slots 0, 1, ... (n_local > 0: that
+        expert shard of every MoE block); returns the number of layers uploaded."""
+        n = ctypes.c_uint32()
+        st = self._lib.lfm_gpu_moe_upload_gguf(self._h, str(path).encode(), first_block, n_blocks, expert_first,
+                                               n_local, ctypes.byref(n))
+        if st != 0:
+            raise MoEError(st, self._lib.lfm_gpu_moe_gguf_last_error().decode(errors="replace"))
+        for i in range(n_blocks or n.value):
+            self.layers[i] = ("gguf", first_block + i)
+        return n.value
 
     def reserve(self, max_tokens: int):
         self._check(self._lib.lfm_gpu_moe_reserve(self._h, max_tokens))
