@@ -391,6 +391,10 @@ def stack_cpu_baseline(cfg, seconds, threads=0):
                       f", extrapolated to the {len(stack_layers(cfg))}-layer stack; {R.isa}; nproc={os.cpu_count()}"}
 
 
+KERNEL_NAMES = ("route", "gateup", "quant_h", "down", "combine", "moe_layer", "gemm_plan", "gemm_gate", "gemm_up",
+                "swiglu_q8", "gemm_down", "xt_gather", "gemm_gateup", "ep_publish", "ep_plan")
+
+
 def run_stack(args, cfg):
     """Configs 4 and 5: a stack of FFN layers, T tokens in total per step (strong scaling over ranks).
     One GPU: the stack as one captured forward.  N GPUs with --ep: experts sharded across ranks,
@@ -529,6 +533,28 @@ def run_stack(args, cfg):
         e2e_s = float(t.item())
     e2e = T * n_e2e / e2e_s
 
+    kprof = None
+    if args.kernel_profile:  # after the timed region: events around every launch (no graphs), mean us per launch
+        g.profile(True)
+        for _ in range(max(1, min(args.steps, 5))):
+            if p2p:
+                for kind, l in layers:
+                    if kind == "dense":
+                        g.forward_device(l, x.data_ptr(), Tl, stream=sp)
+                    else:
+                        g.ep_p2p_forward(l, x.data_ptr(), Tl, sp)
+            else:
+                step()
+        torch.cuda.synchronize()
+        prof = g.profile_read()
+        g.profile(False)
+        names = sorted(KERNEL_NAMES)
+        mean = torch.tensor([prof[n][1] / prof[n][0] * 1e3 if n in prof else 0.0 for n in names], dtype=torch.float64,
+                            device="cuda")
+        if ws > 1:  # the slowest rank's figure per kernel
+            torch.distributed.all_reduce(mean, op=torch.distributed.ReduceOp.MAX)
+        kprof = {n: round(float(v), 1) for n, v in zip(names, mean.tolist()) if v > 0}
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = stack_cpu_baseline(cfg, args.cpu_seconds)
@@ -547,6 +573,9 @@ def run_stack(args, cfg):
                "roofline": roof, "cpu_baseline": cpu,
                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4},
                "gpu_launches": launches_per_step * args.steps, "clocks": clk}
+        if kprof is not None:
+            out["kernel_profile"] = {"us_per_launch_max_over_ranks": kprof,
+                                     "how": "library event profile after the timed region, eager launches"}
         print(json.dumps(out), flush=True)
     if ws > 1:
         torch.distributed.barrier()  # no rank frees its arena while another may still write into it
@@ -562,6 +591,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--ep", action="store_true", help="configs 4/5 under torchrun: expert parallelism")
+    ap.add_argument("--kernel-profile", action="store_true",
+                    help="stack configs: add per-kernel event times (max over ranks) to the JSON line")
     ap.add_argument("--ep-comm", default="p2p", choices=["p2p", "nccl"],
                     help="--ep exchange: the library's peer-memory kernels (p2p) or torch all_to_all over NCCL")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
