@@ -282,15 +282,9 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ RouteSmem s;
     __shared__ float s_inv[kClusterMaxT];
-    __shared__ int s_last;
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t c = cluster.block_rank();
     const uint32_t D = L.D, E = L.E;
-    /* cluster j routes tokens [16 j, 16 j + 16) of the call's T */
-    const uint32_t n_cl = gridDim.x / cluster.num_blocks(), tok0 = (blockIdx.x / cluster.num_blocks()) * kClusterMaxT;
-    const uint32_t T_all = T;
-    T = min((uint32_t)kClusterMaxT, T_all - tok0);
-    x += (size_t)tok0 * D;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int hw = threadIdx.x >> 4, l16 = threadIdx.x & 15; /* half-warp */
     float *xs = reinterpret_cast<float *>(dsm);   /* [T][D] x, then xb */
@@ -360,28 +354,19 @@ __global__ void __launch_bounds__(kClusterThreads) k_route_cluster(MoeLayerDev L
     cluster_sync_release_acquire();
     if (c != 0) return;
 
-    for (uint32_t t = warp; t < T; t += kClusterThreads / 32) route_topk(L, tok0 + t, rt, lg + (size_t)t * E, false);
+    for (uint32_t t = warp; t < T; t += kClusterThreads / 32) route_topk(L, t, rt, lg + (size_t)t * E, false);
     const uint32_t nb = D / 256;
     for (uint32_t q = warp; q < T * nb; q += kClusterThreads / 32) {
         const uint32_t t = q / nb, b = q % nb;
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = xs[(size_t)t * D + 256 * b + 8 * lane + i];
-        lfm_quant_block_warp(v, xq, tok0 + t, b);
+        lfm_quant_block_warp(v, xq, t, b);
     }
     if (rt.logits) /* keep the logits observable like the multi-block path does */
-        for (uint32_t q = threadIdx.x; q < T * E; q += kClusterThreads) rt.logits[(size_t)tok0 * E + q] = lg[q];
+        for (uint32_t q = threadIdx.x; q < T * E; q += kClusterThreads) rt.logits[q] = lg[q];
     __syncthreads();
-    if (n_cl > 1) { /* the last cluster to finish its tokens dispatches all of them */
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) s_last = atomicAdd(rt.done, 1u) == n_cl - 1;
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-        if (threadIdx.x == 0) *rt.done = 0;
-    }
-    route_dispatch(L, T_all, rt, s);
+    route_dispatch(L, T, rt, s);
     if (pub.world) {
         __syncthreads();
         route_publish(pub, s);
@@ -722,12 +707,9 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
     return cudaGetLastError();
 }
 
-/* Shared memory of the cluster router, or 0 when (T, D, E) does not fit it
- * (one cluster per 16 tokens, up to kClusterMaxClusters clusters). */
-constexpr uint32_t kClusterMaxClusters = 8;
+/* Shared memory of the cluster router, or 0 when (T, D, E) does not fit it. */
 static size_t route_cluster_smem(const MoeLayerDev &L, uint32_t T, uint32_t *epc_out) {
-    if (L.dense || T == 0 || T > kClusterMaxT * kClusterMaxClusters || L.E == 0) return 0;
-    T = T < (uint32_t)kClusterMaxT ? T : (uint32_t)kClusterMaxT;
+    if (L.dense || T == 0 || T > kClusterMaxT || L.E == 0) return 0;
     const uint32_t epc = (L.E + 7) / 8;
     const size_t bytes = sizeof(float) * ((size_t)T * L.D + L.D + (size_t)epc * L.D + (size_t)T * L.E);
     if (bytes > 200 * 1024) return 0;
@@ -753,9 +735,9 @@ cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q
         static size_t cache[16];
         cudaError_t e = lfm_smem_attr((const void *)k_route_cluster, csmem, cache);
         if (e != cudaSuccess) return e;
-        const uint32_t C = (L.E + epc - 1) / epc, n_cl = (T + kClusterMaxT - 1) / kClusterMaxT;
+        const uint32_t C = (L.E + epc - 1) / epc;
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(C * n_cl);
+        cfg.gridDim = dim3(C);
         cfg.blockDim = dim3(kClusterThreads);
         cfg.dynamicSmemBytes = csmem;
         cfg.stream = s;
