@@ -73,15 +73,13 @@ constexpr uint32_t kTmemCols = 512;
  *    accumulator per sub-block, D_j = q4 . q8 over its 32 K, so a super-block
  *    takes 8 MMAs; the epilogue forms acc = sum_j sc_j * D_j (exact).  At few
  *    tokens per expert a tcgen05.mma costs about the same whatever N, so the
- *    instruction count, not the arithmetic, sets the pace.  8 epilogue warps
- *    (two per TMEM lane quarter, half the columns each, so two round trips
- *    to the tensor memory run side by side), 4 producer warps, a deeper
+ *    instruction count, not the arithmetic, sets the pace.  4 epilogue warps,
+ *    8 producer warps (one row each, one half of every super-block), a deeper
  *    raw-weight ring; TMEM: 8 accumulators x 32 columns, double buffered. */
 template <bool kDec>
 struct UCfg {
-    static constexpr int kEpi = kDec ? 8 : 16;   /* two warps per TMEM lane quarter, half the columns each (decode) */
-    static constexpr int kProd = 4;               /* one weight row each, both halves of every super-block */
-    static constexpr int kHalves = 2 * kM / (kProd * 32); /* halves of a super-block per producer thread */
+    static constexpr int kEpi = kDec ? 4 : 16;
+    static constexpr int kProd = kDec ? 8 : 4;
     static constexpr int kSR = kDec ? 5 : 3;                   /* raw weight ring (super-blocks)      */
     static constexpr int kSA = kDec ? 4 : 3;  /* A stages: decode 2 per half super-block, prefill 3 shared */
     static constexpr int kAStage = kDec ? kOp : 2 * kOp;       /* A, or A1|A2                         */
@@ -324,7 +322,7 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
 
     if (warp < C::kEpi) {
         /* ---------------- epilogue ---------------- */
-        constexpr int kCols = (kDec ? (int)kNtDecode : kN) / (C::kEpi / 4); /* most columns of one warp */
+        constexpr int kCols = kDec ? (int)kNtDecode : kN / (C::kEpi / 4); /* most columns of one warp */
         const int q4 = warp & 3, ch = warp >> 2;
         const int r = 32 * q4 + lane;
         const int half = (int)A.nt / (C::kEpi / 4); /* columns of this warp: [ch * half, ch * half + half) */
@@ -432,8 +430,8 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
         /* ---------------- producers ---------------- */
         const int pt = tid - C::kEpi * 32;
         const int p = pt & (kM - 1);             /* weight row of the tile                          */
-        const int nh = C::kHalves;               /* halves of every super-block this thread converts */
-        const int h0 = (pt / kM) * nh;
+        const int h0 = kDec ? pt / kM : 0;       /* decode: this thread's half of every super-block */
+        const int nh = kDec ? 1 : 2;
         const uint32_t rowoff = (uint32_t)(p >> 3) * 128u + (uint32_t)(p & 7) * 16u;
         /* producer 0 issues: the tile's 128 rows x super-block gg (144 bytes at x = 144 * sb) */
         auto issue_raw = [&](uint32_t gg) {
