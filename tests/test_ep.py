@@ -237,9 +237,9 @@ def test_ep_nccl_two_gpus_match_single_gpu_forward(tmp_path):
 P2P_SHAPE = (2048, 32, 4, 1792)
 
 
-def _p2p_layers(g, n_layers, first, count):
+def _p2p_layers(g, n_layers, first, count, shape=P2P_SHAPE):
     import bench
-    D_, E_, K_, I_ = P2P_SHAPE
+    D_, E_, K_, I_ = shape
     for l in range(n_layers):
         if count == E_:
             g.synth_layer_shard(l, D_, E_, K_, I_, bench.layer_seeds(l + 40), 0, E_)
@@ -247,11 +247,11 @@ def _p2p_layers(g, n_layers, first, count):
             g.synth_layer_shard(l, D_, E_, K_, I_, bench.layer_seeds(l + 40), first, count)
 
 
-def _p2p_want(xs, n_layers):
+def _p2p_want(xs, n_layers, shape=P2P_SHAPE):
     """Every step of the test through the one-GPU forward of the full layers."""
     import bench
     from laii_b200.moe import GpuMoE
-    D_, E_, K_, I_ = P2P_SHAPE
+    D_, E_, K_, I_ = shape
     out = []
     with GpuMoE(0) as g:
         for l in range(n_layers):
@@ -321,7 +321,7 @@ def test_ep_p2p_bounded_wait_reports_timeout_and_recovers():
 P2P_STEPS = [(40, 7), (0, 33), (200, 200)]  # tokens of rank 0, rank 1 per step
 
 
-def _p2p_rank(rank, world, port, out_dir):
+def _p2p_rank(rank, world, port, out_dir, shape):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -331,10 +331,10 @@ def _p2p_rank(rank, world, port, out_dir):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=120))
     try:
-        D_, E_, K_, I_ = P2P_SHAPE
+        D_, E_, K_, I_ = shape
         first, count = ep.shard_of(E_, world, rank)
         g = GpuMoE(rank)
-        _p2p_layers(g, 2, first, count)
+        _p2p_layers(g, 2, first, count, shape)
         Tmax = max(max(s) for s in P2P_STEPS)
         ep.p2p_connect(g, Tmax, D_, E_, K_, I_, wait_ms=10000)
         for i, Ts in enumerate(P2P_STEPS):
@@ -366,21 +366,23 @@ def _p2p_rank(rank, world, port, out_dir):
 
 
 @pytest.mark.gpu
-def test_ep_p2p_two_gpus_match_single_gpu_forward(tmp_path):
-    """Two processes, one GPU each, experts split 16/16: uneven and empty token counts per rank,
-    two layers a step, three steps; each rank's tokens against the one-GPU forward, bit-exact."""
+@pytest.mark.parametrize("shape", [P2P_SHAPE, (2048, 64, 4, 1536)])
+def test_ep_p2p_two_gpus_match_single_gpu_forward(tmp_path, shape):
+    """Two processes, one GPU each, experts split in half (the config 1-4 and the config 5 layer
+    shapes): uneven and empty token counts per rank, two layers a step, three steps; each rank's
+    tokens against the one-GPU forward, bit-exact."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     from laii_b200 import synth
     world = 2
-    mp.spawn(_p2p_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
-    D_ = P2P_SHAPE[0]
+    mp.spawn(_p2p_rank, args=(world, _free_port(), str(tmp_path), tuple(shape)), nprocs=world, join=True)
+    D_ = shape[0]
     for i, Ts in enumerate(P2P_STEPS):
         xs = [synth.make_hidden(T, D_, seed_offset=1000 * i + 100 * r) if T else np.zeros((0, D_), np.float32)
               for r, T in enumerate(Ts)]
-        want = _p2p_want(xs, 2)
+        want = _p2p_want(xs, 2, shape)
         for r in range(world):
             got = np.load(tmp_path / f"p2p_{i}_{r}.npy")
             assert np.array_equal(got, want[r]), (i, r)
