@@ -697,10 +697,11 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
     if (e != cudaSuccess) return e;
     if (!L.dense) {
         /* enough CTAs for the grid, two or more resident per SM below 4096 tokens */
-        if (T >= 4096) e = launch_router_tiles<16, 2, 4>(L, x, T, rt, s);
-        else if (T >= 1024) e = launch_router_tiles<8, 1, 2>(L, x, T, rt, s);
-        else if (T >= 256) e = launch_router_tiles<4, 1, 2>(L, x, T, rt, s);
-        else e = launch_router_tiles<2, 1, 2>(L, x, T, rt, s);
+        /* several tokens per thread: each shared-memory load of a router value feeds TPT FMAs */
+        if (T >= 4096) e = launch_router_tiles<16, 4, 4>(L, x, T, rt, s);
+        else if (T >= 1024) e = launch_router_tiles<8, 2, 2>(L, x, T, rt, s);
+        else if (T >= 256) e = launch_router_tiles<4, 2, 2>(L, x, T, rt, s);
+        else e = launch_router_tiles<2, 2, 2>(L, x, T, rt, s);
         if (e != cudaSuccess) return e;
     }
     k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt, pub);
