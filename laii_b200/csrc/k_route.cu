@@ -83,60 +83,25 @@ __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
 /* Expert parallelism: this block's counts (s.cnt) into every rank's count
  * table, then its cnt_flag there.  Every thread fences its own writes (the
  * Q8_K rows and slots the expert ranks read next) before the flag. */
-__device__ void route_publish(const EpPublish &pub, const RouteSmem &s) {
+__device__ void route_publish_counts(const EpPublish &pub, const int *cnt) {
     const uint32_t epoch = __ldcg(pub.step) + 1u;
     const size_t row = ((size_t)(epoch & 1u) * LFM_EP_MAX_RANKS + pub.rank) * pub.E;
     for (uint32_t q = threadIdx.x; q < pub.world * pub.E; q += blockDim.x) {
         const uint32_t p = q / pub.E, e = q - p * pub.E;
-        pub.table[p][row + e] = s.cnt[e];
+        pub.table[p][row + e] = cnt[e];
     }
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x < pub.world) lfm_st_release_sys(pub.cnt_flag[threadIdx.x] + pub.rank, epoch);
 }
+__device__ void route_publish(const EpPublish &pub, const RouteSmem &s) { route_publish_counts(pub, s.cnt); }
 
-/* Expert id of assignment a for the dispatch passes (-1: none or out of range). */
-__device__ __forceinline__ int dispatch_id(const RouteTables &rt, uint32_t a, uint32_t n, uint32_t E, bool flag) {
-    int e = -1;
-    if (a < n) {
-        e = __ldcg(rt.idx + a);
-        if ((unsigned)e >= E) {
-            if (flag) atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
-            e = -1;
-        }
-    }
-    return e;
-}
-
-__device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
-    const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
-    const uint32_t n = T * K;
+/* The dispatch tables from the per-expert counts in s.cnt: offsets, active
+ * experts, GEMV work pairs, summary and load statistics (s.off, s.act,
+ * s.uniq set for the slot pass and the tile plans). */
+__device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteSmem &s) {
+    const uint32_t E = L.dense ? 1u : L.E;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    /* up to kPre ids per thread are loaded once, all in flight together, and
-     * serve both passes; larger n falls back to loads in each pass */
-    constexpr int kPre = 16;
-    const uint32_t npass = (n + blockDim.x - 1) / blockDim.x;
-    const bool pre = npass <= (uint32_t)kPre;
-    int ev[kPre];
-#pragma unroll
-    for (int i = 0; i < kPre; ++i) ev[i] = pre ? dispatch_id(rt, threadIdx.x + i * blockDim.x, n, E, true) : -1;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
-    __syncthreads();
-    /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
-    for (uint32_t i = 0; i < npass; ++i) {
-        const uint32_t a = i * blockDim.x + threadIdx.x;
-        int e = -1;
-        if (pre) {
-#pragma unroll
-            for (int j = 0; j < kPre; ++j)
-                if ((uint32_t)j == i) e = ev[j];
-        } else {
-            e = dispatch_id(rt, a, n, E, true);
-        }
-        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
-        if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
-    }
-    __syncthreads();
     if (threadIdx.x == 0) {
         int acc = 0, uniq = 0, mx = 0, pairs = 0;
         for (uint32_t e = 0; e < E; ++e) {
@@ -170,6 +135,52 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
         const int nch = (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
         for (int c = lane; c < nch; c += 32) rt.pairs[s.pb[u] + c] = make_int2(u, c);
     }
+    __syncthreads();
+}
+
+/* Expert id of assignment a for the dispatch passes (-1: none or out of range). */
+__device__ __forceinline__ int dispatch_id(const RouteTables &rt, uint32_t a, uint32_t n, uint32_t E, bool flag) {
+    int e = -1;
+    if (a < n) {
+        e = __ldcg(rt.idx + a);
+        if ((unsigned)e >= E) {
+            if (flag) atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
+            e = -1;
+        }
+    }
+    return e;
+}
+
+__device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, RouteSmem &s) {
+    const uint32_t E = L.dense ? 1u : L.E, K = L.dense ? 1u : L.K;
+    const uint32_t n = T * K;
+    const int lane = threadIdx.x & 31;
+    /* up to kPre ids per thread are loaded once, all in flight together, and
+     * serve both passes; larger n falls back to loads in each pass */
+    constexpr int kPre = 16;
+    const uint32_t npass = (n + blockDim.x - 1) / blockDim.x;
+    const bool pre = npass <= (uint32_t)kPre;
+    int ev[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) ev[i] = pre ? dispatch_id(rt, threadIdx.x + i * blockDim.x, n, E, true) : -1;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
+    __syncthreads();
+    /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
+    for (uint32_t i = 0; i < npass; ++i) {
+        const uint32_t a = i * blockDim.x + threadIdx.x;
+        int e = -1;
+        if (pre) {
+#pragma unroll
+            for (int j = 0; j < kPre; ++j)
+                if ((uint32_t)j == i) e = ev[j];
+        } else {
+            e = dispatch_id(rt, a, n, E, true);
+        }
+        const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+        if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
+    }
+    __syncthreads();
+    route_tables(L, rt, s);
     /* slots: a run of equal ids in a warp takes consecutive slots with one atomic */
     for (uint32_t i = 0; i < npass; ++i) {
         const uint32_t a = i * blockDim.x + threadIdx.x;
@@ -571,6 +582,92 @@ __global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t 
     }
 }
 
+/*
+ * Dispatch of many assignments (T*K >= kSplitMin) over one CTA per 1024-assignment
+ * chunk, in two launches instead of one block walking them all:
+ *  k_dispatch_hist   each CTA counts its chunk per expert (chunk[c][e]); the
+ *                    last CTA to arrive (counter rt.done) turns the chunk counts
+ *                    into totals, the tables, the tile plans, and each chunk's
+ *                    first rank inside every expert segment (chunk[c][e]);
+ *  k_dispatch_slots  each CTA places its chunk at offset + chunk rank + its own
+ *                    running rank; for expert parallelism the last CTA to
+ *                    finish publishes the counts once every slot is written.
+ * The order inside an expert segment changes no result.
+ */
+constexpr uint32_t kDispChunk = 1024;
+constexpr uint32_t kSplitMin = 4096;
+
+__global__ void __launch_bounds__(kDispChunk) k_dispatch_hist(MoeLayerDev L, uint32_t T, RouteTables rt) {
+    __shared__ RouteSmem s;
+    __shared__ int s_last;
+    const uint32_t E = L.E, n = T * L.K, c = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) s.cnt[e] = 0;
+    __syncthreads();
+    const int e = dispatch_id(rt, c * kDispChunk + threadIdx.x, n, E, true);
+    const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+    if (e >= 0 && lane == __ffs(m) - 1) atomicAdd(&s.cnt[e], __popc(m));
+    __syncthreads();
+    for (uint32_t q = threadIdx.x; q < E; q += blockDim.x) rt.chunk[(size_t)c * E + q] = s.cnt[q];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(rt.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) *rt.done = 0;
+    for (uint32_t q = threadIdx.x; q < E; q += blockDim.x) { /* chunk counts -> ranks of each chunk's first slot */
+        int acc = 0;
+        for (uint32_t cc = 0; cc < gridDim.x; ++cc) {
+            int *p = rt.chunk + (size_t)cc * E + q;
+            const int v = __ldcg(p);
+            *p = acc;
+            acc += v;
+        }
+        s.cnt[q] = acc;
+    }
+    __syncthreads();
+    route_tables(L, rt, s);
+    if (rt.plan.nt) route_plan(rt, s);
+}
+
+__global__ void __launch_bounds__(kDispChunk) k_dispatch_slots(MoeLayerDev L, uint32_t T, RouteTables rt,
+                                                               EpPublish pub) {
+    __shared__ int cur[LFM_GPU_MAX_EXPERTS_DEV];
+    __shared__ int s_last;
+    const uint32_t E = L.E, n = T * L.K, c = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    for (uint32_t q = threadIdx.x; q < E; q += blockDim.x)
+        cur[q] = __ldcg(rt.offsets + q) + __ldcg(rt.chunk + (size_t)c * E + q);
+    __syncthreads();
+    const uint32_t a = c * kDispChunk + threadIdx.x;
+    const int e = dispatch_id(rt, a, n, E, false);
+    const unsigned m = __match_any_sync(LFM_FULL_MASK, e);
+    const int leader = __ffs(m) - 1;
+    int base = 0;
+    if (e >= 0 && lane == leader) base = atomicAdd(&cur[e], __popc(m));
+    base = __shfl_sync(LFM_FULL_MASK, base, leader);
+    if (e >= 0) {
+        const int pos = base + __popc(m & ((1u << lane) - 1u));
+        rt.perm[pos] = (int)a;
+        rt.inv[a] = pos;
+    } else if (a < n) {
+        rt.inv[a] = -1;
+    }
+    if (!pub.world) return;
+    /* expert parallelism: every CTA's slots (and the Q8_K rows before them) before the counts go out */
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(rt.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) *rt.done = 0;
+    for (uint32_t q = threadIdx.x; q < E; q += blockDim.x) cur[q] = __ldcg(rt.counts + q);
+    __syncthreads();
+    route_publish_counts(pub, cur);
+}
+
 /* Dispatch tables alone, for rows whose experts are given (expert parallelism). */
 __global__ void __launch_bounds__(256) k_dispatch_only(MoeLayerDev L, uint32_t T, RouteTables rt) {
     __shared__ RouteSmem s;
@@ -704,6 +801,15 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
         else e = launch_router_tiles<2, 2, 2>(L, x, T, rt, s);
         if (e != cudaSuccess) return e;
     }
+    const uint32_t n = T * lfm_layer_K(L);
+    if (!L.dense && rt.chunk && n >= kSplitMin) {
+        const uint32_t nc = (n + kDispChunk - 1) / kDispChunk;
+        k_dispatch_hist<<<nc, kDispChunk, 0, s>>>(L, T, rt);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        k_dispatch_slots<<<nc, kDispChunk, 0, s>>>(L, T, rt, pub);
+        return cudaGetLastError();
+    }
     k_dispatch_wide<<<1, 1024, 0, s>>>(L, T, rt, pub);
     return cudaGetLastError();
 }
@@ -722,7 +828,8 @@ uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T) {
     uint32_t epc = 0;
     if (T == 0) return 0;
     if (route_cluster_smem(L, T, &epc) > 0) return 1;
-    return L.dense ? 2u : 3u;
+    if (L.dense) return 2u;
+    return T * L.K >= kSplitMin ? 4u : 3u; /* the wide dispatch splits in two at many assignments */
 }
 
 cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,

@@ -219,6 +219,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     const size_t o_y = take(sizeof(float) * TK * D);
     const size_t o_xrec = take((size_t)T * (D / 256) * 304);
     const size_t o_scores = take(sizeof(float) * 2 * T * E);
+    const size_t o_chunk = take(sizeof(int32_t) * ((TK + 1023) / 1024) * E);
     const size_t mt_gu = lfm_gemm_tiles_max(I, (uint32_t)TK, E), mt_dn = lfm_gemm_tiles_max(D, (uint32_t)TK, E);
     const size_t o_u = take(sizeof(float) * TK * I);
     const size_t o_tgu = take(lfm_gemm_tile_bytes() * mt_gu);
@@ -262,6 +263,7 @@ lfm_gpu_status_t ensure_workspace(lfm_gpu_moe_t *h, uint32_t T, uint32_t D, uint
     w.rt.tok_count = reinterpret_cast<uint32_t *>(b + o_tc);
     w.rt.done = reinterpret_cast<uint32_t *>(b + o_done);
     w.rt.logits = reinterpret_cast<float *>(b + o_log);
+    w.rt.chunk = reinterpret_cast<int32_t *>(b + o_chunk);
     w.rt.rms = reinterpret_cast<float *>(b + o_rms);
     w.rt.err = h->dev_err;
     w.rt.loads = h->loads;

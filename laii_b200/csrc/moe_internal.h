@@ -71,7 +71,8 @@ struct RouteTables {
     int2 *pairs;         /* [E + T*K/8] (u, chunk) work pairs, u-major                   */
     int32_t *summary;    /* [4]   active experts U, max segment, slots, pairs            */
     uint32_t *tok_count; /* [T]   per-token router-block arrival counters (kept at 0)     */
-    uint32_t *done;      /* [1]   routed-token counter (kept at 0)                        */
+    uint32_t *done;      /* [1]   CTA arrival counter of the dispatch (kept at 0)          */
+    int32_t *chunk;      /* [T*K/1024][E] per-chunk expert counts, then ranks (split dispatch; NULL: one block) */
     float *logits;       /* [T*E] router logits                                          */
     float *rms;          /* [T]   1/rms of x (the prefill router's two passes)            */
     uint32_t *err;       /* device error word                                            */

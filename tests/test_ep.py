@@ -266,7 +266,7 @@ def _p2p_want(xs, n_layers, shape=P2P_SHAPE):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("Ts", [(8, 24, 0, 300), (64, 1)])
+@pytest.mark.parametrize("Ts", [(8, 24, 0, 300), (64, 1), (1100, 40)])
 def test_ep_p2p_world_of_one_matches_forward(Ts):
     """The peer-memory layer step as a world of one (every exchange to itself), two layers a step,
     against the regular forward: the same grouped GEMMs and k-ordered combine, so bit-exact."""
