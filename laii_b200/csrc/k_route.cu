@@ -616,15 +616,25 @@ __global__ void __launch_bounds__(kDispChunk) k_dispatch_hist(MoeLayerDev L, uin
     if (!s_last) return;
     __threadfence();
     if (threadIdx.x == 0) *rt.done = 0;
-    for (uint32_t q = threadIdx.x; q < E; q += blockDim.x) { /* chunk counts -> ranks of each chunk's first slot */
+    /* chunk counts -> rank of each chunk's first slot in the expert's segment:
+     * one warp per expert, 32 chunks per step through a warp scan */
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (uint32_t q = warp; q < E; q += nwarps) {
         int acc = 0;
-        for (uint32_t cc = 0; cc < gridDim.x; ++cc) {
+        for (uint32_t c0 = 0; c0 < gridDim.x; c0 += 32) {
+            const uint32_t cc = c0 + lane;
             int *p = rt.chunk + (size_t)cc * E + q;
-            const int v = __ldcg(p);
-            *p = acc;
-            acc += v;
+            const int v = cc < gridDim.x ? __ldcg(p) : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(LFM_FULL_MASK, incl, o);
+                if (lane >= o) incl += u;
+            }
+            if (cc < gridDim.x) *p = acc + incl - v;
+            acc += __shfl_sync(LFM_FULL_MASK, incl, 31);
         }
-        s.cnt[q] = acc;
+        if (lane == 0) s.cnt[q] = acc;
     }
     __syncthreads();
     route_tables(L, rt, s);
