@@ -805,7 +805,7 @@ static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, ui
     if (!L.dense) {
         /* enough CTAs for the grid, two or more resident per SM below 4096 tokens */
         /* several tokens per thread: each shared-memory load of a router value feeds TPT FMAs */
-        if (T >= 4096) e = launch_router_tiles<16, 4, 4>(L, x, T, rt, s);
+        if (T >= 4096) e = launch_router_tiles<16, 4, 2>(L, x, T, rt, s);
         else if (T >= 1024) e = launch_router_tiles<8, 2, 2>(L, x, T, rt, s);
         else if (T >= 256) e = launch_router_tiles<4, 2, 2>(L, x, T, rt, s);
         else e = launch_router_tiles<2, 2, 2>(L, x, T, rt, s);
