@@ -168,7 +168,7 @@ lfm_gpu_status_t lfm_gpu_moe_ep_combine(lfm_gpu_moe_t *h, uint32_t layer, float 
  * experts [first, first + n) with (first, n) as in the host-side shard_of
  * (the first E % world ranks hold one expert more). */
 #define LFM_GPU_MOE_EP_MAX_RANKS 8
-#define LFM_GPU_MOE_IPC_HANDLE_BYTES 64
+#define LFM_GPU_MOE_IPC_HANDLE_BYTES 128
 
 /* Step 1 (every rank): allocate this rank's exchange arena for up to
  * max_tokens tokens per rank and layers of shape D, E, K, I, and return its
@@ -180,7 +180,10 @@ lfm_gpu_status_t lfm_gpu_moe_ep_p2p_attach(lfm_gpu_moe_t *h, int rank, int world
                                            void *ipc_handle_out);
 
 /* Step 2 (every rank, after every rank's attach returned): map the other
- * ranks' arenas; handles[r] is rank r's handle from step 1, in rank order. */
+ * ranks' arenas; handles[r] is rank r's handle from step 1, in rank order.
+ * Every rank must have attached with the same world, max_tokens, D, E, K and
+ * I (each handle carries them): otherwise LFM_GPU_ERR_INVALID_ARG and nothing
+ * is mapped. */
 lfm_gpu_status_t lfm_gpu_moe_ep_p2p_connect(lfm_gpu_moe_t *h, const void *handles);
 
 /* x[T][D] += MoE(x) for this rank's tokens (device x), experts spread over
@@ -226,7 +229,7 @@ typedef struct {
  * the ".block_count" key or one past the highest blk.N in the file. */
 lfm_gpu_status_t lfm_gpu_moe_gguf_describe(const char *path, uint32_t block, lfm_gpu_moe_gguf_block_t *out,
                                            uint32_t *n_blocks);
-/* Text of the last GGUF error of this process. */
+/* Text of the calling thread's last GGUF error. */
 const char *lfm_gpu_moe_gguf_last_error(void);
 
 /* Upload blocks [first_block, first_block + n_blocks) (n_blocks 0: to the

@@ -290,7 +290,7 @@ BlockFfn bind_block(GgufFile &f, uint32_t l) {
 
 const void *ptr(const TensorInfo *t) { return t ? t->data : nullptr; }
 
-char g_describe_err[256];
+thread_local char g_describe_err[256]; /* per calling thread */
 
 }  // namespace
 

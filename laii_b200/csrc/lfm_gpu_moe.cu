@@ -1158,6 +1158,28 @@ void ep_layout(EpP2P &p) {
     p.bytes = off;
 }
 
+/* What an exchanged handle carries besides the IPC handle: the attach
+ * arguments every rank must share (the arena layout follows from them). */
+struct EpSignature {
+    uint32_t magic, rank, world, T_max, D, E, K, I;
+    uint64_t bytes;
+};
+constexpr uint32_t kEpSigMagic = 0x5045464Cu; /* "LFEP" */
+constexpr size_t kEpSigOffset = 64;
+static_assert(sizeof(cudaIpcMemHandle_t) <= kEpSigOffset, "IPC handle size");
+static_assert(kEpSigOffset + sizeof(EpSignature) <= LFM_GPU_MOE_IPC_HANDLE_BYTES, "exchanged handle size");
+
+EpSignature ep_signature(const EpP2P &p, uint32_t rank) {
+    EpSignature g{};
+    g.magic = kEpSigMagic;
+    g.rank = rank;
+    g.world = p.world;
+    g.T_max = p.T_max;
+    g.D = p.D; g.E = p.E; g.K = p.K; g.I = p.I;
+    g.bytes = p.bytes;
+    return g;
+}
+
 EpArena ep_arena_view(const EpP2P &p, uint8_t *b) {
     EpArena a{};
     a.cnt_flag = reinterpret_cast<uint32_t *>(b + p.o_cnt);
@@ -1204,7 +1226,6 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_attach(lfm_gpu_moe_t *h, int rank, i
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p_attach: max_tokens=%u not in 1..65535", max_tokens);
     if (!(lfm_umma_ok(I) && lfm_umma_ok(D)))
         return fail(h, LFM_GPU_ERR_UNSUPPORTED, "ep_p2p_attach: D=%u, I=%u need multiples of 128 rows", D, I);
-    static_assert(sizeof(cudaIpcMemHandle_t) <= LFM_GPU_MOE_IPC_HANDLE_BYTES, "IPC handle size");
     DeviceGuard g(h->device);
     EpP2P &p = h->ep;
     p = EpP2P{};
@@ -1231,6 +1252,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_attach(lfm_gpu_moe_t *h, int rank, i
     if (e != cudaSuccess) { ep_release(h); return cuda_fail(h, e, "ep_p2p_attach: arena setup"); }
     memset(ipc_handle_out, 0, LFM_GPU_MOE_IPC_HANDLE_BYTES);
     memcpy(ipc_handle_out, &ipc, sizeof ipc);
+    const EpSignature sig = ep_signature(p, p.rank);
+    memcpy(static_cast<uint8_t *>(ipc_handle_out) + kEpSigOffset, &sig, sizeof sig);
     p.peer[p.rank] = p.arena;
     p.attached = true;
     return LFM_GPU_OK;
@@ -1243,6 +1266,19 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_ep_p2p_connect(lfm_gpu_moe_t *h, const void
     if (p.connected) return LFM_GPU_OK;
     DeviceGuard g(h->device);
     const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    /* every rank must have attached with the same shapes: the arenas' layouts are computed, not exchanged */
+    for (uint32_t r = 0; r < p.world; ++r) {
+        EpSignature theirs;
+        memcpy(&theirs, hb + (size_t)r * LFM_GPU_MOE_IPC_HANDLE_BYTES + kEpSigOffset, sizeof theirs);
+        const EpSignature want = ep_signature(p, r);
+        if (memcmp(&theirs, &want, sizeof want) != 0)
+            return fail(h, LFM_GPU_ERR_INVALID_ARG,
+                        "ep_p2p_connect: handle %u is not rank %u of this world with this rank's shapes "
+                        "(it has rank %u of %u, max_tokens %u, D %u, E %u, K %u, I %u; this rank %u of %u, "
+                        "max_tokens %u, D %u, E %u, K %u, I %u)",
+                        r, r, theirs.rank, theirs.world, theirs.T_max, theirs.D, theirs.E, theirs.K, theirs.I, p.rank,
+                        p.world, p.T_max, p.D, p.E, p.K, p.I);
+    }
     for (uint32_t r = 0; r < p.world; ++r) {
         if (r == p.rank) continue;
         cudaIpcMemHandle_t ipc;

@@ -143,7 +143,7 @@ class GpuMoE:
                                                      ctypes.c_void_p(y_ptr), ctypes.c_void_p(stream or None)))
 
     # -- expert parallelism over peer memory (one process per GPU) --------
-    IPC_HANDLE_BYTES = 64
+    IPC_HANDLE_BYTES = 128  # LFM_GPU_MOE_IPC_HANDLE_BYTES
 
     def ep_p2p_attach(self, rank: int, world: int, max_tokens: int, D: int, E: int, K: int, I: int,
                       wait_ms: int = 0) -> bytes:

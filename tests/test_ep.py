@@ -421,3 +421,21 @@ def test_ep_p2p_stack_world_of_one_with_dense_layer_replays():
             torch.cuda.synchronize()
             g.sync()
             assert np.array_equal(xbuf.cpu().numpy(), want), rep
+
+
+@pytest.mark.gpu
+def test_ep_p2p_connect_refuses_handles_of_other_shapes():
+    """Every rank computes the arena layout from its own attach arguments, so a handle attached with
+    other shapes (here max_tokens) is refused before anything is mapped."""
+    from laii_b200.moe import GpuMoE, MoEError
+    D_, E_, K_, I_ = P2P_SHAPE
+    with GpuMoE(0) as a, GpuMoE(0) as b:
+        ha = a.ep_p2p_attach(0, 1, 24, D_, E_, K_, I_)
+        hb = b.ep_p2p_attach(0, 1, 32, D_, E_, K_, I_)
+        assert len(ha) == len(hb) == GpuMoE.IPC_HANDLE_BYTES
+        with pytest.raises(MoEError) as ei:
+            a.ep_p2p_connect([hb])
+        assert ei.value.status == -1 and "max_tokens 32" in str(ei.value)
+        a.ep_p2p_connect([ha])  # its own handle still connects
+        a.ep_p2p_detach()
+        b.ep_p2p_detach()
