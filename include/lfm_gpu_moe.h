@@ -88,6 +88,23 @@ lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint
                                           const void *down_exps, uint32_t w_type,
                                           int norm_topk_prob, float routed_scale);
 
+/* As lfm_gpu_moe_upload_layer, with the down tensor's own GGUF type: Q4_K_M
+ * checkpoints store some blk.l.ffn_down_exps as Q6_K (the reference's
+ * lfm2_compute_4rows_avx2 picks its Q6_K x Q8_K kernel by the tensor type,
+ * tools/lfm2_decode_1x4.c:618-630; Q6_K block, tools/lfm2_cpuid_quants.c:101-106):
+ *   gate_up_type 12 (Q4_K); down_type 12 (Q4_K) or 14 (Q6_K: [E][D][I/256]
+ *   210-byte blocks).
+ * A Q6_K-down layer runs the route, the Q4_K gate|up GEMV (or GEMM) and a
+ * dedicated Q6_K down kernel; the fused decode kernel, the tcgen05 GEMMs, the
+ * peer-memory expert-parallel path and lfm_gpu_moe_forward_noalloc take Q4_K
+ * layers only (they refuse a Q6_K layer with LFM_GPU_ERR_UNSUPPORTED). */
+lfm_gpu_status_t lfm_gpu_moe_upload_layer_typed(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                const float *router_w, const float *exp_probs_b,
+                                                const void *gate_exps, const void *up_exps,
+                                                const void *down_exps, uint32_t gate_up_type,
+                                                uint32_t down_type, int norm_topk_prob, float routed_scale);
+
 /* Upload a dense SwiGLU FFN layer (the leading layers of an lfm2moe stack,
  * run by lfm2_forward_ffn_fused_1x4, tools/lfm2_decode_1x4.c:1070-1104):
  * gate/up Q4_K [I][D/256], down Q4_K [D][I/256]. */

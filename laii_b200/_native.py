@@ -41,6 +41,8 @@ GPU_API = [
     ("lfm_gpu_moe_last_error", ctypes.c_char_p, [c_vp]),
     ("lfm_gpu_moe_upload_layer", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32, c_vp, c_vp, c_vp, c_vp,
                                          c_vp, c_vp, c_u32, c_int, c_f32]),
+    ("lfm_gpu_moe_upload_layer_typed", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32, c_vp, c_vp, c_vp,
+                                               c_vp, c_vp, c_vp, c_u32, c_u32, c_int, c_f32]),
     ("lfm_gpu_moe_upload_dense", c_int, [c_vp, c_u32, c_u32, c_u32, c_f32, c_vp, c_vp, c_vp, c_vp, c_u32]),
     ("lfm_gpu_moe_synth_layer", c_int, [c_vp, c_u32, c_u32, c_u32, c_u32, c_u32, c_f32, ctypes.POINTER(c_u64),
                                         c_f32, c_f32, c_f32, c_vp]),

@@ -26,7 +26,7 @@ BUILD = os.path.join(PKG, "_build")
 GPU_SO = os.path.join(LIB, "liblfm_gpu_moe.so")
 SYNTH_SO = os.path.join(LIB, "liblfm_synth.so")
 
-CU_SOURCES = ["lfm_gpu_moe.cu", "k_route.cu", "k_gemv.cu", "k_layer.cu", "k_gemm.cu", "k_umma.cu", "k_expert.cu", "k_ep.cu", "k_synth.cu", "lfm_gguf.cpp"]
+CU_SOURCES = ["lfm_gpu_moe.cu", "k_route.cu", "k_gemv.cu", "k_layer.cu", "k_gemm.cu", "k_umma.cu", "k_expert.cu", "k_ep.cu", "k_q6k.cu", "k_synth.cu", "lfm_gguf.cpp"]
 HEADERS = ["lfm_formats.h", "lfm_synth_core.h", "moe_internal.h", "moe_device.cuh"]
 
 NVCC_FLAGS = [

@@ -29,6 +29,7 @@
 #define LFM_QK_K 256          /* elements per K-quant super-block            */
 #define LFM_Q4K_BYTES 144     /* sizeof(lfm_block_q4_K)                      */
 #define LFM_Q8K_BYTES 292     /* sizeof(lfm_block_q8_K)                      */
+#define LFM_Q6K_BYTES 210     /* block_q6_K: ql[128] qh[64] int8 scales[16] fp16 d */
 #define LFM_GGML_TYPE_F32 0u
 #define LFM_GGML_TYPE_Q4_K 12u
 #define LFM_GGML_TYPE_Q6_K 14u

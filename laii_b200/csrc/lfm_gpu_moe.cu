@@ -335,7 +335,8 @@ cudaError_t timed(lfm_gpu_moe_t *h, int kid, cudaStream_t s, F &&launch, uint32_
  * step to build (nt == 0 when the tcgen05 GEMMs are not the path). */
 UmmaPlanOut umma_plan_for(lfm_gpu_moe_t *h, const MoeLayerDev &L, uint32_t T) {
     UmmaPlanOut p{};
-    if (!(h->use_gemm && h->use_umma && T > LFM_FUSED_MAX_T && lfm_umma_ok(L.I) && lfm_umma_ok(L.D))) return p;
+    if (!(h->use_gemm && h->use_umma && T > LFM_FUSED_MAX_T && lfm_umma_ok(L.I) && lfm_umma_ok(L.D)) || L.down_q6k)
+        return p;
     Workspace &w = h->ws;
     const uint32_t TK = T * lfm_layer_K(L), E = lfm_layer_E(L);
     p.nt = lfm_umma_nt(TK, E);
@@ -386,6 +387,7 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
         }));
         LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_quant(w.h, w.u, T * K, L.I, hq, s); }));
         LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
+            if (L.down_q6k) return lfm_launch_down_q6k(L, hq, w.rt, w.y, grid, s);
             return lfm_launch_q4k_gemm(L.down, L.D, L.I, hq, nullptr, 1, w.tiles_dn, w.n_tiles + 1, w.y, w.rt.err, grid, s);
         }));
         LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
@@ -393,7 +395,9 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
     }
     LFM_CUDA(h, timed(h, K_GATEUP, s, [&] { return lfm_launch_gateup(L, xq, w.rt, w.h, grid, s, pdl); }));
     LFM_CUDA(h, timed(h, K_QUANT_H, s, [&] { return lfm_launch_quant_rows(w.h, T * K, L.I, hq, s, pdl); }));
-    LFM_CUDA(h, timed(h, K_DOWN, s, [&] { return lfm_launch_down(L, hq, w.rt, w.y, grid, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_DOWN, s, [&] {
+        return L.down_q6k ? lfm_launch_down_q6k(L, hq, w.rt, w.y, grid, s) : lfm_launch_down(L, hq, w.rt, w.y, grid, s, pdl);
+    }));
     LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, pdl); }));
     return LFM_GPU_OK;
 }
@@ -410,7 +414,7 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
     Q8Rows xq = w.xq; xq.cols = L.D;
     const bool pdl = !h->prof;
     const int grid = h->sm_count;
-    if (h->use_fused && lfm_fused_ok(L, T, grid)) {
+    if (h->use_fused && !L.down_q6k && lfm_fused_ok(L, T, grid)) {
         LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
         return LFM_GPU_OK;
     }
@@ -494,14 +498,17 @@ LFM_API const char *lfm_gpu_moe_last_error(const lfm_gpu_moe_t *h) { return h ? 
 static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E, uint32_t K,
                                           uint32_t I, float eps, const float *ffn_norm, const float *router_w,
                                           const float *exp_probs_b, const void *gate_exps, const void *up_exps,
-                                          const void *down_exps, uint32_t w_type, int norm_topk_prob,
-                                          float routed_scale, uint32_t first, uint32_t n) {
+                                          const void *down_exps, uint32_t w_type, uint32_t down_type,
+                                          int norm_topk_prob, float routed_scale, uint32_t first, uint32_t n) {
     if (!h) return LFM_GPU_ERR_INVALID_ARG;
     lfm_gpu_status_t st = check_layer_shape(h, layer, D, E, K, I);
     if (st != LFM_GPU_OK) return st;
     if (n == 0 || first >= E || n > E - first)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "expert shard [%u, %u+%u) not inside 0..%u", first, first, n, E);
     if (w_type != LFM_GGML_TYPE_Q4_K) return fail(h, LFM_GPU_ERR_UNSUPPORTED, "expert weight type %u (only Q4_K=12)", w_type);
+    if (down_type != LFM_GGML_TYPE_Q4_K && down_type != LFM_GGML_TYPE_Q6_K)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "down weight type %u (Q4_K=12 or Q6_K=14)", down_type);
+    const bool q6k = down_type == LFM_GGML_TYPE_Q6_K;
     if (!router_w || !gate_exps || !up_exps || !down_exps) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
     DeviceGuard g(h->device);
     drop_graphs(h);
@@ -510,7 +517,7 @@ static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint
     const size_t nbd = D / 256, nbi = I / 256;
     const size_t sz[6] = {sizeof(float) * D, sizeof(float) * E * D, sizeof(float) * ((E + 3) / 4 * 4),
                           (size_t)n * I * nbd * LFM_Q4K_BYTES, (size_t)n * I * nbd * LFM_Q4K_BYTES,
-                          (size_t)n * D * nbi * LFM_Q4K_BYTES};
+                          (size_t)n * D * nbi * (q6k ? LFM_Q6K_BYTES : LFM_Q4K_BYTES)};
     const void *src[6] = {ffn_norm, router_w, exp_probs_b, gate_exps, up_exps, down_exps};
     for (int i = 0; i < 6; ++i) {
         if (i == 0 && !ffn_norm) continue;
@@ -525,7 +532,8 @@ static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint
     S.dev = MoeLayerDev{D, E, K, I, 0, eps, routed_scale, norm_topk_prob ? 1 : 0,
                         static_cast<float *>(S.bufs[0]), static_cast<float *>(S.bufs[1]),
                         static_cast<float *>(S.bufs[2]), static_cast<const uint8_t *>(S.bufs[3]),
-                        static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5])};
+                        static_cast<const uint8_t *>(S.bufs[4]), static_cast<const uint8_t *>(S.bufs[5]),
+                        q6k ? 1u : 0u};
     S.ep_first = first;
     S.ep_count = n;
     S.present = true;
@@ -539,7 +547,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t lay
                                                   const void *down_exps, uint32_t w_type, int norm_topk_prob,
                                                   float routed_scale) {
     return upload_layer_impl(h, layer, D, E, K, I, eps, ffn_norm, router_w, exp_probs_b, gate_exps, up_exps,
-                             down_exps, w_type, norm_topk_prob, routed_scale, 0, E);
+                             down_exps, w_type, w_type, norm_topk_prob, routed_scale, 0, E);
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer_shard(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
@@ -550,7 +558,17 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer_shard(lfm_gpu_moe_t *h, uint32
                                                         int norm_topk_prob, float routed_scale,
                                                         uint32_t expert_first, uint32_t n_local) {
     return upload_layer_impl(h, layer, D, E, K, I, eps, ffn_norm, router_w, exp_probs_b, gate_local, up_local,
-                             down_local, w_type, norm_topk_prob, routed_scale, expert_first, n_local);
+                             down_local, w_type, w_type, norm_topk_prob, routed_scale, expert_first, n_local);
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_layer_typed(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t E,
+                                                        uint32_t K, uint32_t I, float eps, const float *ffn_norm,
+                                                        const float *router_w, const float *exp_probs_b,
+                                                        const void *gate_exps, const void *up_exps,
+                                                        const void *down_exps, uint32_t gate_up_type,
+                                                        uint32_t down_type, int norm_topk_prob, float routed_scale) {
+    return upload_layer_impl(h, layer, D, E, K, I, eps, ffn_norm, router_w, exp_probs_b, gate_exps, up_exps,
+                             down_exps, gate_up_type, down_type, norm_topk_prob, routed_scale, 0, E);
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_dense(lfm_gpu_moe_t *h, uint32_t layer, uint32_t D, uint32_t I,
@@ -999,6 +1017,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t 
     if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
         return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
     const MoeLayerDev &L = h->layers[layer].dev;
+    if (L.down_q6k)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "forward_noalloc: layer %u has a Q6_K down tensor (Q4_K only)", layer);
     const size_t need = noalloc_layout(T, L, nullptr, nullptr, nullptr);
     if (T > 65535 || need > kNoAllocBytes)
         return fail(h, LFM_GPU_ERR_UNSUPPORTED,
@@ -1318,6 +1338,9 @@ lfm_gpu_status_t ep_check_layer(lfm_gpu_moe_t *h, uint32_t layer, const LayerSlo
     if (L.dense || L.D != p.D || L.E != p.E || L.K != p.K || L.I != p.I)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p: layer %u is not a %ux%ux%ux%u MoE layer", layer, p.D, p.E,
                     p.K, p.I);
+    if (L.down_q6k)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "ep_p2p: layer %u has a Q6_K down tensor (the peer-memory path is Q4_K only)",
+                    layer);
     if (S.ep_first != first || (S.ep_count ? S.ep_count : L.E) != count)
         return fail(h, LFM_GPU_ERR_INVALID_ARG, "ep_p2p: layer %u holds experts [%u, %u), rank %u owns [%u, %u)", layer,
                     S.ep_first, S.ep_first + (S.ep_count ? S.ep_count : L.E), p.rank, first, first + count);

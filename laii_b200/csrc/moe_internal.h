@@ -90,6 +90,7 @@ struct MoeLayerDev {
     const uint8_t *gate; /* Q4_K blocks */
     const uint8_t *up;
     const uint8_t *down;
+    uint32_t down_q6k;   /* 1: down is Q6_K [E][D][I/256] 210-byte blocks (k_q6k.cu), 0: Q4_K */
 };
 
 /* Expert-side geometry of a layer (dense layers are one expert, top-1). */
@@ -122,6 +123,9 @@ cudaError_t lfm_launch_gateup(const MoeLayerDev &L, Q8Rows xq, const RouteTables
 cudaError_t lfm_launch_quant_rows(const float *h, uint32_t rows, uint32_t cols, Q8Rows hq, cudaStream_t s, bool pdl);
 cudaError_t lfm_launch_down(const MoeLayerDev &L, Q8Rows hq, const RouteTables &rt, float *y, int grid,
                             cudaStream_t s, bool pdl);
+/* k_q6k.cu: down projection of a layer whose down tensor is Q6_K (pairs of the dispatch tables) */
+cudaError_t lfm_launch_down_q6k(const MoeLayerDev &L, Q8Rows hq, const RouteTables &rt, float *y, int grid,
+                                cudaStream_t s);
 cudaError_t lfm_launch_combine(const MoeLayerDev &L, float *x, uint32_t T, const RouteTables &rt, const float *y,
                                cudaStream_t s, bool pdl);
 cudaError_t lfm_launch_debug_q4k_rows(const uint8_t *w, uint32_t n_rows, uint32_t n_cols, Q8Rows xq,

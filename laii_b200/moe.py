@@ -18,6 +18,7 @@ from . import _native
 from .synth import DenseLayer, MoELayer, Q8K_BYTES
 
 GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q6_K = 14
 
 STATUS = {0: "OK", -1: "INVALID_ARG", -2: "UNSUPPORTED", -3: "NOT_READY", -4: "OOM", -7: "CUDA", -8: "COMM",
           -9: "TIMEOUT", -10: "DEVICE_CHECK"}
@@ -83,11 +84,19 @@ class GpuMoE:
 
     # -- weights ---------------------------------------------------------
     def upload_layer(self, layer: int, L: MoELayer):
+        """Copy L into HBM; a layer whose down tensor is Q6_K (L.down_type 14) goes through
+        lfm_gpu_moe_upload_layer_typed."""
         keep = [np.ascontiguousarray(a) for a in (L.ffn_norm, L.router_w, L.gate, L.up, L.down)]
         bias = None if L.bias is None else np.ascontiguousarray(L.bias, dtype=np.float32)
-        self._check(self._lib.lfm_gpu_moe_upload_layer(
-            self._h, layer, L.D, L.E, L.K, L.I, L.eps, _ptr(keep[0]), _ptr(keep[1]), _ptr(bias), _ptr(keep[2]),
-            _ptr(keep[3]), _ptr(keep[4]), GGML_TYPE_Q4_K, int(L.norm_topk_prob), L.routed_scale))
+        down_type = int(getattr(L, "down_type", GGML_TYPE_Q4_K))
+        if down_type == GGML_TYPE_Q4_K:
+            self._check(self._lib.lfm_gpu_moe_upload_layer(
+                self._h, layer, L.D, L.E, L.K, L.I, L.eps, _ptr(keep[0]), _ptr(keep[1]), _ptr(bias), _ptr(keep[2]),
+                _ptr(keep[3]), _ptr(keep[4]), GGML_TYPE_Q4_K, int(L.norm_topk_prob), L.routed_scale))
+        else:
+            self._check(self._lib.lfm_gpu_moe_upload_layer_typed(
+                self._h, layer, L.D, L.E, L.K, L.I, L.eps, _ptr(keep[0]), _ptr(keep[1]), _ptr(bias), _ptr(keep[2]),
+                _ptr(keep[3]), _ptr(keep[4]), GGML_TYPE_Q4_K, down_type, int(L.norm_topk_prob), L.routed_scale))
         self.layers[layer] = ("moe", L.D, L.E, L.K, L.I)
 
     def upload_dense(self, layer: int, L: DenseLayer):

@@ -22,6 +22,9 @@ import numpy as np
 from . import _native
 
 Q4K_BYTES = 144
+Q6K_BYTES = 210
+GGML_Q4_K = 12  # GGUF tensor type ids (ggml_type)
+GGML_Q6_K = 14
 Q8K_BYTES = 292
 QK = 256
 
@@ -86,11 +89,66 @@ def dequantize_q4k(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_q6k(x: np.ndarray) -> np.ndarray:
+    """fp32 -> GGUF Q6_K blocks (210 bytes per 256 values), our own quantiser.
+
+    Per 16-value sub-block the scale is amax/31 (so codes q = rint(x/scale) lie in
+    [-32, 31]); the super-block d = max scale / 127 is stored as fp16 and each
+    sub-block keeps the int8 sc = rint(scale/d).  Codes are stored as q + 32 in
+    the GGUF bit layout: value i (half = i/128, m = (i/32)%4, l = i%32) keeps its
+    low nibble in ql[64*half + 32*(m%2) + l] (high nibble when m >= 2) and its top
+    two bits at bits 2m..2m+1 of qh[32*half + l]; then int8 scales[16], fp16 d.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    if x.size % QK:
+        raise ValueError("Q6_K quantisation needs a multiple of 256 values")
+    nb = x.size // QK
+    v = x.reshape(nb, 16, 16).astype(np.float64)
+    scale = np.abs(v).max(axis=2) / 31.0                       # [nb, 16]
+    d = (scale.max(axis=1) / 127.0).astype(np.float16)         # [nb]
+    d32 = d.astype(np.float64)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d32[:, None] > 0, np.rint(scale / d32[:, None]), 0.0)
+    sc = np.clip(sc, -128, 127).astype(np.int8)
+    eff = d32[:, None] * sc.astype(np.float64)                 # effective sub-block scale
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(eff[:, :, None] > 0, np.rint(v / eff[:, :, None]), 0.0)
+    u = (np.clip(q, -32, 31) + 32).astype(np.uint8).reshape(nb, 2, 4, 32)  # [b, half, m, l]
+    ql = np.empty((nb, 2, 64), np.uint8)
+    ql[:, :, :32] = (u[:, :, 0] & 15) | ((u[:, :, 2] & 15) << 4)
+    ql[:, :, 32:] = (u[:, :, 1] & 15) | ((u[:, :, 3] & 15) << 4)
+    qh = (u[:, :, 0] >> 4) | ((u[:, :, 1] >> 4) << 2) | ((u[:, :, 2] >> 4) << 4) | ((u[:, :, 3] >> 4) << 6)
+    out = np.empty((nb, Q6K_BYTES), np.uint8)
+    out[:, :128] = ql.reshape(nb, 128)
+    out[:, 128:192] = qh.reshape(nb, 64)
+    out[:, 192:208] = sc.view(np.uint8)
+    out[:, 208:210] = d.reshape(nb, 1).view(np.uint8)
+    return out.ravel()
+
+
+def dequantize_q6k(blocks: np.ndarray) -> np.ndarray:
+    """GGUF Q6_K blocks -> fp32: d * sc[i/16] * (q_i - 32)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, Q6K_BYTES)
+    nb = b.shape[0]
+    ql = b[:, :128].reshape(nb, 2, 64)
+    qh = b[:, 128:192].reshape(nb, 2, 32)
+    sc = b[:, 192:208].copy().view(np.int8).astype(np.float32)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32).reshape(nb)
+    u = np.empty((nb, 2, 4, 32), np.int32)
+    u[:, :, 0] = (ql[:, :, :32] & 15) | ((qh & 3) << 4)
+    u[:, :, 1] = (ql[:, :, 32:] & 15) | (((qh >> 2) & 3) << 4)
+    u[:, :, 2] = (ql[:, :, :32] >> 4) | (((qh >> 4) & 3) << 4)
+    u[:, :, 3] = (ql[:, :, 32:] >> 4) | (((qh >> 6) & 3) << 4)
+    q = (u.reshape(nb, 256) - 32).astype(np.float32)
+    return (d[:, None] * np.repeat(sc, 16, axis=1) * q).ravel()
+
+
 @dataclasses.dataclass
 class MoELayer:
     """Host copy of one lfm2moe layer, in GGUF layout.
 
-    gate/up: Q4_K [E][I][D/256] blocks; down: Q4_K [E][D][I/256] blocks;
+    gate/up: Q4_K [E][I][D/256] blocks; down: [E][D][I/256] blocks of Q4_K
+    (down_type 12) or Q6_K (down_type 14);
     router_w: fp32 [E, D]; bias (exp_probs_b): fp32 [E] or None; ffn_norm: fp32 [D].
     """
     D: int
@@ -106,6 +164,7 @@ class MoELayer:
     eps: float = 1e-5
     norm_topk_prob: bool = True
     routed_scale: float = 1.0
+    down_type: int = GGML_Q4_K
 
     def digest(self) -> str:
         h = hashlib.sha256()
@@ -129,19 +188,26 @@ class DenseLayer:
 
 def make_moe_layer(D: int, E: int, K: int, I: int, layer: int = 0, w_std: float = 0.02,
                    router_std: float = 0.02, bias_std: float = 0.1, bias: Optional[np.ndarray] = None,
-                   threads: int = 0) -> MoELayer:
-    """A synthetic lfm2moe layer: expert weights N(0, w_std) -> Q4_K, router N(0, router_std),
-    exp_probs_b N(0, bias_std) (or the given bias), ffn_norm = 1 (as the reference's MoE bench)."""
+                   threads: int = 0, down_type: int = GGML_Q4_K) -> MoELayer:
+    """A synthetic lfm2moe layer: expert weights N(0, w_std) -> Q4_K (down: Q6_K when
+    down_type is 14), router N(0, router_std), exp_probs_b N(0, bias_std) (or the given
+    bias), ffn_norm = 1 (as the reference's MoE bench)."""
     if D % QK or I % QK:
         raise ValueError("D and I must be multiples of 256")
+    if down_type not in (GGML_Q4_K, GGML_Q6_K):
+        raise ValueError(f"down_type {down_type}: only Q4_K (12) and Q6_K (14)")
     gate = q4k_normal(E * I * D // QK, layer_seed(SEED_GATE, layer), w_std, threads=threads)
     up = q4k_normal(E * I * D // QK, layer_seed(SEED_UP, layer), w_std, threads=threads)
-    down = q4k_normal(E * D * I // QK, layer_seed(SEED_DOWN, layer), w_std, threads=threads)
+    if down_type == GGML_Q6_K:
+        down = quantize_q6k(normal_f32(E * D * I, layer_seed(SEED_DOWN, layer), std=w_std, threads=threads))
+    else:
+        down = q4k_normal(E * D * I // QK, layer_seed(SEED_DOWN, layer), w_std, threads=threads)
     router = normal_f32(E * D, layer_seed(SEED_ROUTER, layer), std=router_std, threads=threads).reshape(E, D)
     if bias is None:
         bias = normal_f32(E, layer_seed(SEED_BIAS, layer), std=bias_std)
     return MoELayer(D=D, E=E, K=K, I=I, ffn_norm=np.ones(D, np.float32), router_w=router,
-                    bias=np.ascontiguousarray(bias, dtype=np.float32), gate=gate, up=up, down=down)
+                    bias=np.ascontiguousarray(bias, dtype=np.float32), gate=gate, up=up, down=down,
+                    down_type=down_type)
 
 
 def make_dense_layer(D: int, I: int, layer: int = 0, w_std: float = 0.02, threads: int = 0) -> DenseLayer:

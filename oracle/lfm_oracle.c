@@ -40,9 +40,11 @@ enum { ORC_ORDER_VNNI = 0, ORC_ORDER_AVX2 = 1 };
 #pragma pack(push, 1)
 typedef struct { uint16_t d, dmin; uint8_t scales[12]; uint8_t qs[128]; } orc_q4k;
 typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } orc_q8k;
+typedef struct { uint8_t ql[128]; uint8_t qh[64]; int8_t scales[16]; uint16_t d; } orc_q6k;
 #pragma pack(pop)
 
 _Static_assert(sizeof(orc_q4k) == 144, "q4k");
+_Static_assert(sizeof(orc_q6k) == 210, "q6k");
 _Static_assert(sizeof(orc_q8k) == 292, "q8k");
 
 static float orc_h2f(uint16_t h) {
@@ -228,6 +230,61 @@ ORC_EXPORT void orc_q4k_row_ints(const void *row, const void *xq, uint32_t n_col
         orc_q4k_sb_ints(&w[b], &x[b], sub_dots + 8 * b, &acc[b], &mins[b]);
 }
 
+/* Exact integer part of one Q6_K x Q8_K super-block (tools/lfm2_cpuid_quants.c:
+ * 467-509 scalar, :1398-1540 AVX-VNNI): element i (half = i/128, m = (i/32)%4,
+ * l = i%32) is  q = nibble m/2 of ql[64*half + 32*(m%2) + l]  |  bits 2m..2m+1 of
+ * qh[32*half + l] << 4  (0..63), with the signed scale of sub-block i/16;
+ * acc = sum sc*q*q8, off = sum sc_j*bsums_j, total = acc - 32*off. */
+static int32_t orc_q6k_sb_int(const orc_q6k *w, const orc_q8k *x, int32_t *acc_out, int32_t *off_out) {
+    int32_t acc = 0, off = 0;
+    for (int j = 0; j < 16; ++j) off += (int32_t)w->scales[j] * (int32_t)x->bsums[j];
+    for (int i = 0; i < 256; ++i) {
+        const int half = i >> 7, m = (i >> 5) & 3, l = i & 31;
+        const uint8_t lo = w->ql[64 * half + 32 * (m & 1) + l];
+        const int q = ((m & 2) ? (lo >> 4) : (lo & 15)) | (((w->qh[32 * half + l] >> (2 * m)) & 3) << 4);
+        acc += q * (int32_t)x->qs[i] * (int32_t)w->scales[i >> 4];
+    }
+    if (acc_out) *acc_out = acc;
+    if (off_out) *off_out = off;
+    return acc - 32 * off;
+}
+
+/* fp32 update per super-block, skipped where d8 == 0: AVX-VNNI 1x4 kernel
+ * sum = fma(d8*d, total, sum) (:1534); AVX2 1x4 kernel
+ * sum = sum + (d8*d)*total (tools/lfm2_cpuid_quants.c:1124). */
+static float orc_q6k_row(int order, const orc_q6k *row, const orc_q8k *x, uint32_t nb) {
+    float sum = 0.0f;
+    for (uint32_t b = 0; b < nb; ++b) {
+        const float d8 = x[b].d;
+        if (d8 == 0.0f) continue;
+        const int32_t tot = orc_q6k_sb_int(&row[b], &x[b], NULL, NULL);
+        const float dd = d8 * orc_h2f(row[b].d);
+        if (order == ORC_ORDER_VNNI) sum = fmaf(dd, (float)tot, sum);
+        else sum = sum + dd * (float)tot;
+    }
+    return sum;
+}
+
+/* out[r] = row r0+r of a Q6_K matrix [n_rows x n_cols] dotted with Q8_K xq. */
+ORC_EXPORT void orc_q6k_rows(int order, const void *W, uint32_t n_cols, uint32_t r0, uint32_t n_rows,
+                             const void *xq, float *out) {
+    const uint32_t nb = n_cols / 256;
+    const orc_q6k *w = (const orc_q6k *)W;
+    for (uint32_t r = 0; r < n_rows; ++r)
+        out[r] = orc_q6k_row(order, w + (size_t)(r0 + r) * nb, (const orc_q8k *)xq, nb);
+}
+
+/* Integer parts of one Q6_K row: acc[nb], off[nb], total[nb] = acc - 32*off. */
+ORC_EXPORT void orc_q6k_row_ints(const void *row, const void *xq, uint32_t n_cols, int32_t *acc, int32_t *off,
+                                 int32_t *total) {
+    const orc_q6k *w = (const orc_q6k *)row;
+    const orc_q8k *x = (const orc_q8k *)xq;
+    for (uint32_t b = 0; b < n_cols / 256; ++b) total[b] = orc_q6k_sb_int(&w[b], &x[b], &acc[b], &off[b]);
+}
+
+/* Bytes of one GGUF block of the down tensor's type (12: Q4_K, 14: Q6_K; 0 = unsupported). */
+static size_t orc_block_bytes(uint32_t type) { return type == 12u ? sizeof(orc_q4k) : type == 14u ? sizeof(orc_q6k) : 0; }
+
 /* Gate + Up + SwiGLU + Q8_K of h, tools/lfm2_decode_1x4.c:963-1065:
  * h = (g / (1 + expf(-g))) * u; then h quantised per 256. */
 static void orc_swiglu(int order, const orc_q4k *gate, const orc_q4k *up, uint32_t D, uint32_t I,
@@ -246,23 +303,28 @@ static void orc_swiglu(int order, const orc_q4k *gate, const orc_q4k *up, uint32
  * lfm2_forward_moe_ffn_1x4 (tools/lfm2_moe_checkpoint.c:312-365):
  *   RMSNorm+Q8_K, route, then for k = 0..K-1 in order:
  *   h = SwiGLU(gate_e x, up_e x) -> Q8_K, x[r] = fma(w_k, down_e[r] . h, x[r]).
- * Expert tensors are GGUF 3-D [E][rows][cols/256] Q4_K.  Optional outputs:
+ * Expert tensors are GGUF 3-D [E][rows][cols/256]: gate/up Q4_K, down Q4_K
+ * (down_type 12) or Q6_K (14, as Q4_K_M checkpoints store some ffn_down_exps,
+ * tools/lfm2_decode_1x4.c:618-630 selects the kernel by type).  Optional outputs:
  * idx/w [T*K], xq [T*D/256] (Q8_K of the normalised input), h [T*K*I].
  * Returns 0, or -1 on a shape it does not support.
  */
 ORC_EXPORT int orc_moe_forward(int order, float *x, uint32_t T, uint32_t D, uint32_t E, uint32_t K,
                                uint32_t I, float eps, const float *ffn_norm, const float *router_w,
                                const float *bias, const void *gate, const void *up, const void *down,
-                               int norm_topk, float routed_scale, uint32_t *idx_out, float *w_out,
-                               void *xq_out, float *h_out) {
+                               uint32_t down_type, int norm_topk, float routed_scale, uint32_t *idx_out,
+                               float *w_out, void *xq_out, float *h_out) {
     if (D % 256 || I % 256 || E == 0 || E > 256 || K == 0 || K > E || K > 8) return -1;
+    const size_t dn_bytes = orc_block_bytes(down_type);
+    if (!dn_bytes) return -1;
     const uint32_t nbd = D / 256, nbi = I / 256;
     float *xb = (float *)malloc(sizeof(float) * D);
     float *h = (float *)malloc(sizeof(float) * I);
     float *dn = (float *)malloc(sizeof(float) * D);
     orc_q8k *xq = (orc_q8k *)malloc(sizeof(orc_q8k) * (nbd + nbi));
     if (!xb || !h || !dn || !xq) { free(xb); free(h); free(dn); free(xq); return -2; }
-    const orc_q4k *G = (const orc_q4k *)gate, *U = (const orc_q4k *)up, *Dn = (const orc_q4k *)down;
+    const orc_q4k *G = (const orc_q4k *)gate, *U = (const orc_q4k *)up;
+    const uint8_t *Dn = (const uint8_t *)down;
     for (uint32_t t = 0; t < T; ++t) {
         float *xt = x + (size_t)t * D;
         orc_rmsnorm_q8k(xt, ffn_norm, D, eps, xb, xq);
@@ -276,7 +338,9 @@ ORC_EXPORT int orc_moe_forward(int order, float *x, uint32_t T, uint32_t D, uint
             if (w_out) w_out[(size_t)t * K + k] = w[k];
             orc_swiglu(order, G + (size_t)e * I * nbd, U + (size_t)e * I * nbd, D, I, xq, h, xq + nbd);
             if (h_out) memcpy(h_out + ((size_t)t * K + k) * I, h, sizeof(float) * I);
-            orc_q4k_rows(order, Dn + (size_t)e * D * nbi, I, 0, D, xq + nbd, dn);
+            const uint8_t *De = Dn + (size_t)e * D * nbi * dn_bytes;
+            if (down_type == 14u) orc_q6k_rows(order, De, I, 0, D, xq + nbd, dn);
+            else orc_q4k_rows(order, De, I, 0, D, xq + nbd, dn);
             for (uint32_t r = 0; r < D; ++r) xt[r] = fmaf(w[k], dn[r], xt[r]);
         }
     }

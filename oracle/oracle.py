@@ -50,8 +50,10 @@ class Oracle:
         lib.orc_q4k_rows.argtypes = [_int, _vp, _u32, _u32, _u32, _vp, _vp]
         lib.orc_q4k_row_ints.argtypes = [_vp, _vp, _u32, _vp, _vp, _vp]
         lib.orc_moe_forward.restype = _int
+        lib.orc_q6k_rows.argtypes = [_int, _vp, _u32, _u32, _u32, _vp, _vp]
+        lib.orc_q6k_row_ints.argtypes = [_vp, _vp, _u32, _vp, _vp, _vp]
         lib.orc_moe_forward.argtypes = [_int, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _vp, _vp, _vp, _vp, _vp,
-                                        _vp, _int, _f32, _vp, _vp, _vp, _vp]
+                                        _vp, _u32, _int, _f32, _vp, _vp, _vp, _vp]
         lib.orc_kat_router_inputs.argtypes = [_vp, _vp, _vp, _u32, _u32]
         lib.orc_kat_q8k_inputs.argtypes = [_vp, _u32]
         lib.orc_dense_ffn_forward.restype = _int
@@ -108,6 +110,20 @@ class Oracle:
         self.lib.orc_q4k_rows(order, _p(np.ascontiguousarray(W)), n_cols, r0, n_rows,
                               _p(np.ascontiguousarray(xq)), _p(out))
         return out
+
+    def q6k_rows(self, W, n_cols, n_rows, xq, order=ORDER_VNNI, r0=0):
+        out = np.zeros(n_rows, np.float32)
+        self.lib.orc_q6k_rows(order, _p(np.ascontiguousarray(W)), n_cols, r0, n_rows, _p(np.ascontiguousarray(xq)),
+                              _p(out))
+        return out
+
+    def q6k_row_ints(self, row, xq, n_cols):
+        """Per super-block (acc, off, total = acc - 32*off) of one Q6_K row against Q8_K xq."""
+        nb = n_cols // 256
+        acc, off, tot = (np.zeros(nb, np.int32) for _ in range(3))
+        self.lib.orc_q6k_row_ints(_p(np.ascontiguousarray(row)), _p(np.ascontiguousarray(xq)), n_cols, _p(acc),
+                                  _p(off), _p(tot))
+        return acc, off, tot
 
     def q4k_row_ints(self, row, xq, n_cols):
         nb = n_cols // 256
@@ -166,8 +182,8 @@ class Oracle:
         xq = np.zeros(T * (L.D // 256) * 292, np.uint8)
         h = np.zeros((T, L.K, L.I), np.float32) if want_h else None
         st = self.lib.orc_moe_forward(order, _p(x), T, L.D, L.E, L.K, L.I, L.eps, _p(L.ffn_norm), _p(L.router_w),
-                                      _p(L.bias), _p(L.gate), _p(L.up), _p(L.down), int(L.norm_topk_prob),
-                                      L.routed_scale, _p(idx), _p(w), _p(xq), _p(h))
+                                      _p(L.bias), _p(L.gate), _p(L.up), _p(L.down), int(getattr(L, "down_type", 12)),
+                                      int(L.norm_topk_prob), L.routed_scale, _p(idx), _p(w), _p(xq), _p(h))
         if st != 0:
             raise RuntimeError(f"oracle moe_forward status {st}")
         return x, idx, w, xq, h
@@ -258,7 +274,8 @@ class Reference:
         w = np.zeros((T, L.K), np.float32) if capture else None
         xq = np.zeros(T * (L.D // 256) * 292, np.uint8) if capture else None
         st = self.lib.ref_moe_forward(_p(x), T, L.D, L.E, L.K, L.I, L.eps, _p(L.ffn_norm), _p(L.router_w),
-                                      _p(L.bias), _p(L.gate), _p(L.up), _p(L.down), 12, _p(idx), _p(w), _p(xq))
+                                      _p(L.bias), _p(L.gate), _p(L.up), _p(L.down), int(getattr(L, "down_type", 12)), _p(idx), _p(w),
+                                      _p(xq))
         if st != 0:
             raise RuntimeError(f"reference moe_forward status {st}")
         return x, idx, w, xq

@@ -30,9 +30,9 @@ def reference():
 
 
 @functools.lru_cache(maxsize=None)
-def cached_layer(D, E, K, I, layer=0, zipf=None):
+def cached_layer(D, E, K, I, layer=0, zipf=None, down_type=12):
     from laii_b200 import synth
-    L = synth.make_moe_layer(D, E, K, I, layer=layer)
+    L = synth.make_moe_layer(D, E, K, I, layer=layer, down_type=down_type)
     if zipf is not None:
         L.bias = synth.zipf_bias(L, s=zipf)
     return L

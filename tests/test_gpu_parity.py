@@ -87,6 +87,38 @@ SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("D,E,K,I,T", [
+    (1024, 16, 4, 768, 1),     # decode: route, gate|up GEMV, h -> Q8_K, Q6_K down
+    (1024, 16, 4, 768, 8),
+    (1024, 16, 4, 768, 40),
+    (1024, 16, 4, 768, 300),   # prefill-sized: mma.sync gate/up GEMM, then the Q6_K down
+    (2048, 8, 4, 1792, 8),     # config-1/2 row lengths (D=2048, I=1792: 7 Q6_K super-blocks)
+])
+def test_q6k_down_layer_parity(oracle, gpu, D, E, K, I, T):
+    """Q6_K ffn_down_exps (upload_layer_typed): same bars as the Q4_K layers."""
+    from laii_b200 import synth
+    L = cached_layer(D, E, K, I, down_type=14)
+    x = synth.make_hidden(T, D, seed_offset=11)
+    xg, xo, match = compare_layer(oracle, gpu, L, x, 1)
+    # exact integers and the reference's fp32 order: equal on almost every element
+    assert np.mean(xg[match] == xo[match]) > 0.9
+    assert gpu.last_stats()["tokens"] == T
+
+
+def test_q6k_down_layer_refused_where_q4k_only(gpu):
+    """The no-allocate entry point takes Q4_K layers only: a Q6_K-down layer is an
+    error status with a message, not a wrong result."""
+    import ctypes
+    torch = pytest.importorskip("torch")
+    from laii_b200 import _native, synth
+    lib = _native.load_gpu()
+    gpu.upload_layer(2, cached_layer(1024, 16, 4, 768, down_type=14))
+    xt = torch.from_numpy(synth.make_hidden(4, 1024, seed_offset=3)).cuda()
+    st = lib.lfm_gpu_moe_forward_noalloc(gpu._h, 2, ctypes.c_void_p(xt.data_ptr()), 4, None)
+    assert st != 0 and b"Q6_K" in lib.lfm_gpu_moe_last_error(gpu._h)
+    gpu.sync()
+
+
 @pytest.mark.parametrize("D,E,K,I,T", SHAPES)
 def test_moe_layer_parity(oracle, gpu, D, E, K, I, T):
     from laii_b200 import synth

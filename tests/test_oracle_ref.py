@@ -72,6 +72,21 @@ def test_moe_layer(oracle, reference, D, E, K, I, T):
     assert np.array_equal(xr, xo)
 
 
+@pytest.mark.parametrize("D,E,K,I,T", [(512, 8, 2, 512, 3), (1024, 16, 4, 768, 5)])
+def test_moe_layer_q6k_down(oracle, reference, D, E, K, I, T):
+    """Q6_K ffn_down_exps (Q4_K_M checkpoints): the reference selects its Q6_K x Q8_K
+    kernel by tensor type (tools/lfm2_decode_1x4.c:618-630); bit for bit."""
+    from laii_b200 import synth
+    L = cached_layer(D, E, K, I, down_type=14)
+    x = synth.make_hidden(T, D, seed_offset=33)
+    xr, ir, wr, qr = reference.moe_forward(L, x)
+    xo, io, wo, qo, _ = oracle.moe_forward(L, x, order=reference.order)
+    assert np.array_equal(ir, io) and np.array_equal(wr, wo) and np.array_equal(qr, qo)
+    assert np.array_equal(xr, xo)
+    # the Q6_K layer is a different layer from its Q4_K twin, not a relabelled one
+    assert not np.array_equal(xo, oracle.moe_forward(cached_layer(D, E, K, I), x, order=reference.order)[0])
+
+
 def test_dense_layer(oracle, reference):
     from conftest import cached_dense
     from laii_b200 import synth

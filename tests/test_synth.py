@@ -86,3 +86,32 @@ def test_zipf_bias_skews_popularity(oracle):
         counts[idx] += 1
     c = np.sort(counts)[::-1]
     assert c[0] > 2.5 * c[-1]
+
+
+def test_q6k_quantiser_layout_and_oracle_integer_sums(oracle):
+    """Our Q6_K quantiser round-trips within 6-bit error, and the oracle's exact
+    super-block integers equal a direct numpy restatement over the dequantised
+    codes: total = sum_i sc[i/16] * (q_i - 32) * q8_i (GGUF Q6_K layout)."""
+    from laii_b200 import synth
+    from oracle.oracle import q8k_fields
+    x = synth.normal_f32(256 * 16, seed=77, std=0.02)
+    x[:256] = 0.0                                  # all-zero super-block: d = 0
+    blocks = synth.quantize_q6k(x)
+    assert blocks.size == 16 * synth.Q6K_BYTES
+    y = synth.dequantize_q6k(blocks)
+    assert np.array_equal(y[:256], np.zeros(256, np.float32))
+    assert np.linalg.norm(y - x) / np.linalg.norm(x) < 0.03
+    v = synth.normal_f32(256 * 16, seed=78, std=1.0)
+    xq = oracle.quantize_q8k(v)
+    acc, off, tot = oracle.q6k_row_ints(blocks, xq, x.size)
+    _, qs, bs = q8k_fields(xq, 16)
+    b = blocks.reshape(16, synth.Q6K_BYTES)
+    sc = b[:, 192:208].copy().view(np.int8).astype(np.int64)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float64).reshape(16)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        codes = np.where(d[:, None] > 0, y.reshape(16, 256) / (d[:, None] * np.repeat(sc, 16, axis=1)), 0)
+    q = np.rint(codes).astype(np.int64)            # q_i - 32
+    want = (np.repeat(sc, 16, axis=1) * q * qs.astype(np.int64)).sum(axis=1)
+    assert np.array_equal(tot.astype(np.int64), want)
+    assert np.array_equal(off.astype(np.int64), (sc * bs.astype(np.int64)).sum(axis=1))
+    assert np.array_equal(tot, acc - 32 * off)
