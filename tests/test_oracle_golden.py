@@ -53,7 +53,7 @@ def test_q8k_known_answer(oracle):
 def test_moe_layer_golden(oracle, name):
     from laii_b200 import synth
     c = META["cases"]["moe"][name]
-    L = synth.make_moe_layer(c["D"], c["E"], c["K"], c["I"], layer=c["layer"])
+    L = synth.make_moe_layer(c["D"], c["E"], c["K"], c["I"], layer=c["layer"], down_type=c.get("down_type", 12))
     x = synth.make_hidden(c["T"], c["D"], seed_offset=c["seed_offset"])
     assert L.digest() == META["digests"][name]["layer"], "synthetic generator changed"
     assert hashlib.sha256(x.tobytes()).hexdigest() == META["digests"][name]["x"]
