@@ -231,7 +231,7 @@ lfm_gpu_status_t lfm_gpu_moe_ep_p2p_detach(lfm_gpu_moe_t *h);
  * them (lfm2_bind_moe_layer, tools/lfm2_moe_checkpoint.c:70-102, on the
  * tensors and keys its loader reads, tools/lfm2_loader.c:359-366, :537-602):
  * block l is an lfm2moe layer when blk.l.ffn_gate_exps.weight exists (Q4_K
- * experts, F32 ffn_gate_inp router, optional exp_probs_b(.bias), top-K from
+ * experts, ffn_down_exps Q4_K or Q6_K, F32 ffn_gate_inp router, optional exp_probs_b(.bias), top-K from
  * the ".expert_used_count" key, default 4), else a dense SwiGLU layer from
  * blk.l.ffn_{gate,up,down}.weight; both take blk.l.ffn_norm.weight and the
  * ".attention.layer_norm_rms_epsilon" key (default 1e-5). */
@@ -240,6 +240,7 @@ typedef struct {
     uint32_t D, E, K, I;
     float eps;
     int has_bias, has_norm;
+    uint32_t down_type; /* GGUF type of the down tensor: 12 (Q4_K) or, lfm2moe only, 14 (Q6_K); 0: no FFN */
 } lfm_gpu_moe_gguf_block_t;
 
 /* Describe block `block` of the file (host only, no GPU needed); *n_blocks =

@@ -27,7 +27,7 @@ class Stats(ctypes.Structure):
 
 class GgufBlock(ctypes.Structure):
     _fields_ = [("kind", c_u32), ("D", c_u32), ("E", c_u32), ("K", c_u32), ("I", c_u32), ("eps", c_f32),
-                ("has_bias", c_int), ("has_norm", c_int)]
+                ("has_bias", c_int), ("has_norm", c_int), ("down_type", c_u32)]
 
 
 class KernelTime(ctypes.Structure):

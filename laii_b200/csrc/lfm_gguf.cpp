@@ -35,8 +35,8 @@
 namespace {
 
 constexpr uint32_t kGgufMagic = 0x46554747u; /* "GGUF" little-endian */
-constexpr uint32_t kTypeF32 = 0, kTypeQ4K = 12;
-constexpr uint64_t kQ4kBytes = 144;
+constexpr uint32_t kTypeF32 = 0, kTypeQ4K = 12, kTypeQ6K = 14;
+constexpr uint64_t kQ4kBytes = 144, kQ6kBytes = 210;
 
 enum ValueType : uint32_t {
     V_U8 = 0, V_I8, V_U16, V_I16, V_U32, V_I32, V_F32, V_BOOL, V_STR, V_ARR, V_U64, V_I64, V_F64
@@ -154,9 +154,9 @@ bool tensor_bytes(TensorInfo &t) {
     uint64_t n = 1;
     for (uint32_t i = 0; i < t.n_dims; ++i) n *= t.ne[i];
     if (t.type == kTypeF32) { t.bytes = 4 * n; return true; }
-    if (t.type == kTypeQ4K) {
+    if (t.type == kTypeQ4K || t.type == kTypeQ6K) {
         if (t.ne[0] % 256) return false;
-        t.bytes = n / 256 * kQ4kBytes;
+        t.bytes = n / 256 * (t.type == kTypeQ4K ? kQ4kBytes : kQ6kBytes);
         return true;
     }
     t.bytes = 0; /* another type: described, never uploaded */
@@ -254,11 +254,13 @@ BlockFfn bind_block(GgufFile &f, uint32_t l) {
         b.I = (uint32_t)b.gate->ne[1];
         b.E = b.gate->n_dims >= 3 ? (uint32_t)b.gate->ne[2] : (uint32_t)f.expert_count;
         b.K = f.expert_used ? (uint32_t)f.expert_used : 4u;
+        /* Q4_K_M files store some ffn_down_exps as Q6_K */
         if (!is(b.gate, kTypeQ4K, 3, b.D, b.I, b.E) || !is(b.up, kTypeQ4K, 3, b.D, b.I, b.E) ||
-            !is(b.down, kTypeQ4K, 3, b.I, b.D, b.E) || !is(b.router, kTypeF32, 2, b.D, b.E) ||
+            !(is(b.down, kTypeQ4K, 3, b.I, b.D, b.E) || is(b.down, kTypeQ6K, 3, b.I, b.D, b.E)) ||
+            !is(b.router, kTypeF32, 2, b.D, b.E) ||
             (b.bias && !is(b.bias, kTypeF32, 1, b.E)) || (b.norm && !is(b.norm, kTypeF32, 1, b.D))) {
             snprintf(f.err, sizeof f.err,
-                     "block %u: MoE tensors must be Q4_K experts [D,I,E]/[I,D,E] with F32 router [D,E], bias [E], norm [D]", l);
+                     "block %u: MoE tensors must be Q4_K experts [D,I,E]/[I,D,E] (down Q4_K or Q6_K) with F32 router [D,E], bias [E], norm [D]", l);
             b.kind = -1;
             return b;
         }
@@ -317,6 +319,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_gguf_describe(const char *path, uint32_t bl
     out->eps = f.eps;
     out->has_bias = b.bias ? 1 : 0;
     out->has_norm = b.norm ? 1 : 0;
+    out->down_type = b.kind > 0 ? b.down->type : 0;
     return LFM_GPU_OK;
 }
 
@@ -352,10 +355,14 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_upload_gguf(lfm_gpu_moe_t *h, const char *p
             st = lfm_gpu_moe_upload_dense(h, i, b.D, b.I, f.eps, static_cast<const float *>(ptr(b.norm)), ptr(b.gate),
                                           ptr(b.up), ptr(b.down), kTypeQ4K);
         } else if (n_local == 0) {
-            st = lfm_gpu_moe_upload_layer(h, i, b.D, b.E, b.K, b.I, f.eps, static_cast<const float *>(ptr(b.norm)),
-                                          static_cast<const float *>(ptr(b.router)),
-                                          static_cast<const float *>(ptr(b.bias)), ptr(b.gate), ptr(b.up), ptr(b.down),
-                                          kTypeQ4K, 1, 1.0f);
+            st = lfm_gpu_moe_upload_layer_typed(h, i, b.D, b.E, b.K, b.I, f.eps, static_cast<const float *>(ptr(b.norm)),
+                                                static_cast<const float *>(ptr(b.router)),
+                                                static_cast<const float *>(ptr(b.bias)), ptr(b.gate), ptr(b.up),
+                                                ptr(b.down), kTypeQ4K, b.down->type, 1, 1.0f);
+        } else if (b.down->type != kTypeQ4K) {
+            snprintf(g_describe_err, sizeof g_describe_err,
+                     "block %u: an expert shard needs Q4_K down experts (this file's are type %u)", l, b.down->type);
+            return LFM_GPU_ERR_UNSUPPORTED;
         } else {
             if (expert_first + n_local > b.E) {
                 snprintf(g_describe_err, sizeof g_describe_err, "block %u: experts [%u, %u) past E=%u", l, expert_first,

@@ -44,7 +44,7 @@ def gguf_describe(path: str, block: int) -> Tuple[dict, int]:
         raise MoEError(st, lib.lfm_gpu_moe_gguf_last_error().decode(errors="replace"))
     kind = {0: "none", 1: "dense", 2: "moe"}[out.kind]
     return ({"kind": kind, "D": out.D, "E": out.E, "K": out.K, "I": out.I, "eps": out.eps,
-             "has_bias": bool(out.has_bias), "has_norm": bool(out.has_norm)}, n.value)
+             "has_bias": bool(out.has_bias), "has_norm": bool(out.has_norm), "down_type": out.down_type}, n.value)
 
 
 class GpuMoE:

@@ -27,6 +27,7 @@ def _layers():
 def _write(path, dense, m1, m2, drop=None, eps=1e-5):
     gguf = pytest.importorskip("gguf")
     Q4K = gguf.GGMLQuantizationType.Q4_K
+    Q6K = gguf.GGMLQuantizationType.Q6_K
     w = gguf.GGUFWriter(str(path), "lfm2moe")
     w.add_uint32("lfm2moe.block_count", 3)
     w.add_uint32("lfm2moe.expert_count", E)
@@ -42,6 +43,15 @@ def _write(path, dense, m1, m2, drop=None, eps=1e-5):
         if name != drop:
             w.add_tensor(name, np.ascontiguousarray(arr, dtype=np.float32))
 
+    def down_exps(name, m):  # Q4_K, or Q6_K as Q4_K_M files store some ffn_down_exps
+        if name == drop:
+            return
+        if m.down_type == 14:
+            w.add_tensor(name, np.ascontiguousarray(m.down, dtype=np.uint8).reshape(E, D, I // 256 * 210),
+                         raw_dtype=Q6K)
+        else:
+            q4k(name, m.down, (E, D, I // 256 * 144))
+
     nb, nbi, nbd = D // 256 * 144, I // 256 * 144, DI // 256 * 144
     f32("blk.0.ffn_norm.weight", dense.ffn_norm)
     q4k("blk.0.ffn_gate.weight", dense.gate, (DI, nb))
@@ -53,7 +63,7 @@ def _write(path, dense, m1, m2, drop=None, eps=1e-5):
         f32(f"blk.{l}.{bias_name}", m.bias)
         q4k(f"blk.{l}.ffn_gate_exps.weight", m.gate, (E, I, nb))
         q4k(f"blk.{l}.ffn_up_exps.weight", m.up, (E, I, nb))
-        q4k(f"blk.{l}.ffn_down_exps.weight", m.down, (E, D, nbi))
+        down_exps(f"blk.{l}.ffn_down_exps.weight", m)
     w.write_header_to_file()
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
@@ -73,7 +83,7 @@ def test_describe_binds_dense_and_moe_blocks(stack):
     b0, n = gguf_describe(path, 0)
     assert n == 3
     assert b0 == {"kind": "dense", "D": D, "E": 1, "K": 1, "I": DI, "eps": pytest.approx(1e-5), "has_bias": False,
-                  "has_norm": True}
+                  "has_norm": True, "down_type": 12}
     for l in (1, 2):  # exp_probs_b.bias and the bare exp_probs_b name both bind
         b, _ = gguf_describe(path, l)
         assert (b["kind"], b["D"], b["E"], b["K"], b["I"], b["has_bias"]) == ("moe", D, E, K, I, True)
@@ -99,6 +109,41 @@ def test_describe_refuses_incomplete_and_truncated_files(tmp_path):
     bad.write_bytes(b"NOTGGUF" + bytes(64))
     with pytest.raises(MoEError):
         gguf_describe(bad, 0)
+
+
+@pytest.fixture(scope="module")
+def stack_q6k(tmp_path_factory):
+    """Block 2's ffn_down_exps stored as Q6_K."""
+    dense, m1, _ = _layers()
+    m2 = synth.make_moe_layer(D, E, K, I, layer=3, down_type=14)
+    path = tmp_path_factory.mktemp("gguf") / "lfm2moe-ffn-q6k.gguf"
+    _write(path, dense, m1, m2)
+    return path, dense, m1, m2
+
+
+def test_describe_binds_q6k_down_experts(stack_q6k):
+    path = stack_q6k[0]
+    b1, _ = gguf_describe(path, 1)
+    b2, _ = gguf_describe(path, 2)
+    assert (b1["kind"], b1["down_type"]) == ("moe", 12)
+    assert (b2["kind"], b2["D"], b2["E"], b2["I"], b2["down_type"]) == ("moe", D, E, I, 14)
+
+
+@pytest.mark.gpu
+def test_upload_gguf_q6k_down_matches_upload_of_the_same_arrays(stack_q6k):
+    path, dense, m1, m2 = stack_q6k
+    x = synth.make_hidden(24, D, seed_offset=5)
+    with GpuMoE(0) as ref:
+        ref.upload_dense(0, dense)
+        ref.upload_layer(1, m1)
+        ref.upload_layer(2, m2)
+        want = ref.forward_stack(0, 3, np.array(x, copy=True))
+    with GpuMoE(0) as g:
+        assert g.upload_gguf(path) == 3
+        got = g.forward_stack(0, 3, np.array(x, copy=True))
+        with pytest.raises(MoEError, match="Q4_K down"):
+            g.upload_gguf(path, first_block=2, n_blocks=1, expert_first=0, n_local=4)
+    assert np.array_equal(got, want)
 
 
 @pytest.mark.gpu
