@@ -108,8 +108,9 @@ def dist_setup():
 
 
 def config_dict(cfg_id, cfg, ring, extra=None):
+    experts = "Q4_K gate/up and Q6_K down experts" if cfg.get("down_q6k") else "Q4_K experts"
     d = {"workload": f"cfg{cfg_id}: {cfg['name']} (lfm2moe FFN layer, D={cfg['D']} E={cfg['E']} top-{cfg['K']} "
-                     f"I={cfg['I']}, Q4_K experts, T={cfg['T']} tokens per step)",
+                     f"I={cfg['I']}, {experts}, T={cfg['T']} tokens per step)",
          "tokens_per_step": cfg["T"], "D": cfg["D"], "E": cfg["E"], "K": cfg["K"], "I": cfg["I"],
          "layers_in_ring": ring,
          "l2": f"steps cycle a ring of {ring} distinct layers "
@@ -120,9 +121,13 @@ def config_dict(cfg_id, cfg, ring, extra=None):
     return d
 
 
+def down_block_bytes(cfg):
+    return 210 if cfg.get("down_q6k") else Q4K  # Q6_K or Q4_K super-block of the down tensor
+
+
 def expert_bytes(cfg):
     D, I = cfg["D"], cfg["I"]
-    return (2 * I * (D // 256) + D * (I // 256)) * Q4K
+    return 2 * I * (D // 256) * Q4K + D * (I // 256) * down_block_bytes(cfg)
 
 
 def layer_seeds(layer):
@@ -144,7 +149,8 @@ def cpu_baseline(cfg, seconds=12.0, threads=0):
     """The reference's CPU MoE FFN (built from its sources) on this host, bounded sample."""
     from laii_b200 import synth
     from oracle.oracle import REF_SO, Oracle, Reference
-    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0)
+    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0,
+                             down_type=14 if cfg.get("down_q6k") else 12)
     T = cfg["T"]
     x = synth.make_hidden(T, cfg["D"], seed_offset=0)
     if os.path.exists(REF_SO):
@@ -175,7 +181,8 @@ def run_reference(args, cfg):
         return
     from laii_b200 import synth
     from oracle.oracle import REF_SO, Oracle, Reference
-    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0)
+    L = synth.make_moe_layer(cfg["D"], cfg["E"], cfg["K"], cfg["I"], layer=0,
+                             down_type=14 if cfg.get("down_q6k") else 12)
     T = cfg["T"]
     x = synth.make_hidden(T, cfg["D"], seed_offset=0)
     if os.path.exists(REF_SO):
@@ -220,7 +227,11 @@ def run_ours(args, cfg):
     D, E, K, I, T = cfg["D"], cfg["E"], cfg["K"], cfg["I"], cfg["T"]
     R = args.ring
     g = GpuMoE(local)
-    for l in range(R):
+    if cfg.get("down_q6k"):  # host-made layers (Q6_K down from our own quantiser), fewer of them
+        R = min(R, 2)
+        for l in range(R):
+            g.upload_layer(l, synth.make_moe_layer(D, E, K, I, layer=l, down_type=14))
+    for l in range(0 if cfg.get("down_q6k") else R):
         bias = zipf_bias_for(cfg, l) if cfg.get("zipf") else None
         g.synth_layer(l, D, E, K, I, layer_seeds(l), bias=bias)
     g.reserve(T)
@@ -283,7 +294,7 @@ def run_ours(args, cfg):
     dom = max(known or list(prof), key=lambda k: prof[k][1])
     n_launch, tot_ms = prof[dom]
     gu_bytes = 2 * I * (D // 256) * Q4K
-    dn_bytes = D * (I // 256) * Q4K
+    dn_bytes = D * (I // 256) * down_block_bytes(cfg)
     # algorithmic bytes per launch: the active experts' Q4_K bytes (each read once) plus, for the
     # fused layer, the router rows and x in/out; Q8_K activations at 292/256 bytes per value
     per_launch_bytes = {"gateup": ploads * gu_bytes / n_launch + T * D * 1.140625,
@@ -329,7 +340,9 @@ def run_ours(args, cfg):
     if rank == 0:
         out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-               "vs_baseline": None, "dtype": "u8 x s8 -> s32 (q4_k x q8_k), fp32 accum", "data": "synthetic (seeded)",
+               "vs_baseline": None, "data": "synthetic (seeded)",
+               "dtype": ("u8 x s8 -> s32 (q4_k x q8_k; down q6_k x q8_k), fp32 accum" if cfg.get("down_q6k")
+                         else "u8 x s8 -> s32 (q4_k x q8_k), fp32 accum"),
                "config": config_dict(args.config, cfg, R, {"parallelism": f"replicas x{ws}" if ws > 1 else "single",
                                                            "layer_hbm_frac": round(layer_frac, 4),
                                                            "unique_experts_per_step": loads / args.steps}),
@@ -599,9 +612,15 @@ def main():
     ap.add_argument("--ring", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--down-q6k", action="store_true",
+                    help="configs 1-3: the layers' ffn_down_exps in Q6_K (as Q4_K_M checkpoints store some)")
     args = ap.parse_args()
     from laii_b200.synth import CONFIGS
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.down_q6k:
+        if args.config >= 4:
+            raise SystemExit("--down-q6k: single-layer configs 1-3 only")
+        cfg["down_q6k"] = True
     if args.impl == "reference":
         run_reference(args, cfg)
     elif args.config >= 4:

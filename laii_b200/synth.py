@@ -102,6 +102,9 @@ def quantize_q6k(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     if x.size % QK:
         raise ValueError("Q6_K quantisation needs a multiple of 256 values")
+    step = 1 << 24  # values per piece: bounds the float64 temporaries
+    if x.size > step:
+        return np.concatenate([quantize_q6k(x[i:i + step]) for i in range(0, x.size, step)])
     nb = x.size // QK
     v = x.reshape(nb, 16, 16).astype(np.float64)
     scale = np.abs(v).max(axis=2) / 31.0                       # [nb, 16]
