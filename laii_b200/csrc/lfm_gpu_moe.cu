@@ -509,6 +509,8 @@ static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint
     if (down_type != LFM_GGML_TYPE_Q4_K && down_type != LFM_GGML_TYPE_Q6_K)
         return fail(h, LFM_GPU_ERR_UNSUPPORTED, "down weight type %u (Q4_K=12 or Q6_K=14)", down_type);
     const bool q6k = down_type == LFM_GGML_TYPE_Q6_K;
+    if (q6k && I > 3072)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED, "Q6_K down with I=%u (the Q6_K kernel stages rows of I <= 3072)", I);
     if (!router_w || !gate_exps || !up_exps || !down_exps) return fail(h, LFM_GPU_ERR_INVALID_ARG, "null tensor");
     DeviceGuard g(h->device);
     drop_graphs(h);
@@ -522,7 +524,8 @@ static lfm_gpu_status_t upload_layer_impl(lfm_gpu_moe_t *h, uint32_t layer, uint
     for (int i = 0; i < 6; ++i) {
         if (i == 0 && !ffn_norm) continue;
         if (i == 2 && !exp_probs_b) continue;
-        cudaError_t e = cudaMalloc(&S.bufs[i], sz[i]);
+        /* a Q6_K down tensor gets 16 bytes of slack: k_q6k.cu copies 16-byte aligned spans around its rows */
+        cudaError_t e = cudaMalloc(&S.bufs[i], sz[i] + (i == 5 && q6k ? 16 : 0));
         if (e == cudaSuccess && i == 2) e = cudaMemset(S.bufs[i], 0, sz[i]); /* bias padded to 16 bytes */
         if (e == cudaSuccess)
             e = cudaMemcpy(S.bufs[i], src[i], i == 2 ? sizeof(float) * E : sz[i], cudaMemcpyHostToDevice);
