@@ -93,7 +93,7 @@ lfm_gpu_status_t lfm_gpu_moe_upload_layer(lfm_gpu_moe_t *h, uint32_t layer, uint
  * lfm2_compute_4rows_avx2 picks its Q6_K x Q8_K kernel by the tensor type,
  * tools/lfm2_decode_1x4.c:618-630; Q6_K block, tools/lfm2_cpuid_quants.c:101-106):
  *   gate_up_type 12 (Q4_K); down_type 12 (Q4_K) or 14 (Q6_K: [E][D][I/256]
- *   210-byte blocks).
+ *   210-byte blocks; I <= 3072).
  * A Q6_K-down layer runs the route, the Q4_K gate|up GEMV (or GEMM) and a
  * dedicated Q6_K down kernel; the fused decode kernel, the tcgen05 GEMMs, the
  * peer-memory expert-parallel path and lfm_gpu_moe_forward_noalloc take Q4_K

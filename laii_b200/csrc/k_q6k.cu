@@ -21,14 +21,14 @@
  * packs sc*q of a value pair as two int16 and dots it with the pair's Q8_K
  * codes by dp2a.
  *
- * Work unit of a CTA (8 warps): one dispatch pair and 64 consecutive down rows.
- *  - Each warp starts 16-byte cp.async copies of its 8 weight rows into its own
+ * Work unit of a CTA (8 warps): one dispatch pair and 32 consecutive down rows.
+ *  - Each warp starts 16-byte cp.async copies of its 4 weight rows into its own
  *    shared-memory slab: a row of nb 210-byte blocks starts only 2-byte
  *    aligned, so the copy covers the 16-byte aligned span around it and the
  *    row is read at its offset inside the span (the upload pads the tensor by
  *    16 bytes so the span of the last row stays inside the allocation).
  *  - Meanwhile the CTA stages the pair's Q8_K activations (codes, bsums, d of
- *    its nt tokens) in shared memory once for all 64 rows.
+ *    its nt tokens) in shared memory once for all 32 rows (64 KB a CTA at I = 1792: three CTAs an SM).
  *  - Then each warp computes its rows from shared memory only.
  *
  * Exact integer part per (token, super-block): the lanes' dp2a sums, lanes
@@ -47,9 +47,9 @@ namespace {
 
 constexpr int kCh = LFM_GEMV_CHUNK; /* tokens per pair (8) */
 constexpr int kWarps = 8;
-constexpr int kRowsPerWarp = 8;
+constexpr int kRowsPerWarp = 4;
 constexpr int kUnitRows = kWarps * kRowsPerWarp; /* 64 */
-constexpr uint32_t kMaxNb = 12;                  /* I <= 3072: 190 KB of shared memory */
+constexpr uint32_t kMaxNb = 12;                  /* I <= 3072: 109 KB of shared memory a CTA */
 
 /* bytes of one staged weight row: the 16-byte aligned span around nb blocks */
 __host__ __device__ inline uint32_t q6k_row_span(uint32_t nb) { return (nb * LFM_Q6K_BYTES + 14u + 15u) & ~15u; }
@@ -169,6 +169,6 @@ cudaError_t lfm_launch_down_q6k(const MoeLayerDev &L, Q8Rows hq, const RouteTabl
     const size_t smem = q6k_smem(L.I / 256);
     cudaError_t e = lfm_smem_attr((const void *)k_q6k_down, smem, cache);
     if (e != cudaSuccess) return e;
-    k_q6k_down<<<grid * 2, kWarps * 32, smem, s>>>(L, hq, rt, y);
+    k_q6k_down<<<grid * 3, kWarps * 32, smem, s>>>(L, hq, rt, y);
     return cudaGetLastError();
 }
