@@ -4,8 +4,8 @@
  * tensor's type, tools/lfm2_decode_1x4.c:618-630).
  *
  * Work list: the dispatch tables' (active expert u, 8-token chunk c) pairs, as
- * for the Q4_K GEMVs.  One warp computes one down row r of expert e for the
- * chunk's nt <= 8 slots: y[slot][r] = Down_e[r,:] . hq[slot].
+ * for the Q4_K GEMVs.  A warp computes down rows r of expert e for the chunk's
+ * nt <= 8 slots: y[slot][r] = Down_e[r,:] . hq[slot].
  *
  * Super-block layout (block_q6_K, 210 bytes, tools/lfm2_cpuid_quants.c:101-106):
  * ql[128], qh[64], int8 scales[16], fp16 d.  Value v = 128h + 32m + k (half h,
@@ -48,7 +48,7 @@ namespace {
 constexpr int kCh = LFM_GEMV_CHUNK; /* tokens per pair (8) */
 constexpr int kWarps = 8;
 constexpr int kRowsPerWarp = 4;
-constexpr int kUnitRows = kWarps * kRowsPerWarp; /* 64 */
+constexpr int kUnitRows = kWarps * kRowsPerWarp; /* 32 */
 constexpr uint32_t kMaxNb = 12;                  /* I <= 3072: 109 KB of shared memory a CTA */
 
 /* bytes of one staged weight row: the 16-byte aligned span around nb blocks */
