@@ -325,6 +325,13 @@ lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void *w, uin
 lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
                                               size_t bytes);
 
+/* As lfm_gpu_moe_debug_read_layer, bytes [offset, offset + bytes) of the tensor
+ * (one expert's slab of a 3-D expert tensor, for a parity check that needs only
+ * the experts its tokens were routed to).  Synchronous.  No counterpart in the
+ * reference. */
+lfm_gpu_status_t lfm_gpu_moe_debug_read_layer_range(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which,
+                                                    size_t offset, void *out, size_t bytes);
+
 /* Wait for all work on the handle's stream and report any device-side error
  * (bounds check or timeout) raised since the last call. */
 lfm_gpu_status_t lfm_gpu_moe_sync(lfm_gpu_moe_t *h);

@@ -69,6 +69,7 @@ GPU_API = [
     ("lfm_gpu_moe_debug_route", c_int, [c_vp, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_debug_q4k_rows", c_int, [c_vp, c_vp, c_u32, c_u32, c_vp, c_u32, c_vp, c_vp, c_vp, c_vp]),
     ("lfm_gpu_moe_debug_read_layer", c_int, [c_vp, c_u32, c_u32, c_vp, ctypes.c_size_t]),
+    ("lfm_gpu_moe_debug_read_layer_range", c_int, [c_vp, c_u32, c_u32, ctypes.c_size_t, c_vp, ctypes.c_size_t]),
     ("lfm_gpu_moe_sync", c_int, [c_vp]),
     ("lfm_gpu_moe_last_stats", c_int, [c_vp, ctypes.POINTER(Stats)]),
     ("lfm_gpu_moe_profile", c_int, [c_vp, c_int]),
@@ -115,6 +116,11 @@ def load_gpu(build_if_missing: bool = True):
                 raise RuntimeError(f"CUDA library missing: {_build.GPU_SO} (run python -m laii_b200.build)")
             _gpu = _bind(ctypes.CDLL(_build.GPU_SO), GPU_API)
         return _gpu
+
+
+def bind_synth(lib):
+    """Bind the generator entry points on an already loaded build of csrc/lfm_synth.c."""
+    return _bind(lib, SYNTH_API)
 
 
 def load_synth(build_if_missing: bool = True):

@@ -150,14 +150,20 @@ struct GgufFile {
     }
 };
 
+/* Byte size of a tensor from its dims.  Dims come from the file, so every one
+ * must be in [1, 2^32) and the products must not wrap: a wrapped size would pass
+ * the end-of-file check below while the shapes cast to uint32 describe far more
+ * bytes than the mapping holds. */
 bool tensor_bytes(TensorInfo &t) {
     uint64_t n = 1;
-    for (uint32_t i = 0; i < t.n_dims; ++i) n *= t.ne[i];
-    if (t.type == kTypeF32) { t.bytes = 4 * n; return true; }
+    for (uint32_t i = 0; i < t.n_dims; ++i) {
+        if (t.ne[i] == 0 || t.ne[i] > 0xFFFFFFFFull) return false;
+        if (__builtin_mul_overflow(n, t.ne[i], &n)) return false;
+    }
+    if (t.type == kTypeF32) return !__builtin_mul_overflow(n, (uint64_t)4, &t.bytes);
     if (t.type == kTypeQ4K || t.type == kTypeQ6K) {
         if (t.ne[0] % 256) return false;
-        t.bytes = n / 256 * (t.type == kTypeQ4K ? kQ4kBytes : kQ6kBytes);
-        return true;
+        return !__builtin_mul_overflow(n / 256, (uint64_t)(t.type == kTypeQ4K ? kQ4kBytes : kQ6kBytes), &t.bytes);
     }
     t.bytes = 0; /* another type: described, never uploaded */
     return true;
@@ -200,7 +206,8 @@ bool open_gguf(const char *path, GgufFile &f) {
         for (uint32_t d = 0; d < ti.n_dims; ++d) ti.ne[d] = c.get<uint64_t>();
         ti.type = c.get<uint32_t>();
         ti.offset = c.get<uint64_t>();
-        if (!tensor_bytes(ti)) { snprintf(f.err, sizeof f.err, "tensor %s: bad Q4_K shape", ti.name.c_str()); return false; }
+        if (!c.ok) break;
+        if (!tensor_bytes(ti)) { snprintf(f.err, sizeof f.err, "tensor %s: bad shape", ti.name.c_str()); return false; }
         f.tensors.push_back(ti);
     }
     if (!c.ok) { snprintf(f.err, sizeof f.err, "%s: truncated key/value or tensor-info section", path); return false; }
@@ -208,7 +215,7 @@ bool open_gguf(const char *path, GgufFile &f) {
     const uint64_t head = (uint64_t)(c.p - base);
     const uint64_t data0 = (head + f.alignment - 1) / f.alignment * f.alignment;
     for (TensorInfo &t : f.tensors) {
-        if (data0 + t.offset + t.bytes > f.size) {
+        if (data0 > f.size || t.offset > f.size - data0 || t.bytes > f.size - data0 - t.offset) {
             snprintf(f.err, sizeof f.err, "tensor %s: data past the end of the file", t.name.c_str());
             return false;
         }

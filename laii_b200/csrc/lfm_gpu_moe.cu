@@ -867,19 +867,25 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_q4k_rows(lfm_gpu_moe_t *h, const void
     return LFM_GPU_OK;
 }
 
-LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
-                                                      size_t bytes) {
+LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_read_layer_range(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which,
+                                                            size_t offset, void *out, size_t bytes) {
     if (!h || !out || which > 5) return LFM_GPU_ERR_INVALID_ARG;
     if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
         return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
     const LayerSlot &S = h->layers[layer];
     if (!S.bufs[which]) return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u has no tensor %u", layer, which);
-    if (bytes == 0 || bytes > S.sizes[which])
-        return fail(h, LFM_GPU_ERR_INVALID_ARG, "tensor %u holds %zu bytes, asked for %zu", which, S.sizes[which], bytes);
+    if (bytes == 0 || offset > S.sizes[which] || bytes > S.sizes[which] - offset)
+        return fail(h, LFM_GPU_ERR_INVALID_ARG, "tensor %u holds %zu bytes, asked for [%zu, %zu+%zu)", which,
+                    S.sizes[which], offset, offset, bytes);
     DeviceGuard g(h->device);
     LFM_CUDA(h, cudaStreamSynchronize(h->stream));
-    LFM_CUDA(h, cudaMemcpy(out, S.bufs[which], bytes, cudaMemcpyDeviceToHost));
+    LFM_CUDA(h, cudaMemcpy(out, static_cast<const uint8_t *>(S.bufs[which]) + offset, bytes, cudaMemcpyDeviceToHost));
     return LFM_GPU_OK;
+}
+
+LFM_API lfm_gpu_status_t lfm_gpu_moe_debug_read_layer(lfm_gpu_moe_t *h, uint32_t layer, uint32_t which, void *out,
+                                                      size_t bytes) {
+    return lfm_gpu_moe_debug_read_layer_range(h, layer, which, 0, out, bytes);
 }
 
 LFM_API lfm_gpu_status_t lfm_gpu_moe_sync(lfm_gpu_moe_t *h) {
@@ -1020,6 +1026,12 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t 
     if (layer >= LFM_GPU_MOE_MAX_LAYERS || !h->layers[layer].present)
         return fail(h, LFM_GPU_ERR_NOT_READY, "layer %u not uploaded", layer);
     const MoeLayerDev &L = h->layers[layer].dev;
+    /* a shard holds only its experts' slabs while the router spans all E: routing
+     * it here would read expert weights past the end of the shard's allocation */
+    const uint32_t ep_count = h->layers[layer].ep_count;
+    if (ep_count && ep_count != L.E)
+        return fail(h, LFM_GPU_ERR_UNSUPPORTED,
+                    "forward_noalloc: layer %u holds an expert shard: use the lfm_gpu_moe_ep_* calls", layer);
     if (L.down_q6k)
         return fail(h, LFM_GPU_ERR_UNSUPPORTED, "forward_noalloc: layer %u has a Q6_K down tensor (Q4_K only)", layer);
     const size_t need = noalloc_layout(T, L, nullptr, nullptr, nullptr);
@@ -1045,7 +1057,7 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t 
     size_t counters_end = 0;
     noalloc_layout(T, L, base, &w, &counters_end);
     w.rt.err = h->dev_err;
-    w.rt.loads = h->loads;
+    w.rt.loads = nullptr; /* leaves the handle's statistics alone */
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int grid = h->sm_count;
     const uint32_t K = lfm_layer_K(L);

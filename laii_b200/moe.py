@@ -248,11 +248,14 @@ class GpuMoE:
 
     TENSORS = ("ffn_norm", "router_w", "exp_probs_b", "gate", "up", "down")
 
-    def read_layer(self, layer: int, which: str, nbytes: int) -> np.ndarray:
-        """Bytes of one device tensor of an uploaded layer (see TENSORS)."""
-        out = np.zeros(nbytes, np.uint8)
-        self._check(self._lib.lfm_gpu_moe_debug_read_layer(self._h, layer, self.TENSORS.index(which), _ptr(out),
-                                                           nbytes))
+    def read_layer(self, layer: int, which: str, nbytes: int, offset: int = 0, out: Optional[np.ndarray] = None
+                   ) -> np.ndarray:
+        """Bytes [offset, offset + nbytes) of one device tensor of an uploaded layer (see TENSORS),
+        into `out` (a contiguous uint8 buffer of nbytes) when given."""
+        if out is None:
+            out = np.zeros(nbytes, np.uint8)
+        self._check(self._lib.lfm_gpu_moe_debug_read_layer_range(self._h, layer, self.TENSORS.index(which), offset,
+                                                                 _ptr(out), nbytes))
         return out
 
     def profile(self, enable: bool = True):

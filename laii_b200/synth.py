@@ -46,9 +46,19 @@ def layer_seed(base: int, layer: int) -> int:
     return (base + layer * LAYER_STRIDE) & 0xFFFF_FFFF_FFFF_FFFF
 
 
+_gen = None  # a generator library chosen by use_generator_library()
+
+
+def use_generator_library(path: str) -> None:
+    """Generate with the build of csrc/lfm_synth.c at `path` instead of the package's own
+    liblfm_synth.so (the bench's CPU reference arm uses the oracle's build, so that it maps
+    no library of the GPU package).  Both builds compute the same bytes."""
+    global _gen
+    _gen = _native.bind_synth(ctypes.CDLL(path))
+
+
 def _lib():
-    lib = _native.load_synth()
-    return lib
+    return _gen if _gen is not None else _native.load_synth()
 
 
 def normal_f32(n: int, seed: int, first: int = 0, mean: float = 0.0, std: float = 1.0,

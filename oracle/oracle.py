@@ -18,6 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liblfm_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_moe.so")
+GEN_SO = os.path.join(HERE, "_build", "liblfm_gen.so")
 
 ORDER_VNNI = 0
 ORDER_AVX2 = 1

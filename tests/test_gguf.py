@@ -172,3 +172,34 @@ def test_upload_gguf_expert_shard_holds_the_slice(stack):
         assert g.upload_gguf(path, first_block=1, n_blocks=1, expert_first=3, n_local=2) == 1
         part = g.read_layer(0, "gate", 2 * per_gu)
         assert np.array_equal(part, m1.gate.reshape(-1)[3 * per_gu:5 * per_gu])
+
+
+def _raw_gguf(path, ne, offset=0, type_=12):
+    """A GGUF v3 file with one tensor "blk.0.attn_q.weight" of the given dims, type and data offset."""
+    import struct
+    name = b"blk.0.attn_q.weight"
+    b = b"GGUF" + struct.pack("<IQQ", 3, 1, 0)
+    b += struct.pack("<Q", len(name)) + name + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
+    b += struct.pack("<IQ", type_, offset)
+    b += bytes((-len(b)) % 32) + bytes(4096)
+    path.write_bytes(b)
+    return path
+
+
+def test_describe_refuses_shapes_and_offsets_that_wrap(tmp_path):
+    """Dims and offsets come from the file: a product or a sum that wraps 64 bits
+    must not pass the end-of-file check."""
+    cases = {
+        "wrap.gguf": ([(1 << 32) - 256, (1 << 32) - 1, (1 << 32) - 1], 0),   # Q4_K bytes wrap
+        "huge-dim.gguf": ([256, 1 << 40], 0),                                # a dim above 2^32
+        "zero-dim.gguf": ([256, 0], 0),
+        "offset.gguf": ([256, 1], (1 << 64) - 16),                           # data0 + offset wraps
+    }
+    for name, (ne, off) in cases.items():
+        p = _raw_gguf(tmp_path / name, ne, off)
+        with pytest.raises(MoEError) as ei:
+            gguf_describe(p, 0)
+        assert ei.value.status == -1, name
+    ok = _raw_gguf(tmp_path / "ok.gguf", [256, 16])   # 16 rows x 144 B fit in the 4 KiB of data
+    b, n = gguf_describe(ok, 0)
+    assert (b["kind"], n) == ("none", 1)

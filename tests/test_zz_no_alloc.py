@@ -79,3 +79,23 @@ def test_noalloc_rejects_scratch_above_its_limit():
         assert b"above its fixed" in lib.lfm_gpu_moe_last_error(g._h)
         assert _noalloc(lib, g._h, 5, xt, 1, 0) == -3   # layer not uploaded
         assert float(xt.abs().sum()) == 0.0             # nothing ran
+
+
+def test_noalloc_refuses_an_expert_shard():
+    """A shard layer keeps the full router but only its own experts' weights, so
+    routing it here would read past the shard: the call refuses it on the host."""
+    torch = pytest.importorskip("torch")
+    from laii_b200 import _native, synth
+    from laii_b200.moe import GpuMoE
+    lib = _native.load_gpu()
+    D, E, K, I, T = 512, 8, 2, 512, 4
+    L = synth.make_moe_layer(D, E, K, I, layer=0)
+    with GpuMoE(0) as g:
+        g.upload_layer_shard(3, L, 2, 4)
+        x0 = synth.make_hidden(T, D, seed_offset=79)
+        xt = torch.from_numpy(np.array(x0, copy=True)).cuda()
+        st = _noalloc(lib, g._h, 3, xt, T, 0)
+        assert st == -2
+        assert b"expert shard" in lib.lfm_gpu_moe_last_error(g._h)
+        torch.cuda.synchronize()
+        assert np.array_equal(xt.cpu().numpy(), x0)      # x untouched
