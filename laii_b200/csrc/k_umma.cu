@@ -40,6 +40,7 @@
  */
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "moe_device.cuh"
@@ -601,6 +602,402 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
     }
 }
 
+/* ---------------------------------------------------------------------------
+ * The same GEMM with the weight operand in tensor memory.
+ *
+ * Expander warps (one thread per weight row = TMEM lane) unpack each super-
+ * block straight from the raw Q4_K tile into TMEM with tcgen05.st:
+ * A1 = b_j * q4 and A2 = a_j * q4 (sc_j = 16 a_j + b_j), so acc = D1 + 16 D2
+ * over the super-block exactly as above, and the MMA reads A from TMEM
+ * (tcgen05.mma ... [a-tmem]).  Shared memory then carries only the raw
+ * weights (TMA), their one read by the expanders and the token operand: the
+ * nibble-to-byte operand never makes a shared-memory round trip.
+ *
+ * Input ring: slot s holds one super-block's A operand (TMEM columns
+ * 128 s .. 128 s + 127: per half h, A1 in 64 h + 0..31 and A2 in 64 h + 32..63,
+ * the half's K bytes 4c..4c+3 in column c, i.e. the element order of the
+ * token operand: 32-byte chunk 2h low nibbles, its high nibbles, chunk 2h+1
+ * low, high) and its token operand (both halves, one bulk copy).  The
+ * expanders and the token loader fill a slot together (one in_full
+ * barrier); one commit per MMA stream releases it (in_empty).  So per
+ * super-block each MMA thread waits twice, issues 8 MMAs back to back and
+ * commits twice.
+ *
+ * TMEM: the A slots (as many as the two accumulator buffers of 2*nt columns,
+ * D1 | D2, leave room for: 3 for nt <= 32, 2 for nt <= 64), then the
+ * accumulators.
+ * Warps: epilogue (4 for nt <= 32, else 16: four per TMEM lane quarter,
+ * splitting the tokens), 4 expanders, two MMA-issuing warps (one thread each:
+ * A1 -> D1 and A2 -> D2; the first also allocates TMEM), then one warp each
+ * for the weight TMA and the token loader.
+ * --------------------------------------------------------------------------- */
+template <bool kDec>
+struct TCfg {
+    static constexpr int kEpi = kDec ? 4 : 16;
+    static constexpr int kWarpExp = kEpi;            /* 4 expander warps: lane quarter = warp & 3 */
+    static constexpr int kWarpMma = kEpi + 4;        /* two MMA-issuing warps: A1 -> D1, A2 -> D2 */
+    static constexpr int kWarpTma = kWarpMma + 2;
+    static constexpr int kWarpLoad = kWarpMma + 3;
+    static constexpr int kThreads = (kWarpLoad + 1) * 32;
+    static constexpr int kSR = 6;                    /* raw weight ring (super-blocks)  */
+    static constexpr int kBBytes = 64 * 1024;        /* token operand slots             */
+    static constexpr int kRowInfo = kM * 16;         /* d, dmin, m0..3, m4..7 per row   */
+    static constexpr int kOffB = 0;
+    static constexpr int kOffR = kOffB + kBBytes;
+    static constexpr int kOffT = kOffR + kSR * kRawSlot;
+    static constexpr int kOffW = kOffT + kSI * kTokInfo;
+    static constexpr int kSmem = kOffW + kSI * kRowInfo;
+};
+static_assert(TCfg<false>::kSmem <= 227 * 1024 && TCfg<true>::kSmem <= 227 * 1024, "shared memory");
+constexpr uint32_t kTmSlot = 128;   /* TMEM columns of one A slot (a super-block: A1 | A2 per half) */
+constexpr uint32_t kNtTm = 64;      /* most tokens per block: two A slots + two 2*nt buffers = 512 columns */
+constexpr uint32_t kMaxSlots = 3;
+static_assert(2 * kTmSlot + 4 * kNtTm <= kTmemCols, "tensor memory");
+/* input ring slots for nt tokens a block: TMEM (A) and the shared-memory token slots (B) */
+__host__ __device__ constexpr uint32_t tm_slots(uint32_t nt) {
+    const uint32_t a = (kTmemCols - 4 * nt) / kTmSlot, b = (uint32_t)TCfg<true>::kBBytes / (2 * nt * kHalf);
+    const uint32_t n = a < b ? a : b;
+    return n < kMaxSlots ? n : kMaxSlots;
+}
+
+struct TmBars {
+    uint64_t in_full[kMaxSlots], in_empty[kMaxSlots], r_full[8], r_empty[8];
+    uint64_t t_full[2], t_empty[2], ti_full[kSI], ri_full[kSI], i_empty[kSI];
+    uint32_t tmem;
+    int abort;
+};
+
+__device__ __forceinline__ void umma_i8_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/* 8 consecutive 32-bit columns of this thread's TMEM lane. */
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+template <bool kDec, bool kEp>
+__global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid_constant__ CUtensorMap tmw0,
+                                                         const __grid_constant__ CUtensorMap tmw1, UmmaArgs A,
+                                                         const __grid_constant__ UmmaEpOut ep) {
+    using C = TCfg<kDec>;
+    extern __shared__ __align__(1024) uint8_t sm[];
+    __shared__ TmBars bars;
+    __shared__ UTile s_tile[kCtaTiles];
+    __shared__ UTokBlock s_blk[kCtaTiles];
+    __shared__ float *s_yh[LFM_EP_MAX_RANKS];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t nt = A.nt;
+    const uint32_t ns = tm_slots(nt);
+    if (kEp && tid < LFM_EP_MAX_RANKS) s_yh[tid] = ep.yhome[tid];
+    if (tid == 0) {
+        for (uint32_t i = 0; i < ns; ++i) {
+            lfm_mbar_init(&bars.in_full[i], 5); /* the 4 expander warps and the loader's expect_tx */
+            lfm_mbar_init(&bars.in_empty[i], 2); /* one commit per MMA stream */
+        }
+        for (int i = 0; i < 2; ++i) {
+            lfm_mbar_init(&bars.t_full[i], 2);
+            lfm_mbar_init(&bars.t_empty[i], C::kEpi);
+        }
+        for (int i = 0; i < C::kSR; ++i) {
+            lfm_mbar_init(&bars.r_full[i], 1);
+            lfm_mbar_init(&bars.r_empty[i], 4);
+        }
+        for (uint32_t i = 0; i < kSI; ++i) {
+            lfm_mbar_init(&bars.ti_full[i], 1);
+            lfm_mbar_init(&bars.ri_full[i], 4);
+            lfm_mbar_init(&bars.i_empty[i], C::kEpi);
+        }
+        bars.abort = 0;
+        lfm_fence_mbar_init();
+    }
+    if (warp == C::kWarpMma) {
+        tmem_alloc(&bars.tmem, kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    const int n_tiles = __ldcg(A.n_tiles);
+    const uint32_t my_tiles =
+        (int)blockIdx.x < n_tiles ? (uint32_t)(n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / gridDim.x : 0u;
+    for (uint32_t it = tid; it < my_tiles && it < kCtaTiles; it += blockDim.x) {
+        const UTile t = A.tiles[blockIdx.x + it * gridDim.x];
+        s_tile[it] = t;
+        s_blk[it] = A.tbs[t.tb];
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars.tmem;
+    volatile int *abort = &bars.abort;
+    const uint32_t nb = A.nb;
+    const uint32_t G = my_tiles * nb;
+    auto tile_at = [&](uint32_t it) -> UTile {
+        return it < kCtaTiles ? s_tile[it] : A.tiles[blockIdx.x + it * gridDim.x];
+    };
+    const uint32_t acc0 = ns * kTmSlot; /* first accumulator column */
+    const uint32_t opb = nt * kHalf;    /* one half super-block of the token operand */
+    uint8_t *sB = sm + C::kOffB, *sR = sm + C::kOffR, *sT = sm + C::kOffT, *sW = sm + C::kOffW;
+
+    if (warp < C::kEpi) {
+        /* ---------------- epilogue ---------------- */
+        constexpr int kCols = kDec ? (int)kNtDecode : (int)kNtTm / (C::kEpi / 4);
+        const int q4 = warp & 3, ch = warp >> 2;
+        const int r = 32 * q4 + lane;
+        const int half = (int)nt / (C::kEpi / 4);
+        const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t it = 0; it < my_tiles && ok; ++it) {
+            const UTile tile = tile_at(it);
+            const UTokBlock blk = it < kCtaTiles ? s_blk[it] : A.tbs[tile.tb];
+            const int nv = min(blk.ntok - ch * half, half);
+            float S[kCols];
+#pragma unroll
+            for (int i = 0; i < kCols; ++i) S[i] = 0.0f;
+            for (uint32_t sb = 0; sb < nb; ++sb, ++g) {
+                const uint32_t buf = g & 1u, ph = (g >> 1) & 1u;
+                ok = __all_sync(LFM_FULL_MASK, uwait(&bars.t_full[buf], ph, abort, A.err) &&
+                                                   uwait(&bars.ti_full[g % kSI], (g / kSI) & 1u, abort, A.err) &&
+                                                   uwait(&bars.ri_full[g % kSI], (g / kSI) & 1u, abort, A.err));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t is = g % kSI;
+                const uint4 ri = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * 16);
+                const uint64_t dd = pk2(__uint_as_float(ri.x), __uint_as_float(ri.x));
+                const uint64_t nm = pk2(-__uint_as_float(ri.y), -__uint_as_float(ri.y)); /* -dmin */
+                const float *d8s = reinterpret_cast<const float *>(sT + is * kTokInfo) + ch * half;
+                const uint4 *bps = reinterpret_cast<const uint4 *>(sT + is * kTokInfo + nt * 4) + ch * half;
+                constexpr int kStep = 8; /* columns per TMEM round trip */
+#pragma unroll
+                for (int c = 0; c < kCols / kStep; ++c) {
+                    if (kStep * c < nv) { /* warp-uniform */
+                        const uint32_t col = acc0 + buf * 2 * nt + (uint32_t)(ch * half) + (uint32_t)(kStep * c);
+                        uint32_t v1[8], v2[8];
+                        tmem_ld8(tl + col, v1);
+                        tmem_ld8(tl + col + nt, v2);
+                        tmem_wait(v1, v2);
+                        int acc[kStep];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc[i] = (int)v1[i] + 16 * (int)v2[i];
+#pragma unroll
+                        for (int i = 0; i < kStep; i += 2) {
+                            const int t = kStep * c + i;
+                            const float2 d8 = *reinterpret_cast<const float2 *>(d8s + t);
+                            const uint64_t d8p = pk2(d8.x, d8.y);
+                            const int m0 = mins_of(bps[t], ri.z, ri.w), m1 = mins_of(bps[t + 1], ri.z, ri.w);
+                            const uint64_t inner = fma2(mul2(d8p, nm), pk2((float)m0, (float)m1), pk2(S[t], S[t + 1]));
+                            const uint64_t out = fma2(mul2(d8p, dd), pk2((float)acc[i], (float)acc[i + 1]), inner);
+                            S[t] = __uint_as_float((uint32_t)out);
+                            S[t + 1] = __uint_as_float((uint32_t)(out >> 32));
+                        }
+                    }
+                }
+                /* the loads above completed (tcgen05.wait::ld): the buffer may be overwritten */
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    lfm_mbar_arrive(&bars.t_empty[buf]);
+                    lfm_mbar_arrive(&bars.i_empty[is]);
+                }
+            }
+            if (!ok) break;
+            if constexpr (kEp) {
+                const uint32_t *rt = ep.ret + blk.slot0 + ch * half;
+#pragma unroll
+                for (int t = 0; t < kCols; ++t)
+                    if (t < nv) {
+                        const uint32_t v = __ldg(rt + t), hr = v >> 24, a = v & 0xffffffu;
+                        if (hr < ep.world && a < ep.max_assign)
+                            s_yh[hr][(size_t)a * A.rows + tile.row0 + r] = S[t];
+                        else
+                            atomicOr(A.err, LFM_DEVERR_SEGMENT);
+                    }
+            } else {
+                float *yb = (tile.mat ? A.Y[1] : A.Y[0]) + (size_t)(blk.slot0 + ch * half) * A.rows + tile.row0 + r;
+#pragma unroll
+                for (int t = 0; t < kCols; ++t)
+                    if (t < nv) yb[(size_t)t * A.rows] = S[t];
+            }
+        }
+        if (!ok) *abort = 1;
+    } else if (warp < C::kWarpMma) {
+        /* ---------------- expanders: raw Q4_K rows -> A1 | A2 in TMEM ---------------- */
+        const int q4 = warp & 3;
+        const int p = 32 * q4 + lane;                     /* weight row of the tile = TMEM lane */
+        const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
+        bool ok = true;
+        uint32_t slot = 0, spar = 0, rs = 0, rpar = 0;
+        for (uint32_t g = 0; g < G && ok; ++g) {
+            ok = __all_sync(LFM_FULL_MASK, uwait(&bars.r_full[rs], rpar, abort, A.err));
+            if (!ok) break;
+            const uint8_t *raw = sR + rs * kRawSlot + p * kRaw;
+            const uint4 hdr = lfm_ld16<true>(raw);
+            const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+            const uint32_t scA = s0 & 0x3F3F3F3Fu;
+            const uint32_t scB = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+            const uint32_t mA = s1 & 0x3F3F3F3Fu;
+            const uint32_t mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+            ok = __all_sync(LFM_FULL_MASK, g < kSI || uwait(&bars.i_empty[g % kSI], ((g / kSI) & 1u) ^ 1u, abort, A.err));
+            if (!ok) break;
+            sts128(sW + (g % kSI) * C::kRowInfo + p * 16, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
+                   __float_as_uint(lfm_h2f((uint16_t)(hdr.x >> 16))), mA, mB);
+            __syncwarp();
+            if (lane == 0) lfm_mbar_arrive(&bars.ri_full[g % kSI]);
+            ok = __all_sync(LFM_FULL_MASK, g < ns || uwait(&bars.in_empty[slot], spar ^ 1u, abort, A.err));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t abase = tl + slot * kTmSlot;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t scw = h ? scB : scA; /* sub-blocks 4h..4h+3 */
+#pragma unroll
+                for (int cc = 0; cc < 2; ++cc) { /* 32-byte chunk 2h + cc: sub-blocks 4h+2cc (low), 4h+2cc+1 (high) */
+                    const uint32_t slo = (scw >> (16 * cc)) & 0xFFu, shi = (scw >> (16 * cc + 8)) & 0xFFu;
+                    const uint32_t bl = slo & 15u, al = slo >> 4, bh = shi & 15u, ah = shi >> 4;
+                    const uint4 w0 = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc));
+                    const uint4 w1 = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc) + 16);
+                    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    const uint32_t c0 = abase + 64 * h + 16 * cc;
+                    uint32_t v1[8], v2[8];
+                    /* bytes of a nibble word times a scalar <= 15 stay below 256: no carries */
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t lo = wv[i] & 0x0F0F0F0Fu;
+                        v1[i] = lo * bl;
+                        v2[i] = lo * al;
+                    }
+                    tmem_st8(c0, v1);
+                    tmem_st8(c0 + 32, v2);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t hi = (wv[i] >> 4) & 0x0F0F0F0Fu;
+                        v1[i] = hi * bh;
+                        v2[i] = hi * ah;
+                    }
+                    tmem_st8(c0 + 8, v1);
+                    tmem_st8(c0 + 40, v2);
+                }
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                lfm_mbar_arrive(&bars.in_full[slot]);
+                lfm_mbar_arrive(&bars.r_empty[rs]);
+            }
+            if (++slot == ns) { slot = 0; spar ^= 1u; }
+            if (++rs == (uint32_t)C::kSR) { rs = 0; rpar ^= 1u; }
+        }
+        if (!ok) *abort = 1;
+    } else if (warp < C::kWarpTma) {
+        /* ---------------- MMA issue: stream 0 A1 -> D1, stream 1 A2 -> D2 ----------------
+         * Ring positions advance by counters (no runtime division in these
+         * single-thread loops), and the operand descriptors are a base plus
+         * constant offsets. */
+        const uint32_t stream = (uint32_t)(warp - C::kWarpMma);
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t idesc = kIdescBase | ((nt >> 3) << 17), blbo = nt * 16u;
+            const uint64_t bdesc0 = udesc(lfm_smem_u32(sB), blbo);
+            const uint32_t dstep = (2 * blbo) >> 4;      /* one K step (32 bytes) in descriptor address units */
+            const uint32_t hstep = opb >> 4;             /* one half super-block                              */
+            const uint32_t aoff = tmem + stream * 32u;   /* A1 or A2 columns of a half                         */
+            uint32_t slot = 0, spar = 0, g = 0;
+            for (uint32_t it = 0; it < my_tiles && ok; ++it) {
+                for (uint32_t sbk = 0; sbk < nb; ++sbk, ++g) {
+                    const uint32_t buf = g & 1u;
+                    if ((g >= 2 && !uwait(&bars.t_empty[buf], ((g >> 1) & 1u) ^ 1u, abort, A.err)) ||
+                        !uwait(&bars.in_full[slot], spar, abort, A.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc0 + buf * 2 * nt + stream * nt;
+                    const uint64_t bd = bdesc0 + (uint64_t)(slot * 2 * hstep);
+                    const uint32_t a = aoff + slot * kTmSlot;
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                        for (uint32_t k = 0; k < 4; ++k)
+                            umma_i8_ta(d, a + 64 * h + 8 * k, bd + h * hstep + k * dstep, idesc, (h | k) ? 1u : 0u);
+                    umma_commit(&bars.in_empty[slot]);
+                    umma_commit(&bars.t_full[buf]);
+                    if (++slot == ns) { slot = 0; spar ^= 1u; }
+                }
+            }
+            if (!ok) *abort = 1;
+        }
+    } else if (warp == C::kWarpTma) {
+        /* ---------------- weight TMA: the tile's 128 rows x super-block ---------------- */
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t rs = 0, rpar = 0, g = 0;
+            for (uint32_t it = 0; it < my_tiles && ok; ++it) {
+                const UTile tile = tile_at(it);
+                const CUtensorMap *tm = tile.mat ? &tmw1 : &tmw0;
+                const uint32_t row = (uint32_t)tile.expert * A.rows + tile.row0;
+                for (uint32_t sbk = 0; sbk < nb; ++sbk, ++g) {
+                    if (g >= (uint32_t)C::kSR && !uwait(&bars.r_empty[rs], rpar ^ 1u, abort, A.err)) { ok = false; break; }
+                    lfm_mbar_arrive_tx(&bars.r_full[rs], kRawSlot);
+                    lfm_tma_load_2d(sR + rs * kRawSlot, tm, sbk * kRaw, row, &bars.r_full[rs]);
+                    if (++rs == (uint32_t)C::kSR) { rs = 0; rpar ^= 1u; }
+                }
+            }
+            if (!ok) *abort = 1;
+        }
+    } else {
+        /* ---------------- loader: the token operand (both halves, one copy) and scales ---------------- */
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t slot = 0, spar = 0, g = 0;
+            for (uint32_t it = 0; it < my_tiles && ok; ++it) {
+                const UTile tile = tile_at(it);
+                const uint8_t *src0 = A.xt + (size_t)tile.tb * nb * xt_sb_bytes(nt);
+                for (uint32_t sbk = 0; sbk < nb; ++sbk, ++g) {
+                    const uint8_t *src = src0 + (size_t)sbk * xt_sb_bytes(nt);
+                    const uint32_t is = g % kSI;
+                    if ((g >= kSI && !uwait(&bars.i_empty[is], ((g / kSI) & 1u) ^ 1u, abort, A.err)) ||
+                        (g >= ns && !uwait(&bars.in_empty[slot], spar ^ 1u, abort, A.err))) {
+                        ok = false;
+                        break;
+                    }
+                    lfm_mbar_arrive_tx(&bars.ti_full[is], nt * 20u);
+                    lfm_bulk_g2s_plain(sT + is * kTokInfo, src + 2 * opb, nt * 20u, &bars.ti_full[is]);
+                    lfm_mbar_arrive_tx(&bars.in_full[slot], 2 * opb);
+                    lfm_bulk_g2s_plain(sB + slot * 2 * opb, src, 2 * opb, &bars.in_full[slot]);
+                    if (++slot == ns) { slot = 0; spar ^= 1u; }
+                }
+            }
+            if (!ok) *abort = 1;
+        }
+    }
+
+    if (kEp) __threadfence_system();
+    tc_fence_before();
+    __syncthreads();
+    if (*abort) {
+        const uint64_t t0 = lfm_globaltimer();
+        while (lfm_globaltimer() - t0 < 2000000ull) {
+        }
+    }
+    if (warp == C::kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (kEp && tid == 0 && atomicAdd(ep.done, 1u) == gridDim.x - 1) {
+        atomicExch(ep.done, 0u);
+        __threadfence_system();
+        const uint32_t epoch = __ldcg(ep.step) + 1u;
+        for (uint32_t p = 0; p < ep.world; ++p) lfm_st_release_sys(ep.y_flag[p] + ep.rank, epoch);
+    }
+}
+
 /* Tokens of every block, per super-block, in the MMA's canonical K-major
  * layout: half h (K bytes 128h..128h+127) is 8 chunks of 16 K bytes x nt
  * tokens, token t's 16 bytes at chunk*16*nt + 16*t (= 8-token groups of 128
@@ -823,7 +1220,7 @@ uint32_t lfm_umma_nt(uint32_t slots, uint32_t experts) {
     /* about three times the mean tokens per expert, so most experts fit one block */
     const uint32_t mean = (slots + experts - 1) / (experts ? experts : 1u);
     const uint32_t nt = (3 * mean + 15) / 16 * 16;
-    return nt < 16 ? 16u : nt > (uint32_t)kN ? (uint32_t)kN : nt;
+    return nt < 16 ? 16u : nt > kNtTm ? kNtTm : nt;
 }
 size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts, uint32_t nt) { return (slots + nt - 1) / nt + experts; }
 size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint32_t nt) {
@@ -888,6 +1285,17 @@ cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, 
 }
 
 template <bool kDec, bool kEp>
+static cudaError_t launch_tm(const CUtensorMap &tm0, const CUtensorMap &tm1, const UmmaArgs &a, const UmmaEpOut &ep,
+                             int grid, cudaStream_t s) {
+    using C = TCfg<kDec>;
+    static size_t cache[16];
+    const cudaError_t e = lfm_smem_attr((const void *)k_q4k_tm<kDec, kEp>, C::kSmem, cache);
+    if (e != cudaSuccess) return e;
+    k_q4k_tm<kDec, kEp><<<grid, C::kThreads, C::kSmem, s>>>(tm0, tm1, a, ep);
+    return cudaGetLastError();
+}
+
+template <bool kDec, bool kEp>
 static cudaError_t launch_umma(const CUtensorMap &tm0, const CUtensorMap &tm1, const UmmaArgs &a,
                                const UmmaEpOut &ep, int grid, cudaStream_t s) {
     using C = UCfg<kDec>;
@@ -912,11 +1320,23 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
         !lfm_tmap_2d(&tm1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W1, row_bytes, (uint64_t)experts * rows, row_bytes, kRaw, kM))
         return cudaErrorInvalidValue;
     const bool dec = nt <= kNtDecode;
+    const UmmaEpOut eo = ep ? *ep : UmmaEpOut{};
+    static const bool smem_a = [] { /* the shared-memory A operand version, for A/B runs */
+        const char *v = getenv("LFM_GPU_MOE_UMMA_SMEM_A");
+        return v && v[0] == '1';
+    }();
+    if (!smem_a) {
+        if (nt > kNtTm || tm_slots(nt) < 2) return cudaErrorInvalidValue;
+        UmmaArgs a{W0, rows, cols / 256, xt, nt, tm_slots(nt), static_cast<const UTile *>(tiles),
+                   static_cast<const UTokBlock *>(tbs), n_tiles, {Y0, Y1}, err};
+        if (dec)
+            return ep ? launch_tm<true, true>(tm0, tm1, a, eo, grid, s) : launch_tm<true, false>(tm0, tm1, a, eo, grid, s);
+        return ep ? launch_tm<false, true>(tm0, tm1, a, eo, grid, s) : launch_tm<false, false>(tm0, tm1, a, eo, grid, s);
+    }
     uint32_t nsb = min((uint32_t)kMaxSB, (uint32_t)(dec ? UCfg<true>::kBBytes : UCfg<false>::kBBytes) / (nt * kHalf));
     if (dec) nsb &= ~1u; /* one B ring per half super-block */
     UmmaArgs a{W0, rows, cols / 256, xt, nt, nsb, static_cast<const UTile *>(tiles), static_cast<const UTokBlock *>(tbs),
                n_tiles, {Y0, Y1}, err};
-    const UmmaEpOut eo = ep ? *ep : UmmaEpOut{};
     if (dec)
         return ep ? launch_umma<true, true>(tm0, tm1, a, eo, grid, s) : launch_umma<true, false>(tm0, tm1, a, eo, grid, s);
     return ep ? launch_umma<false, true>(tm0, tm1, a, eo, grid, s) : launch_umma<false, false>(tm0, tm1, a, eo, grid, s);
