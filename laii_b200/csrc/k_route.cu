@@ -573,6 +573,146 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
         route_topk(L, tok0 + t, rt, rt.logits + (size_t)(tok0 + t) * E, true);
 }
 
+/*
+ * Decode-size route in one launch (16 < T <= kDecMaxT): CTA (g, p) takes tokens
+ * [8g, 8g + 8) and experts [8p, 8p + 8).  Its router rows and ffn_norm arrive
+ * by bulk copy before griddepcontrol.wait (they do not depend on the preceding
+ * kernel), the tokens' x after it.  Each CTA forms its tokens' RMSNorm in the
+ * reference's order (16 chains + tree) and xb = (x * inv) * ffn_norm in place;
+ * the p == 0 CTAs write Q8_K of xb; every CTA computes its 8 x 8 logits, each
+ * in the reference's 16-chain order (a half-warp per (token, expert): lane l
+ * runs chain l, then the 16-lane tree) and writes them to global memory.  The
+ * last CTA of a token group (arrival counter per group) takes those tokens'
+ * top-K; the last group to finish (counter rt.done) builds the dispatch
+ * tables and the tcgen05 tile plans.  Replaces k_norm_q8 + k_router_tiles +
+ * k_dispatch_wide at these sizes.
+ */
+constexpr uint32_t kDecMaxT = 128;
+constexpr uint32_t kDecTok = 8, kDecExp = 8;
+constexpr uint32_t kDecThreads = 256;
+
+__global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const float *__restrict__ x, uint32_t T,
+                                                           Q8Rows xq, RouteTables rt, EpPublish pub) {
+    extern __shared__ __align__(16) float dsm_dec[];
+    __shared__ uint64_t bar_w, bar_x;
+    __shared__ float s_inv[kDecTok];
+    __shared__ int s_last;
+    __shared__ RouteSmem s;
+    const uint32_t D = L.D, E = L.E;
+    const uint32_t tg = blockIdx.x, pg = blockIdx.y;
+    const uint32_t tok0 = tg * kDecTok, e0 = pg * kDecExp;
+    const uint32_t nt = min(kDecTok, T - tok0), ne = min(kDecExp, E - e0);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t ld = D + 16;                /* padded rows: the two half-warps of a warp read other banks */
+    float *ws = dsm_dec;                       /* [8][ld] router rows     */
+    float *xs = ws + (size_t)kDecExp * ld;     /* [8][ld] x, then xb      */
+    float *nw = xs + (size_t)kDecTok * ld;     /* [D]     ffn_norm        */
+    if (threadIdx.x == 0) {
+        lfm_mbar_init(&bar_w, 1);
+        lfm_mbar_init(&bar_x, 1);
+        lfm_fence_mbar_init();
+        const uint32_t wb = ne * D * 4 + (L.ffn_norm ? D * 4 : 0);
+        lfm_mbar_arrive_tx(&bar_w, wb);
+        for (uint32_t e = 0; e < ne; ++e) lfm_bulk_g2s_plain(ws + (size_t)e * ld, L.router_w + (size_t)(e0 + e) * D, D * 4, &bar_w);
+        if (L.ffn_norm) lfm_bulk_g2s_plain(nw, L.ffn_norm, D * 4, &bar_w);
+    }
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* x, and every table this kernel writes, belong to the preceding kernels */
+    if (threadIdx.x == 0) {
+        lfm_mbar_arrive_tx(&bar_x, nt * D * 4);
+        for (uint32_t t = 0; t < nt; ++t) lfm_bulk_g2s_plain(xs + (size_t)t * ld, x + (size_t)(tok0 + t) * D, D * 4, &bar_x);
+    }
+    __syncthreads();
+    bool ok = true;
+    if (threadIdx.x == 0) ok = lfm_mbar_wait(&bar_x, 0, rt.err) && lfm_mbar_wait(&bar_w, 0, rt.err);
+    if (threadIdx.x == 0) s_last = ok ? 1 : 0;
+    __syncthreads();
+    if (!s_last) return;
+    /* RMSNorm of token w (warp w): lanes 0-15 run the 16 chains, then the tree */
+    if ((uint32_t)warp < nt) {
+        const float *xr = xs + (size_t)warp * ld;
+        float acc = 0.0f;
+        if (lane < 16) {
+#pragma unroll 16
+            for (uint32_t i = 0; i < D; i += 16) {
+                const float v = xr[i + lane];
+                acc = __fmaf_rn(v, v, acc);
+            }
+        }
+        const float ss = lfm_hsum16_ref(acc);
+        if (lane == 0) {
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
+            s_inv[warp] = inv;
+            if (pg == 0) rt.rms[tok0 + warp] = inv;
+        }
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < nt * D; i += blockDim.x) {
+        const uint32_t t = i / D, c = i - t * D;
+        float *xp = xs + (size_t)t * ld + c;
+        const float n = __fmul_rn(*xp, s_inv[t]);
+        *xp = L.ffn_norm ? __fmul_rn(n, nw[c]) : n;
+    }
+    __syncthreads();
+    if (pg == 0) { /* Q8_K of xb: one warp per (token, 256-block) */
+        const uint32_t nb = D / 256;
+        for (uint32_t q = warp; q < nt * nb; q += blockDim.x / 32) {
+            const uint32_t t = q / nb, b = q - t * nb;
+            const float4 p0 = reinterpret_cast<const float4 *>(xs + (size_t)t * ld + 256 * b + 8 * lane)[0];
+            const float4 p1 = reinterpret_cast<const float4 *>(xs + (size_t)t * ld + 256 * b + 8 * lane)[1];
+            const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            lfm_quant_block_warp(v, xq, tok0 + t, b);
+        }
+    }
+    /* logits: half-warp h takes (token, expert) pairs h, h + 16, ...; lane l runs chain l */
+    {
+        const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+        constexpr int kPairs = kDecTok * kDecExp / (kDecThreads / 16); /* 4 pairs a half-warp */
+        float acc[kPairs];
+        const float *wr[kPairs], *xr[kPairs];
+#pragma unroll
+        for (int j = 0; j < kPairs; ++j) {
+            const uint32_t pr = (uint32_t)hw + 16u * j, t = pr / kDecExp, e = pr % kDecExp;
+            acc[j] = 0.0f;
+            wr[j] = ws + (size_t)min(e, ne - 1) * ld + l;
+            xr[j] = xs + (size_t)min(t, nt - 1) * ld + l;
+        }
+#pragma unroll 4
+        for (uint32_t i = 0; i < D; i += 16)
+#pragma unroll
+            for (int j = 0; j < kPairs; ++j) acc[j] = __fmaf_rn(wr[j][i], xr[j][i], acc[j]);
+#pragma unroll
+        for (int j = 0; j < kPairs; ++j) {
+            const float z = lfm_hsum16_ref(acc[j]);
+            const uint32_t pr = (uint32_t)hw + 16u * j, t = pr / kDecExp, e = pr % kDecExp;
+            if (l == 0 && t < nt && e < ne) rt.logits[(size_t)(tok0 + t) * E + e0 + e] = z;
+        }
+    }
+    /* the last expert-group CTA of this token group takes its tokens' top-K */
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(rt.tok_count + tg, 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) rt.tok_count[tg] = 0;
+    for (uint32_t t = warp; t < nt; t += blockDim.x / 32)
+        route_topk(L, tok0 + t, rt, rt.logits + (size_t)(tok0 + t) * E, true);
+    /* the last token group to finish builds the dispatch tables and tile plans */
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(rt.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) *rt.done = 0;
+    route_dispatch(L, T, rt, s);
+    if (pub.world) {
+        __syncthreads();
+        route_publish(pub, s);
+    }
+}
+
 __global__ void __launch_bounds__(1024) k_dispatch_wide(MoeLayerDev L, uint32_t T, RouteTables rt, EpPublish pub) {
     __shared__ RouteSmem s;
     route_dispatch(L, T, rt, s);
@@ -792,6 +932,30 @@ static cudaError_t launch_router_tiles(const MoeLayerDev &L, const float *x, uin
     return cudaGetLastError();
 }
 
+static size_t route_dec_smem(const MoeLayerDev &L, uint32_t T) {
+    if (L.dense || T <= kClusterMaxT || T > kDecMaxT || L.E > LFM_GPU_MAX_EXPERTS_DEV) return 0;
+    const size_t bytes = sizeof(float) * ((size_t)(kDecTok + kDecExp) * (L.D + 16) + L.D);
+    return bytes <= 200 * 1024 ? bytes : 0;
+}
+
+static cudaError_t launch_route_dec(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq, const RouteTables &rt,
+                                   cudaStream_t s, bool pdl, const EpPublish &pub, size_t smem) {
+    static size_t cache[16];
+    cudaError_t e = lfm_smem_attr((const void *)k_route_dec, smem, cache);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((T + kDecTok - 1) / kDecTok, (L.E + kDecExp - 1) / kDecExp);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_route_dec, L, x, T, xq, rt, pub);
+}
+
 /* T > 16: normalise + quantise, score (all experts per CTA), dispatch. */
 static cudaError_t launch_route_prefill(const MoeLayerDev &L, const float *x, uint32_t T, Q8Rows xq,
                                         const RouteTables &rt, cudaStream_t s, const EpPublish &pub) {
@@ -838,6 +1002,7 @@ uint32_t lfm_route_kernels(const MoeLayerDev &L, uint32_t T) {
     uint32_t epc = 0;
     if (T == 0) return 0;
     if (route_cluster_smem(L, T, &epc) > 0) return 1;
+    if (route_dec_smem(L, T) > 0) return 1;
     if (L.dense) return 2u;
     return T * L.K >= kSplitMin ? 4u : 3u; /* the wide dispatch splits in two at many assignments */
 }
@@ -870,5 +1035,7 @@ cudaError_t lfm_launch_route(const MoeLayerDev &L, const float *x, uint32_t T, Q
         cfg.numAttrs = 2;
         return cudaLaunchKernelEx(&cfg, k_route_cluster, L, x, T, epc, xq, rt, pub);
     }
+    const size_t dsmem = route_dec_smem(L, T);
+    if (dsmem > 0) return launch_route_dec(L, x, T, xq, rt, s, pdl, pub, dsmem);
     return launch_route_prefill(L, x, T, xq, rt, s, pub);
 }

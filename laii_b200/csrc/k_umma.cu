@@ -626,14 +626,22 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
  * TMEM: the A slots (as many as the two accumulator buffers of 2*nt columns,
  * D1 | D2, leave room for: 3 for nt <= 32, 2 for nt <= 64), then the
  * accumulators.
- * Warps: epilogue (4 for nt <= 32, else 16: four per TMEM lane quarter,
- * splitting the tokens), 4 expanders, two MMA-issuing warps (one thread each:
+ *
+ * Decode variant (kDec, token blocks of 16): A is the raw nibbles (64 TMEM
+ * columns a super-block, no scale multiply) and every 32-wide sub-block j gets
+ * its own accumulator D_j = q4 . q8 (8 x 16 columns a buffer), so a super-block
+ * takes 8 MMAs instead of 16; MMA stream s issues the four sub-blocks of half
+ * s, so the streams never share an accumulator.  The epilogue forms
+ * acc = sum_j sc_j * D_j exactly.  At a few tokens per expert the MMA count,
+ * not the arithmetic, sets the pace.
+ * Warps: epilogue (8 for the decode variant, else 16: two or four per TMEM
+ * lane quarter, splitting the tokens), 4 expanders, two MMA-issuing warps (one thread each:
  * A1 -> D1 and A2 -> D2; the first also allocates TMEM), then one warp each
  * for the weight TMA and the token loader.
  * --------------------------------------------------------------------------- */
 template <bool kDec>
 struct TCfg {
-    static constexpr int kEpi = kDec ? 4 : 16;
+    static constexpr int kEpi = kDec ? 8 : 16;       /* epilogue warps: 2 / 4 per TMEM lane quarter */
     static constexpr int kWarpExp = kEpi;            /* 4 expander warps: lane quarter = warp & 3 */
     static constexpr int kWarpMma = kEpi + 4;        /* two MMA-issuing warps: A1 -> D1, A2 -> D2 */
     static constexpr int kWarpTma = kWarpMma + 2;
@@ -641,7 +649,10 @@ struct TCfg {
     static constexpr int kThreads = (kWarpLoad + 1) * 32;
     static constexpr int kSR = 6;                    /* raw weight ring (super-blocks)  */
     static constexpr int kBBytes = 64 * 1024;        /* token operand slots             */
-    static constexpr int kRowInfo = kM * 16;         /* d, dmin, m0..3, m4..7 per row   */
+    static constexpr int kRowInfo = kM * (kDec ? 32 : 16); /* d, dmin, m0..3, m4..7 (, sc0..3, sc4..7) per row */
+    static constexpr uint32_t kSlotCols = kDec ? 64 : 128; /* TMEM columns of one A slot (a super-block)  */
+    static constexpr uint32_t kAccTok = kDec ? 8 : 2;      /* accumulator columns per token in a buffer   */
+    static constexpr uint32_t kMaxSlotsC = kDec ? 4 : 3;
     static constexpr int kOffB = 0;
     static constexpr int kOffR = kOffB + kBBytes;
     static constexpr int kOffT = kOffR + kSR * kRawSlot;
@@ -649,15 +660,17 @@ struct TCfg {
     static constexpr int kSmem = kOffW + kSI * kRowInfo;
 };
 static_assert(TCfg<false>::kSmem <= 227 * 1024 && TCfg<true>::kSmem <= 227 * 1024, "shared memory");
-constexpr uint32_t kTmSlot = 128;   /* TMEM columns of one A slot (a super-block: A1 | A2 per half) */
 constexpr uint32_t kNtTm = 64;      /* most tokens per block: two A slots + two 2*nt buffers = 512 columns */
-constexpr uint32_t kMaxSlots = 3;
-static_assert(2 * kTmSlot + 4 * kNtTm <= kTmemCols, "tensor memory");
+constexpr uint32_t kNtTmDec = 16;   /* token block of the decode variant: four A slots + two 8*16 buffers */
+constexpr uint32_t kMaxSlots = 4;
+static_assert(2 * 128 + 4 * kNtTm <= kTmemCols && 2 * 64 + 16 * kNtTmDec <= kTmemCols, "tensor memory");
 /* input ring slots for nt tokens a block: TMEM (A) and the shared-memory token slots (B) */
+template <bool kDec>
 __host__ __device__ constexpr uint32_t tm_slots(uint32_t nt) {
-    const uint32_t a = (kTmemCols - 4 * nt) / kTmSlot, b = (uint32_t)TCfg<true>::kBBytes / (2 * nt * kHalf);
+    using C = TCfg<kDec>;
+    const uint32_t a = (kTmemCols - 2 * C::kAccTok * nt) / C::kSlotCols, b = (uint32_t)C::kBBytes / (2 * nt * kHalf);
     const uint32_t n = a < b ? a : b;
-    return n < kMaxSlots ? n : kMaxSlots;
+    return n < C::kMaxSlotsC ? n : C::kMaxSlotsC;
 }
 
 struct TmBars {
@@ -694,7 +707,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
     __shared__ float *s_yh[LFM_EP_MAX_RANKS];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t nt = A.nt;
-    const uint32_t ns = tm_slots(nt);
+    const uint32_t ns = tm_slots<kDec>(nt);
     if (kEp && tid < LFM_EP_MAX_RANKS) s_yh[tid] = ep.yhome[tid];
     if (tid == 0) {
         for (uint32_t i = 0; i < ns; ++i) {
@@ -739,13 +752,14 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
     auto tile_at = [&](uint32_t it) -> UTile {
         return it < kCtaTiles ? s_tile[it] : A.tiles[blockIdx.x + it * gridDim.x];
     };
-    const uint32_t acc0 = ns * kTmSlot; /* first accumulator column */
+    const uint32_t acc0 = ns * C::kSlotCols;  /* first accumulator column         */
+    const uint32_t abuf = C::kAccTok * nt;     /* columns of one accumulator buffer */
     const uint32_t opb = nt * kHalf;    /* one half super-block of the token operand */
     uint8_t *sB = sm + C::kOffB, *sR = sm + C::kOffR, *sT = sm + C::kOffT, *sW = sm + C::kOffW;
 
     if (warp < C::kEpi) {
         /* ---------------- epilogue ---------------- */
-        constexpr int kCols = kDec ? (int)kNtDecode : (int)kNtTm / (C::kEpi / 4);
+        constexpr int kCols = (kDec ? (int)kNtTmDec : (int)kNtTm) / (C::kEpi / 4);
         const int q4 = warp & 3, ch = warp >> 2;
         const int r = 32 * q4 + lane;
         const int half = (int)nt / (C::kEpi / 4);
@@ -767,7 +781,13 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t is = g % kSI;
-                const uint4 ri = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * 16);
+                const uint4 ri = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * (kDec ? 32 : 16));
+                int sc[8];
+                if constexpr (kDec) {
+                    const uint4 r2 = *reinterpret_cast<const uint4 *>(sW + is * C::kRowInfo + r * 32 + 16);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) sc[j] = (int)(((j < 4 ? r2.x : r2.y) >> (8 * (j & 3))) & 0xFFu);
+                }
                 const uint64_t dd = pk2(__uint_as_float(ri.x), __uint_as_float(ri.x));
                 const uint64_t nm = pk2(-__uint_as_float(ri.y), -__uint_as_float(ri.y)); /* -dmin */
                 const float *d8s = reinterpret_cast<const float *>(sT + is * kTokInfo) + ch * half;
@@ -776,14 +796,31 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
 #pragma unroll
                 for (int c = 0; c < kCols / kStep; ++c) {
                     if (kStep * c < nv) { /* warp-uniform */
-                        const uint32_t col = acc0 + buf * 2 * nt + (uint32_t)(ch * half) + (uint32_t)(kStep * c);
-                        uint32_t v1[8], v2[8];
-                        tmem_ld8(tl + col, v1);
-                        tmem_ld8(tl + col + nt, v2);
-                        tmem_wait(v1, v2);
+                        const uint32_t col = acc0 + buf * abuf + (uint32_t)(ch * half) + (uint32_t)(kStep * c);
                         int acc[kStep];
+                        if constexpr (kDec) {
+                            /* acc = sum_j sc_j * D_j, D_j at column block j * nt */
+                            uint32_t v[8][8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) acc[i] = (int)v1[i] + 16 * (int)v2[i];
+                            for (int j = 0; j < 8; ++j) tmem_ld8(tl + col + (uint32_t)j * nt, v[j]);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) tmem_tie(v[j]);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                int a = 0;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) a += sc[j] * (int)v[j][i];
+                                acc[i] = a;
+                            }
+                        } else {
+                            uint32_t v1[8], v2[8];
+                            tmem_ld8(tl + col, v1);
+                            tmem_ld8(tl + col + nt, v2);
+                            tmem_wait(v1, v2);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) acc[i] = (int)v1[i] + 16 * (int)v2[i];
+                        }
 #pragma unroll
                         for (int i = 0; i < kStep; i += 2) {
                             const int t = kStep * c + i;
@@ -844,14 +881,33 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
             const uint32_t mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
             ok = __all_sync(LFM_FULL_MASK, g < kSI || uwait(&bars.i_empty[g % kSI], ((g / kSI) & 1u) ^ 1u, abort, A.err));
             if (!ok) break;
-            sts128(sW + (g % kSI) * C::kRowInfo + p * 16, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
+            uint8_t *rinfo = sW + (g % kSI) * C::kRowInfo + p * (kDec ? 32 : 16);
+            sts128(rinfo, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
                    __float_as_uint(lfm_h2f((uint16_t)(hdr.x >> 16))), mA, mB);
+            if (kDec) sts128(rinfo + 16, scA, scB, 0u, 0u);
             __syncwarp();
             if (lane == 0) lfm_mbar_arrive(&bars.ri_full[g % kSI]);
             ok = __all_sync(LFM_FULL_MASK, g < ns || uwait(&bars.in_empty[slot], spar ^ 1u, abort, A.err));
             if (!ok) break;
             tc_fence_after();
-            const uint32_t abase = tl + slot * kTmSlot;
+            const uint32_t abase = tl + slot * C::kSlotCols;
+            if constexpr (kDec) {
+                /* the nibbles themselves: chunk hc's low nibbles in columns 16hc.., high in 16hc+8.. */
+#pragma unroll
+                for (int hc = 0; hc < 4; ++hc) {
+                    const uint4 w0 = lfm_ld16<true>(raw + 16 + 32 * hc);
+                    const uint4 w1 = lfm_ld16<true>(raw + 16 + 32 * hc + 16);
+                    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    uint32_t v1[8], v2[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        v1[i] = wv[i] & 0x0F0F0F0Fu;
+                        v2[i] = (wv[i] >> 4) & 0x0F0F0F0Fu;
+                    }
+                    tmem_st8(abase + 16 * hc, v1);
+                    tmem_st8(abase + 16 * hc + 8, v2);
+                }
+            } else
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint32_t scw = h ? scB : scA; /* sub-blocks 4h..4h+3 */
@@ -917,14 +973,23 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem + acc0 + buf * 2 * nt + stream * nt;
                     const uint64_t bd = bdesc0 + (uint64_t)(slot * 2 * hstep);
-                    const uint32_t a = aoff + slot * kTmSlot;
+                    if constexpr (kDec) {
+                        /* half `stream`: sub-block 4 s + k into its own accumulator */
+                        const uint32_t d = tmem + acc0 + buf * abuf + 4 * stream * nt;
+                        const uint32_t a = tmem + slot * C::kSlotCols + 32 * stream;
+                        const uint64_t bh = bd + stream * hstep;
 #pragma unroll
-                    for (uint32_t h = 0; h < 2; ++h)
+                        for (uint32_t k = 0; k < 4; ++k) umma_i8_ta(d + k * nt, a + 8 * k, bh + k * dstep, idesc, 0u);
+                    } else {
+                        const uint32_t d = tmem + acc0 + buf * abuf + stream * nt;
+                        const uint32_t a = aoff + slot * C::kSlotCols;
 #pragma unroll
-                        for (uint32_t k = 0; k < 4; ++k)
-                            umma_i8_ta(d, a + 64 * h + 8 * k, bd + h * hstep + k * dstep, idesc, (h | k) ? 1u : 0u);
+                        for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                            for (uint32_t k = 0; k < 4; ++k)
+                                umma_i8_ta(d, a + 64 * h + 8 * k, bd + h * hstep + k * dstep, idesc, (h | k) ? 1u : 0u);
+                    }
                     umma_commit(&bars.in_empty[slot]);
                     umma_commit(&bars.t_full[buf]);
                     if (++slot == ns) { slot = 0; spar ^= 1u; }
@@ -1217,8 +1282,10 @@ __global__ void __launch_bounds__(256) k_swiglu_xt(const float *__restrict__ G, 
 
 bool lfm_umma_ok(uint32_t rows) { return rows % kM == 0; }
 uint32_t lfm_umma_nt(uint32_t slots, uint32_t experts) {
-    /* about three times the mean tokens per expert, so most experts fit one block */
+    /* about three times the mean tokens per expert, so most experts fit one block;
+     * at decode sizes (a mean of up to 8) blocks of 16 for the per-sub-block variant */
     const uint32_t mean = (slots + experts - 1) / (experts ? experts : 1u);
+    if (mean <= 8) return kNtTmDec;
     const uint32_t nt = (3 * mean + 15) / 16 * 16;
     return nt < 16 ? 16u : nt > kNtTm ? kNtTm : nt;
 }
@@ -1326,10 +1393,11 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
         return v && v[0] == '1';
     }();
     if (!smem_a) {
-        if (nt > kNtTm || tm_slots(nt) < 2) return cudaErrorInvalidValue;
-        UmmaArgs a{W0, rows, cols / 256, xt, nt, tm_slots(nt), static_cast<const UTile *>(tiles),
+        const bool tdec = nt <= kNtTmDec;
+        if (nt > kNtTm || (tdec ? tm_slots<true>(nt) : tm_slots<false>(nt)) < 2) return cudaErrorInvalidValue;
+        UmmaArgs a{W0, rows, cols / 256, xt, nt, 0u, static_cast<const UTile *>(tiles),
                    static_cast<const UTokBlock *>(tbs), n_tiles, {Y0, Y1}, err};
-        if (dec)
+        if (tdec)
             return ep ? launch_tm<true, true>(tm0, tm1, a, eo, grid, s) : launch_tm<true, false>(tm0, tm1, a, eo, grid, s);
         return ep ? launch_tm<false, true>(tm0, tm1, a, eo, grid, s) : launch_tm<false, false>(tm0, tm1, a, eo, grid, s);
     }
