@@ -735,6 +735,8 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
         tmem_relinquish();
         tc_fence_before();
     }
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* tile lists, token blocks and outputs belong to the preceding kernels */
     const int n_tiles = __ldcg(A.n_tiles);
     const uint32_t my_tiles =
         (int)blockIdx.x < n_tiles ? (uint32_t)(n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / gridDim.x : 0u;
@@ -1063,6 +1065,23 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
     }
 }
 
+/* Launch `fn` with the programmatic-dependent-launch attribute when pdl is set. */
+template <typename... Args>
+static cudaError_t launch_pdl(void (*fn)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
 /* Tokens of every block, per super-block, in the MMA's canonical K-major
  * layout: half h (K bytes 128h..128h+127) is 8 chunks of 16 K bytes x nt
  * tokens, token t's 16 bytes at chunk*16*nt + 16*t (= 8-token groups of 128
@@ -1119,6 +1138,8 @@ __device__ __forceinline__ void xt_copy_block(const XtRow *rows, int ntok, uint3
 __global__ void __launch_bounds__(kXtThreads) k_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const UTokBlock *tbs,
                                                    const int32_t *n_tb, uint32_t nb, uint32_t nt, uint8_t *xt) {
     __shared__ XtRow rows[kN];
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait();
     const int tb = blockIdx.x;
     if (tb >= __ldcg(n_tb)) return;
     const uint32_t sb = blockIdx.y;
@@ -1256,6 +1277,8 @@ __device__ __forceinline__ void quant_block_xt(const float v[8], uint8_t *dst, u
 __global__ void __launch_bounds__(256) k_swiglu_xt(const float *__restrict__ G, const float *__restrict__ U,
                                                    uint32_t cols, const UTokBlock *tbs, const int32_t *n_tb,
                                                    uint32_t nt, uint8_t *xt) {
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait();
     const int tb = blockIdx.x / (nt / 8);
     if (tb >= __ldcg(n_tb)) return;
     const uint32_t sb = blockIdx.y, nb = cols / 256;
@@ -1296,11 +1319,11 @@ size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint3
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt) { return max_tb * nb * (size_t)xt_sb_bytes(nt); }
 
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
-                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl) {
     const uint32_t nb = X.cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
-    k_xt_gather<<<dim3(max_tb, nb), kXtThreads, 0, s>>>(X, perm, K, static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
-    return cudaGetLastError();
+    return launch_pdl(k_xt_gather, dim3(max_tb, nb), dim3(kXtThreads), 0, s, pdl, X, perm, K,
+                      static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
 }
 
 cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
@@ -1344,22 +1367,21 @@ bool lfm_tmap_2d(CUtensorMap *tm, CUtensorMapDataType type, uint32_t elem_bytes,
 }
 
 cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
-                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl) {
     const uint32_t nb = cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
-    k_swiglu_xt<<<dim3(max_tb * (nt / 8), nb), 256, 0, s>>>(G, U, cols, static_cast<const UTokBlock *>(tbs), n_tb, nt, xt);
-    return cudaGetLastError();
+    return launch_pdl(k_swiglu_xt, dim3(max_tb * (nt / 8), nb), dim3(256), 0, s, pdl, G, U, cols,
+                      static_cast<const UTokBlock *>(tbs), n_tb, nt, xt);
 }
 
 template <bool kDec, bool kEp>
 static cudaError_t launch_tm(const CUtensorMap &tm0, const CUtensorMap &tm1, const UmmaArgs &a, const UmmaEpOut &ep,
-                             int grid, cudaStream_t s) {
+                             int grid, cudaStream_t s, bool pdl) {
     using C = TCfg<kDec>;
     static size_t cache[16];
     const cudaError_t e = lfm_smem_attr((const void *)k_q4k_tm<kDec, kEp>, C::kSmem, cache);
     if (e != cudaSuccess) return e;
-    k_q4k_tm<kDec, kEp><<<grid, C::kThreads, C::kSmem, s>>>(tm0, tm1, a, ep);
-    return cudaGetLastError();
+    return launch_pdl(k_q4k_tm<kDec, kEp>, dim3(grid), dim3(C::kThreads), C::kSmem, s, pdl, tm0, tm1, a, ep);
 }
 
 template <bool kDec, bool kEp>
@@ -1376,7 +1398,7 @@ static cudaError_t launch_umma(const CUtensorMap &tm0, const CUtensorMap &tm1, c
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
                                 const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
                                 const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s,
-                                const UmmaEpOut *ep) {
+                                const UmmaEpOut *ep, bool pdl) {
     if (rows % kM || cols % 256 || experts == 0 || nt % 16 || nt == 0 || nt > (uint32_t)kN)
         return cudaErrorInvalidValue;
     if (ep && (!ep->ret || !ep->done || !ep->step || ep->world == 0 || ep->world > LFM_EP_MAX_RANKS)) return cudaErrorInvalidValue;
@@ -1398,8 +1420,10 @@ cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t e
         UmmaArgs a{W0, rows, cols / 256, xt, nt, 0u, static_cast<const UTile *>(tiles),
                    static_cast<const UTokBlock *>(tbs), n_tiles, {Y0, Y1}, err};
         if (tdec)
-            return ep ? launch_tm<true, true>(tm0, tm1, a, eo, grid, s) : launch_tm<true, false>(tm0, tm1, a, eo, grid, s);
-        return ep ? launch_tm<false, true>(tm0, tm1, a, eo, grid, s) : launch_tm<false, false>(tm0, tm1, a, eo, grid, s);
+            return ep ? launch_tm<true, true>(tm0, tm1, a, eo, grid, s, pdl)
+                      : launch_tm<true, false>(tm0, tm1, a, eo, grid, s, pdl);
+        return ep ? launch_tm<false, true>(tm0, tm1, a, eo, grid, s, pdl)
+                  : launch_tm<false, false>(tm0, tm1, a, eo, grid, s, pdl);
     }
     uint32_t nsb = min((uint32_t)kMaxSB, (uint32_t)(dec ? UCfg<true>::kBBytes : UCfg<false>::kBBytes) / (nt * kHalf));
     if (dec) nsb &= ~1u; /* one B ring per half super-block */

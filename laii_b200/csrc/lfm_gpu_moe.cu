@@ -116,6 +116,7 @@ struct lfm_gpu_moe {
     bool use_fused = true;   /* fused decode layer for T <= LFM_FUSED_MAX_T */
     bool use_gemm = true;    /* tensor-core grouped GEMMs for prefill-sized T */
     bool use_umma = true;    /* ... on tcgen05 (k_umma.cu) where rows % 128 == 0, else mma.sync (k_gemm.cu) */
+    bool use_pdl = true;     /* chain the kernels with programmatic dependent launch */
     std::vector<GraphEntry> graphs;
     EpP2P ep;
 };
@@ -361,17 +362,23 @@ lfm_gpu_status_t run_experts(lfm_gpu_moe_t *h, const MoeLayerDev &L, float *x, u
     const bool prefill = h->use_gemm && T > LFM_FUSED_MAX_T && (uint64_t)T * K >= 32ull * lfm_layer_E(L);
     if (plan.nt) { /* the dispatch step built the tile plans */
         const uint32_t TK = T * K, E = lfm_layer_E(L), nt = plan.nt, mtb = plan.max_tb;
-        LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
+        /* chained with programmatic dependent launch: every kernel waits (griddepcontrol.wait) before it
+         * touches what its predecessor writes, so only launch latency and prologues overlap */
+        LFM_CUDA(h, timed(h, K_XT, s, [&] {
+            return lfm_launch_xt_gather(xq, w.rt.perm, K, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s, pdl);
+        }));
         LFM_CUDA(h, timed(h, K_GEMM_GU, s, [&] { /* gate and up in one launch */
             return lfm_launch_q4k_umma(L.gate, L.up, E, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
-                                       w.rt.err, grid, s);
+                                       w.rt.err, grid, s, nullptr, pdl);
         }));
-        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
+        LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] {
+            return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s, pdl);
+        }));
         LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
             return lfm_launch_q4k_umma(L.down, L.down, E, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y, w.y,
-                                       w.rt.err, grid, s);
+                                       w.rt.err, grid, s, nullptr, pdl);
         }));
-        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, false); }));
+        LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_combine(L, x, T, w.rt, w.y, s, pdl); }));
         return LFM_GPU_OK;
     }
     if (prefill) {
@@ -412,7 +419,7 @@ lfm_gpu_status_t forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x, u
     const MoeLayerDev &L = S.dev;
     Workspace &w = h->ws;  /* sized for the whole call by forward_common */
     Q8Rows xq = w.xq; xq.cols = L.D;
-    const bool pdl = !h->prof;
+    const bool pdl = !h->prof && h->use_pdl;
     const int grid = h->sm_count;
     if (h->use_fused && !L.down_q6k && lfm_fused_ok(L, T, grid)) {
         LFM_CUDA(h, timed(h, K_LAYER, s, [&] { return lfm_launch_layer_fused(L, x, T, w.rt, w.h, w.y, w.gbar, w.xrec, w.scores, grid, s); }));
@@ -453,6 +460,8 @@ LFM_API lfm_gpu_status_t lfm_gpu_moe_create(lfm_gpu_moe_t **out, int device_id) 
         h->use_gemm = !(ng && ng[0] && ng[0] != '0');
         const char *nu = getenv("LFM_GPU_MOE_NO_UMMA"); /* prefill GEMMs on mma.sync instead of tcgen05 (A/B runs) */
         h->use_umma = !(nu && nu[0] && nu[0] != '0');
+        const char *np = getenv("LFM_GPU_MOE_NO_PDL"); /* plain stream order between kernels (A/B runs) */
+        h->use_pdl = !(np && np[0] && np[0] != '0');
     }
     DeviceGuard g(device_id);
     if (cudaDeviceGetAttribute(&h->sm_count, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess ||

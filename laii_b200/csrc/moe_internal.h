@@ -253,13 +253,13 @@ size_t lfm_umma_tb_max(uint32_t slots, uint32_t experts, uint32_t nt);
 size_t lfm_umma_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts, uint32_t nt);
 size_t lfm_umma_xt_bytes(size_t max_tb, uint32_t nb, uint32_t nt);
 cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, const void *tbs, const int32_t *n_tb,
-                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl = false);
 /* the same from other ranks' Q8_K rows (expert parallelism, g.rowmap set); X.cols gives D */
 cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
                                     uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
 /* SwiGLU of the gate|up outputs, Q8_K, written as the down GEMM's token blocks */
 cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
-                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+                                 uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl = false);
 /* W0, W1: `experts` tensors [rows][cols/256] Q4_K back to back (tiles of
  * matrix m read Wm and write Ym; W1/Y1 may repeat W0/Y0 when every tile has m = 0).
  * ep (expert parallelism, down GEMM): store each row at its home rank instead of Y. */
@@ -267,7 +267,7 @@ struct UmmaEpOut;
 cudaError_t lfm_launch_q4k_umma(const uint8_t *W0, const uint8_t *W1, uint32_t experts, uint32_t rows, uint32_t cols,
                                 const uint8_t *xt, uint32_t nt, const void *tiles, const void *tbs,
                                 const int32_t *n_tiles, float *Y0, float *Y1, uint32_t *err, int grid, cudaStream_t s,
-                                const UmmaEpOut *ep = nullptr);
+                                const UmmaEpOut *ep = nullptr, bool pdl = false);
 
 /* k_synth.cu */
 /* blocks [first, first + n_blocks) of the tensor drawn from `seed` */
