@@ -287,10 +287,14 @@ lfm_gpu_status_t lfm_gpu_moe_forward_stack(lfm_gpu_moe_t *h, uint32_t first, uin
  * the library's static device memory; a (T, layer shape) whose scratch does not
  * fit is rejected with LFM_GPU_ERR_UNSUPPORTED before anything is launched
  * (the decode shape D=2048, E=32, K=4, I=1792 fits up to T=58 tokens).
- * The first call on a device looks the array up (cudaGetSymbolAddress); make
- * that first call before any stream capture.  Calls that can overlap on one
- * device -- on different streams, threads or handles -- race on the shared
- * scratch: serialise them.  Asynchronous; device-side errors are reported by
+ * The first call on a device looks the array up (cudaGetSymbolAddress) and
+ * keeps its address for the life of the process; make that first call before
+ * any stream capture, and do not call it again on a device whose primary
+ * context was reset (cudaDeviceReset) in between.  Calls that can overlap on
+ * one device -- on different streams, threads or handles -- race on the shared
+ * scratch: serialise them.  A layer that holds an expert shard (uploaded with
+ * the _shard calls) or a Q6_K down tensor is refused with
+ * LFM_GPU_ERR_UNSUPPORTED.  Asynchronous; device-side errors are reported by
  * the next lfm_gpu_moe_sync.  Does not touch the handle's statistics or
  * profiling records.  No counterpart in the reference. */
 lfm_gpu_status_t lfm_gpu_moe_forward_noalloc(lfm_gpu_moe_t *h, uint32_t layer, float *x, uint32_t T,
