@@ -11,9 +11,10 @@
  *   sigmoid, exp_probs_b-biased top-K (ties to the lowest index), normalised
  *     unbiased weights (tools/lfm2_moe_checkpoint.c:183-239);
  *   Q8_K of xb (tools/lfm2_decode_1x4.c:150-186).
- * Two implementations by size:
- *   T <= 16  k_route_cluster, one thread-block cluster (below);
- *   T > 16   k_norm_q8 + k_router_tiles + k_dispatch_wide.
+ * Three implementations by size:
+ *   T <= 16        k_route_cluster, one thread-block cluster (below);
+ *   16 < T <= 128  k_route_dec, one launch (4 tokens x 8 experts a CTA);
+ *   above          k_norm_q8 + k_router_tiles + the dispatch launches.
  * Dispatch tables (route_dispatch): per-expert histogram, exclusive scan,
  * slot permutation and its inverse, the active experts and their (expert,
  * 8-token chunk) work pairs.  Dense layers route every token to expert 0 with
@@ -41,28 +42,56 @@ struct RouteSmem {
     int uniq, bad;
 };
 
+/* Inclusive sum over the warp (every lane gets its own prefix). */
+__device__ __forceinline__ int warp_incl_scan(int v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(LFM_FULL_MASK, v, o);
+        if (lane >= o) v += u;
+    }
+    return v;
+}
+
+constexpr int kScanPer = LFM_GPU_MAX_EXPERTS_DEV / 32; /* experts (or active experts) per lane in warp 0's scans */
+
 /* The tcgen05 GEMMs' tile plans from the counts just formed (token blocks of
  * <= nt slots per active expert; tiles with the token blocks fastest, so the
- * CTAs that share a weight block run together and share it through L2). */
+ * CTAs that share a weight block run together and share it through L2).
+ * Warp 0 scans the token blocks of the active experts; the tiles are written
+ * by every warp. */
 __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
     const UmmaPlanOut &P = rt.plan;
     const int nt = (int)P.nt, nrg = (int)P.rows_gu / 128, nrd = (int)P.rows_dn / 128;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     __syncthreads();
     const int U = s.uniq;
-    if (threadIdx.x == 0) {
-        int a = 0;
-        for (int u = 0; u < U; ++u) {
-            s.tbb[u] = a;
-            a += (s.cnt[s.act[u]] + nt - 1) / nt;
+    if (warp == 0) { /* token blocks per active expert, scanned: lane l takes u = 8l .. 8l + 7 */
+        int nb[kScanPer], sum = 0;
+#pragma unroll
+        for (int i = 0; i < kScanPer; ++i) {
+            const int u = lane * kScanPer + i;
+            nb[i] = u < U ? (s.cnt[s.act[u]] + nt - 1) / nt : 0;
+            sum += nb[i];
         }
-        s.tbb[U] = a;
-        s.bad = (uint32_t)a > P.max_tb || (uint32_t)(2 * a * nrg) > P.max_gu || (uint32_t)(a * nrd) > P.max_dn;
-        if (s.bad) atomicOr(rt.err, LFM_DEVERR_SEGMENT);
-        P.counts[0] = s.bad ? 0 : 2 * a * nrg;
-        P.counts[1] = s.bad ? 0 : a;
-        P.counts[2] = s.bad ? 0 : a * nrd;
-        P.counts[3] = s.bad ? 0 : a;
+        const int incl = warp_incl_scan(sum);
+        int a = incl - sum;
+#pragma unroll
+        for (int i = 0; i < kScanPer; ++i) {
+            const int u = lane * kScanPer + i;
+            if (u < U) s.tbb[u] = a;
+            a += nb[i];
+        }
+        const int tot = __shfl_sync(LFM_FULL_MASK, incl, 31);
+        if (lane == 0) {
+            s.tbb[U] = tot;
+            s.bad = (uint32_t)tot > P.max_tb || (uint32_t)(2 * tot * nrg) > P.max_gu || (uint32_t)(tot * nrd) > P.max_dn;
+            if (s.bad) atomicOr(rt.err, LFM_DEVERR_SEGMENT);
+            P.counts[0] = s.bad ? 0 : 2 * tot * nrg;
+            P.counts[1] = s.bad ? 0 : tot;
+            P.counts[2] = s.bad ? 0 : tot * nrd;
+            P.counts[3] = s.bad ? 0 : tot;
+        }
     }
     __syncthreads();
     if (s.bad) return;
@@ -98,30 +127,50 @@ __device__ void route_publish(const EpPublish &pub, const RouteSmem &s) { route_
 
 /* The dispatch tables from the per-expert counts in s.cnt: offsets, active
  * experts, GEMV work pairs, summary and load statistics (s.off, s.act,
- * s.uniq set for the slot pass and the tile plans). */
+ * s.uniq set for the slot pass and the tile plans).  Warp 0 scans the counts,
+ * lane l over experts 8l .. 8l + 7, so active experts stay in id order. */
 __device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    if (threadIdx.x == 0) {
-        int acc = 0, uniq = 0, mx = 0, pairs = 0;
-        for (uint32_t e = 0; e < E; ++e) {
-            s.off[e] = acc;
-            acc += s.cnt[e];
-            mx = max(mx, s.cnt[e]);
-            if (s.cnt[e] > 0) {
-                s.act[uniq] = (int)e;
-                s.pb[uniq] = pairs;
-                pairs += (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
-                ++uniq;
+    if (warp == 0) {
+        int c[kScanPer], sum = 0, nact = 0, npair = 0, mx = 0;
+#pragma unroll
+        for (int i = 0; i < kScanPer; ++i) {
+            const uint32_t e = (uint32_t)(lane * kScanPer + i);
+            c[i] = e < E ? s.cnt[e] : 0;
+            sum += c[i];
+            nact += c[i] > 0 ? 1 : 0;
+            npair += (c[i] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
+            mx = max(mx, c[i]);
+        }
+        const int isum = warp_incl_scan(sum), iact = warp_incl_scan(nact), ipair = warp_incl_scan(npair);
+        int acc = isum - sum, uq = iact - nact, pr = ipair - npair;
+#pragma unroll
+        for (int i = 0; i < kScanPer; ++i) {
+            const uint32_t e = (uint32_t)(lane * kScanPer + i);
+            if (e < E) {
+                s.off[e] = acc;
+                if (c[i] > 0) {
+                    s.act[uq] = (int)e;
+                    s.pb[uq] = pr;
+                    ++uq;
+                    pr += (c[i] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
+                }
+                acc += c[i];
             }
         }
-        s.off[E] = acc;
-        s.uniq = uniq;
-        rt.summary[0] = uniq;
-        rt.summary[1] = mx;
-        rt.summary[2] = acc;
-        rt.summary[3] = pairs;
-        if (rt.loads && !L.dense) { rt.loads[0] += (unsigned long long)uniq; rt.loads[1] += 1ull; }
+        mx = __reduce_max_sync(LFM_FULL_MASK, mx);
+        const int tot = __shfl_sync(LFM_FULL_MASK, isum, 31), uniq = __shfl_sync(LFM_FULL_MASK, iact, 31),
+                  pairs = __shfl_sync(LFM_FULL_MASK, ipair, 31);
+        if (lane == 0) {
+            s.off[E] = tot;
+            s.uniq = uniq;
+            rt.summary[0] = uniq;
+            rt.summary[1] = mx;
+            rt.summary[2] = tot;
+            rt.summary[3] = pairs;
+            if (rt.loads && !L.dense) { rt.loads[0] += (unsigned long long)uniq; rt.loads[1] += 1ull; }
+        }
     }
     __syncthreads();
     for (uint32_t e = threadIdx.x; e <= E; e += blockDim.x) {
@@ -208,6 +257,17 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
     if (rt.plan.nt) route_plan(rt, s);
 }
 
+/* Order key of a biased score: a larger score gives a larger key and equal
+ * scores give equal keys (+0 and -0, and, as the flush-to-zero compare sees
+ * them, a denormal and 0); what the reference's strict > against -1e30 never
+ * selects (-1e30 and below, NaN) gives 0. */
+__device__ __forceinline__ uint32_t route_key(float v) {
+    if (!(v > -1e30f)) return 0u;
+    uint32_t b = __float_as_uint(v);
+    if ((b & 0x7f800000u) == 0u) b = 0u;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 /* Top-K of token t from its E logits (global memory written by other blocks,
  * read through L2; or this block's shared memory). */
 __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &rt, const float *logits_t,
@@ -226,44 +286,39 @@ __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &
             sel[i] = L.bias ? __fadd_rn(sig[i], L.bias[e]) : sig[i];
         }
     }
-    float wk[LFM_GPU_MAX_TOPK_DEV];
-    int ik[LFM_GPU_MAX_TOPK_DEV];
+    /* K rounds of argmax under the reference's rule (strict >, the lowest id
+     * among equals, nothing at or below -1e30): each lane's best of its own
+     * experts (ascending ids, strict >), then the warp's largest order key and
+     * the lowest id holding it, by two reductions.  Lane k keeps round k. */
+    int my_i = 0;
+    float my_w = 0.0f, s = 0.0f;
     for (uint32_t k = 0; k < K; ++k) {
-        float bv = -1e30f;
-        int bi = (int)E; /* sentinel: nothing beat -1e30 */
+        uint32_t bkey = 0u;
+        int bi = 0x7fffffff;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t e = lane + 32u * i;
-            if (e < E && sel[i] > bv) { bv = sel[i]; bi = (int)e; }
+            const uint32_t e = lane + 32u * i, key = e < E ? route_key(sel[i]) : 0u;
+            if (key > bkey) { bkey = key; bi = (int)e; }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(LFM_FULL_MASK, bv, o);
-            const int oi = __shfl_xor_sync(LFM_FULL_MASK, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (bi == (int)E) bi = 0; /* the reference keeps best_e = 0 */
-        ik[k] = bi;
+        const uint32_t mkey = __reduce_max_sync(LFM_FULL_MASK, bkey);
+        /* mkey == 0: nothing beat -1e30 and the reference keeps best_e = 0 */
+        const int win = mkey == 0u ? 0 : __reduce_min_sync(LFM_FULL_MASK, bkey == mkey ? bi : 0x7fffffff);
         float s_b = 0.0f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            if (lane + 32u * i == (uint32_t)bi) { s_b = sig[i]; sel[i] = -1e30f; }
+            if (lane + 32u * i == (uint32_t)win) { s_b = sig[i]; sel[i] = -1e30f; }
         }
-        wk[k] = __shfl_sync(LFM_FULL_MASK, s_b, bi & 31);
+        const float wk = __shfl_sync(LFM_FULL_MASK, s_b, win & 31);
+        s = __fadd_rn(s, wk); /* sum of the K weights in round order */
+        if ((uint32_t)lane == k) { my_i = win; my_w = wk; }
     }
-    if (L.norm_topk) {
-        float s = 0.0f;
-        for (uint32_t k = 0; k < K; ++k) s = __fadd_rn(s, wk[k]);
-        const float inv = __fdiv_rn(L.routed_scale, __fadd_rn(s, 1e-20f));
-        for (uint32_t k = 0; k < K; ++k) wk[k] = __fmul_rn(wk[k], inv);
-    } else if (L.routed_scale != 1.0f) {
-        for (uint32_t k = 0; k < K; ++k) wk[k] = __fmul_rn(wk[k], L.routed_scale);
-    }
-    if (lane == 0) {
-        for (uint32_t k = 0; k < K; ++k) {
-            rt.idx[(size_t)t * K + k] = ik[k];
-            rt.w[(size_t)t * K + k] = wk[k];
-        }
+    if (L.norm_topk)
+        my_w = __fmul_rn(my_w, __fdiv_rn(L.routed_scale, __fadd_rn(s, 1e-20f)));
+    else if (L.routed_scale != 1.0f)
+        my_w = __fmul_rn(my_w, L.routed_scale);
+    if ((uint32_t)lane < K) {
+        rt.idx[(size_t)t * K + lane] = my_i;
+        rt.w[(size_t)t * K + lane] = my_w;
     }
 }
 
@@ -575,27 +630,27 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
 
 /*
  * Decode-size route in one launch (16 < T <= kDecMaxT): CTA (g, p) takes tokens
- * [8g, 8g + 8) and experts [8p, 8p + 8).  Its router rows and ffn_norm arrive
+ * [4g, 4g + 4) and experts [8p, 8p + 8).  Its router rows and ffn_norm arrive
  * by bulk copy before griddepcontrol.wait (they do not depend on the preceding
- * kernel), the tokens' x after it.  Each CTA forms its tokens' RMSNorm in the
- * reference's order (16 chains + tree) and xb = (x * inv) * ffn_norm in place;
- * the p == 0 CTAs write Q8_K of xb; every CTA computes its 8 x 8 logits, each
- * in the reference's 16-chain order (a half-warp per (token, expert): lane l
- * runs chain l, then the 16-lane tree) and writes them to global memory.  The
- * last CTA of a token group (arrival counter per group) takes those tokens'
- * top-K; the last group to finish (counter rt.done) builds the dispatch
- * tables and the tcgen05 tile plans.  Replaces k_norm_q8 + k_router_tiles +
- * k_dispatch_wide at these sizes.
+ * kernel), the tokens' x after it.  Warp w takes token w: its RMSNorm in the
+ * reference's order (16 chains + tree), xb = (x * inv) * ffn_norm in place,
+ * then the Q8_K blocks b = p, p + P, ... of xb (the P CTAs of a token group
+ * share the token's blocks).  A half-warp then takes an expert and two tokens:
+ * lane l runs chain l of both logits, then the 16-lane tree, and the logits go
+ * to global memory.  The last CTA of a token group (arrival counter per group)
+ * takes those tokens' top-K; the last group to finish (counter rt.done) builds
+ * the dispatch tables and the tcgen05 tile plans.  Replaces k_norm_q8 +
+ * k_router_tiles + k_dispatch_wide at these sizes.
  */
 constexpr uint32_t kDecMaxT = 128;
-constexpr uint32_t kDecTok = 8, kDecExp = 8;
+constexpr uint32_t kDecTok = 4, kDecExp = 8;
 constexpr uint32_t kDecThreads = 256;
+static_assert(kDecTok <= kDecThreads / 32, "a warp per token");
 
 __global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const float *__restrict__ x, uint32_t T,
                                                            Q8Rows xq, RouteTables rt, EpPublish pub) {
     extern __shared__ __align__(16) float dsm_dec[];
     __shared__ uint64_t bar_w, bar_x;
-    __shared__ float s_inv[kDecTok];
     __shared__ int s_last;
     __shared__ RouteSmem s;
     const uint32_t D = L.D, E = L.E;
@@ -605,7 +660,7 @@ __global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t ld = D + 16;                /* padded rows: the two half-warps of a warp read other banks */
     float *ws = dsm_dec;                       /* [8][ld] router rows     */
-    float *xs = ws + (size_t)kDecExp * ld;     /* [8][ld] x, then xb      */
+    float *xs = ws + (size_t)kDecExp * ld;     /* [4][ld] x, then xb      */
     float *nw = xs + (size_t)kDecTok * ld;     /* [D]     ffn_norm        */
     if (threadIdx.x == 0) {
         lfm_mbar_init(&bar_w, 1);
@@ -628,9 +683,9 @@ __global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const 
     if (threadIdx.x == 0) s_last = ok ? 1 : 0;
     __syncthreads();
     if (!s_last) return;
-    /* RMSNorm of token w (warp w): lanes 0-15 run the 16 chains, then the tree */
     if ((uint32_t)warp < nt) {
-        const float *xr = xs + (size_t)warp * ld;
+        /* token w: RMSNorm (lanes 0-15 run the 16 chains, then the tree) */
+        float *xr = xs + (size_t)warp * ld;
         float acc = 0.0f;
         if (lane < 16) {
 #pragma unroll 16
@@ -639,53 +694,54 @@ __global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const 
                 acc = __fmaf_rn(v, v, acc);
             }
         }
-        const float ss = lfm_hsum16_ref(acc);
-        if (lane == 0) {
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
-            s_inv[warp] = inv;
-            if (pg == 0) rt.rms[tok0 + warp] = inv;
+        const float ss = __shfl_sync(LFM_FULL_MASK, lfm_hsum16_ref(acc), 0);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), L.eps)));
+        if (pg == 0 && lane == 0) rt.rms[tok0 + warp] = inv;
+        /* xb = (x * inv) * ffn_norm in place, four columns a lane */
+        for (uint32_t c = 4 * lane; c < D; c += 128) {
+            float4 v = *reinterpret_cast<const float4 *>(xr + c);
+            v.x = __fmul_rn(v.x, inv);
+            v.y = __fmul_rn(v.y, inv);
+            v.z = __fmul_rn(v.z, inv);
+            v.w = __fmul_rn(v.w, inv);
+            if (L.ffn_norm) {
+                const float4 n = *reinterpret_cast<const float4 *>(nw + c);
+                v.x = __fmul_rn(v.x, n.x);
+                v.y = __fmul_rn(v.y, n.y);
+                v.z = __fmul_rn(v.z, n.z);
+                v.w = __fmul_rn(v.w, n.w);
+            }
+            *reinterpret_cast<float4 *>(xr + c) = v;
         }
-    }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < nt * D; i += blockDim.x) {
-        const uint32_t t = i / D, c = i - t * D;
-        float *xp = xs + (size_t)t * ld + c;
-        const float n = __fmul_rn(*xp, s_inv[t]);
-        *xp = L.ffn_norm ? __fmul_rn(n, nw[c]) : n;
-    }
-    __syncthreads();
-    if (pg == 0) { /* Q8_K of xb: one warp per (token, 256-block) */
-        const uint32_t nb = D / 256;
-        for (uint32_t q = warp; q < nt * nb; q += blockDim.x / 32) {
-            const uint32_t t = q / nb, b = q - t * nb;
-            const float4 p0 = reinterpret_cast<const float4 *>(xs + (size_t)t * ld + 256 * b + 8 * lane)[0];
-            const float4 p1 = reinterpret_cast<const float4 *>(xs + (size_t)t * ld + 256 * b + 8 * lane)[1];
+        __syncwarp();
+        /* this CTA's share of the token's Q8_K blocks */
+        for (uint32_t b = pg; b < D / 256; b += gridDim.y) {
+            const float4 p0 = reinterpret_cast<const float4 *>(xr + 256 * b + 8 * lane)[0];
+            const float4 p1 = reinterpret_cast<const float4 *>(xr + 256 * b + 8 * lane)[1];
             const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-            lfm_quant_block_warp(v, xq, tok0 + t, b);
+            lfm_quant_block_warp(v, xq, tok0 + warp, b);
         }
     }
-    /* logits: half-warp h takes (token, expert) pairs h, h + 16, ...; lane l runs chain l */
+    __syncthreads();
+    /* logits: half-warp h takes expert h % 8 and tokens h / 8, h / 8 + 2; lane l runs chain l of both */
     {
         const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
-        constexpr int kPairs = kDecTok * kDecExp / (kDecThreads / 16); /* 4 pairs a half-warp */
-        float acc[kPairs];
-        const float *wr[kPairs], *xr[kPairs];
-#pragma unroll
-        for (int j = 0; j < kPairs; ++j) {
-            const uint32_t pr = (uint32_t)hw + 16u * j, t = pr / kDecExp, e = pr % kDecExp;
-            acc[j] = 0.0f;
-            wr[j] = ws + (size_t)min(e, ne - 1) * ld + l;
-            xr[j] = xs + (size_t)min(t, nt - 1) * ld + l;
+        constexpr int kPairs = kDecTok * kDecExp / (kDecThreads / 16);
+        static_assert(kPairs == 2, "two tokens a half-warp");
+        const uint32_t e = (uint32_t)hw % kDecExp, t0 = (uint32_t)hw / kDecExp, t1 = t0 + 2;
+        const float *wr = ws + (size_t)min(e, ne - 1) * ld + l;
+        const float *x0 = xs + (size_t)min(t0, nt - 1) * ld + l, *x1 = xs + (size_t)min(t1, nt - 1) * ld + l;
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 8
+        for (uint32_t i = 0; i < D; i += 16) {
+            const float w = wr[i];
+            a0 = __fmaf_rn(w, x0[i], a0);
+            a1 = __fmaf_rn(w, x1[i], a1);
         }
-#pragma unroll 4
-        for (uint32_t i = 0; i < D; i += 16)
-#pragma unroll
-            for (int j = 0; j < kPairs; ++j) acc[j] = __fmaf_rn(wr[j][i], xr[j][i], acc[j]);
-#pragma unroll
-        for (int j = 0; j < kPairs; ++j) {
-            const float z = lfm_hsum16_ref(acc[j]);
-            const uint32_t pr = (uint32_t)hw + 16u * j, t = pr / kDecExp, e = pr % kDecExp;
-            if (l == 0 && t < nt && e < ne) rt.logits[(size_t)(tok0 + t) * E + e0 + e] = z;
+        const float z0 = lfm_hsum16_ref(a0), z1 = lfm_hsum16_ref(a1);
+        if (l == 0 && e < ne) {
+            if (t0 < nt) rt.logits[(size_t)(tok0 + t0) * E + e0 + e] = z0;
+            if (t1 < nt) rt.logits[(size_t)(tok0 + t1) * E + e0 + e] = z1;
         }
     }
     /* the last expert-group CTA of this token group takes its tokens' top-K */
@@ -696,8 +752,7 @@ __global__ void __launch_bounds__(kDecThreads) k_route_dec(MoeLayerDev L, const 
     if (!s_last) return;
     __threadfence();
     if (threadIdx.x == 0) rt.tok_count[tg] = 0;
-    for (uint32_t t = warp; t < nt; t += blockDim.x / 32)
-        route_topk(L, tok0 + t, rt, rt.logits + (size_t)(tok0 + t) * E, true);
+    if ((uint32_t)warp < nt) route_topk(L, tok0 + warp, rt, rt.logits + (size_t)(tok0 + warp) * E, true);
     /* the last token group to finish builds the dispatch tables and tile plans */
     __threadfence();
     __syncthreads();
