@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
                 A.rt.summary[1] = mx;
                 A.rt.summary[2] = cex;
                 A.rt.summary[3] = pex;
-                if (A.rt.loads && !L.dense) { A.rt.loads[0] += (unsigned long long)uq; A.rt.loads[1] += 1ull; }
+                if (A.rt.loads && !L.dense) { atomicAdd(A.rt.loads, (unsigned long long)uq); atomicAdd(A.rt.loads + 1, 1ull); }
             }
         }
         __syncwarp();

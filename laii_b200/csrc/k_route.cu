@@ -40,6 +40,8 @@ struct RouteSmem {
     int pb[LFM_GPU_MAX_EXPERTS_DEV];  /* first work pair of each active expert */
     int tbb[LFM_GPU_MAX_EXPERTS_DEV + 1]; /* first token block of each active expert (tcgen05 plan) */
     int uniq, bad;
+    int wsum[32][4]; /* block scans: per-warp sums, then their exclusive prefixes */
+    int tot[4];      /* block scans: totals */
 };
 
 /* Inclusive sum over the warp (every lane gets its own prefix). */
@@ -53,37 +55,60 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
     return v;
 }
 
-constexpr int kScanPer = LFM_GPU_MAX_EXPERTS_DEV / 32; /* experts (or active experts) per lane in warp 0's scans */
+/* Exclusive scans over the block of three per-thread counts (thread order),
+ * and the block's largest v[3]; every thread of the block calls it.  Totals in
+ * s.tot[0..2], the maximum in s.tot[3]. */
+__device__ __forceinline__ void block_scan3(const int (&v)[4], int (&ex)[3], RouteSmem &s) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (int)(blockDim.x >> 5);
+    int in[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) in[j] = warp_incl_scan(v[j]);
+    const int mx = __reduce_max_sync(LFM_FULL_MASK, v[3]);
+    if (lane == 31) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) s.wsum[warp][j] = in[j];
+        s.wsum[warp][3] = mx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = lane < nw ? s.wsum[lane][j] : 0;
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const int iw = warp_incl_scan(w[j]);
+            if (lane < nw) s.wsum[lane][j] = iw - w[j];
+            if (lane == 31) s.tot[j] = iw;
+        }
+        const int m = __reduce_max_sync(LFM_FULL_MASK, w[3]);
+        if (lane == 0) s.tot[3] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 3; ++j) ex[j] = s.wsum[warp][j] + in[j] - v[j];
+}
 
 /* The tcgen05 GEMMs' tile plans from the counts just formed (token blocks of
  * <= nt slots per active expert; tiles with the token blocks fastest, so the
  * CTAs that share a weight block run together and share it through L2).
- * Warp 0 scans the token blocks of the active experts; the tiles are written
- * by every warp. */
+ * Thread u scans the token blocks of active expert u (blockDim.x >= E); warp w
+ * then writes the tiles of experts w, w + 8, ..., lane l those of row block l,
+ * with no division while an expert has at most kPlanDirect token blocks. */
+constexpr int kPlanDirect = 8;
 __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
     const UmmaPlanOut &P = rt.plan;
     const int nt = (int)P.nt, nrg = (int)P.rows_gu / 128, nrd = (int)P.rows_dn / 128;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     __syncthreads();
     const int U = s.uniq;
-    if (warp == 0) { /* token blocks per active expert, scanned: lane l takes u = 8l .. 8l + 7 */
-        int nb[kScanPer], sum = 0;
-#pragma unroll
-        for (int i = 0; i < kScanPer; ++i) {
-            const int u = lane * kScanPer + i;
-            nb[i] = u < U ? (s.cnt[s.act[u]] + nt - 1) / nt : 0;
-            sum += nb[i];
-        }
-        const int incl = warp_incl_scan(sum);
-        int a = incl - sum;
-#pragma unroll
-        for (int i = 0; i < kScanPer; ++i) {
-            const int u = lane * kScanPer + i;
-            if (u < U) s.tbb[u] = a;
-            a += nb[i];
-        }
-        const int tot = __shfl_sync(LFM_FULL_MASK, incl, 31);
-        if (lane == 0) {
+    {
+        const int u = (int)threadIdx.x;
+        const int v[4] = {u < U ? (s.cnt[s.act[u]] + nt - 1) / nt : 0, 0, 0, 0};
+        int ex[3];
+        block_scan3(v, ex, s);
+        if (u < U) s.tbb[u] = ex[0];
+        if (threadIdx.x == 0) {
+            const int tot = s.tot[0];
             s.tbb[U] = tot;
             s.bad = (uint32_t)tot > P.max_tb || (uint32_t)(2 * tot * nrg) > P.max_gu || (uint32_t)(tot * nrd) > P.max_dn;
             if (s.bad) atomicOr(rt.err, LFM_DEVERR_SEGMENT);
@@ -98,13 +123,25 @@ __device__ void route_plan(const RouteTables &rt, RouteSmem &s) {
     for (int u = warp; u < U; u += nwarps) {
         const int e = s.act[u], cnt = s.cnt[e], off = s.off[e], t0 = s.tbb[u], n = s.tbb[u + 1] - t0;
         for (int i = lane; i < n; i += 32) P.tbs[t0 + i] = LfmUTokBlock{off + i * nt, min(nt, cnt - i * nt)};
-        for (int q = lane; q < 2 * n * nrg; q += 32) { /* gate and up tiles of a block side by side */
-            const int m = q & 1, rb = (q >> 1) / n, i = (q >> 1) - rb * n;
-            P.tiles_gu[2 * t0 * nrg + q] = LfmUTile{e, t0 + i, rb * 128, m};
-        }
-        for (int q = lane; q < n * nrd; q += 32) {
-            const int rb = q / n, i = q - rb * n;
-            P.tiles_dn[t0 * nrd + q] = LfmUTile{e, t0 + i, rb * 128, 0};
+        LfmUTile *gu = P.tiles_gu + 2 * t0 * nrg, *dn = P.tiles_dn + t0 * nrd;
+        if (n <= kPlanDirect) {
+            /* gate and up tiles of a block side by side: index 2 (rb n + i) + m */
+            for (int rb = lane; rb < nrg; rb += 32)
+                for (int i = 0; i < n; ++i) {
+                    gu[2 * (rb * n + i)] = LfmUTile{e, t0 + i, rb * 128, 0};
+                    gu[2 * (rb * n + i) + 1] = LfmUTile{e, t0 + i, rb * 128, 1};
+                }
+            for (int rb = lane; rb < nrd; rb += 32)
+                for (int i = 0; i < n; ++i) dn[rb * n + i] = LfmUTile{e, t0 + i, rb * 128, 0};
+        } else {
+            for (int q = lane; q < 2 * n * nrg; q += 32) {
+                const int m = q & 1, rb = (q >> 1) / n, i = (q >> 1) - rb * n;
+                gu[q] = LfmUTile{e, t0 + i, rb * 128, m};
+            }
+            for (int q = lane; q < n * nrd; q += 32) {
+                const int rb = q / n, i = q - rb * n;
+                dn[q] = LfmUTile{e, t0 + i, rb * 128, 0};
+            }
         }
     }
 }
@@ -127,60 +164,46 @@ __device__ void route_publish(const EpPublish &pub, const RouteSmem &s) { route_
 
 /* The dispatch tables from the per-expert counts in s.cnt: offsets, active
  * experts, GEMV work pairs, summary and load statistics (s.off, s.act,
- * s.uniq set for the slot pass and the tile plans).  Warp 0 scans the counts,
- * lane l over experts 8l .. 8l + 7, so active experts stay in id order. */
+ * s.uniq set for the slot pass and the tile plans).  Thread e takes expert e
+ * (blockDim.x >= E) in one block-wide scan, so active experts stay in id order. */
 __device__ void route_tables(const MoeLayerDev &L, const RouteTables &rt, RouteSmem &s) {
     const uint32_t E = L.dense ? 1u : L.E;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    if (warp == 0) {
-        int c[kScanPer], sum = 0, nact = 0, npair = 0, mx = 0;
-#pragma unroll
-        for (int i = 0; i < kScanPer; ++i) {
-            const uint32_t e = (uint32_t)(lane * kScanPer + i);
-            c[i] = e < E ? s.cnt[e] : 0;
-            sum += c[i];
-            nact += c[i] > 0 ? 1 : 0;
-            npair += (c[i] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
-            mx = max(mx, c[i]);
-        }
-        const int isum = warp_incl_scan(sum), iact = warp_incl_scan(nact), ipair = warp_incl_scan(npair);
-        int acc = isum - sum, uq = iact - nact, pr = ipair - npair;
-#pragma unroll
-        for (int i = 0; i < kScanPer; ++i) {
-            const uint32_t e = (uint32_t)(lane * kScanPer + i);
-            if (e < E) {
-                s.off[e] = acc;
-                if (c[i] > 0) {
-                    s.act[uq] = (int)e;
-                    s.pb[uq] = pr;
-                    ++uq;
-                    pr += (c[i] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
-                }
-                acc += c[i];
+    {
+        const uint32_t e = threadIdx.x;
+        const int c = e < E ? s.cnt[e] : 0;
+        const int v[4] = {c, c > 0 ? 1 : 0, (c + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK, c};
+        int ex[3];
+        block_scan3(v, ex, s);
+        if (e < E) {
+            s.off[e] = ex[0];
+            rt.offsets[e] = ex[0];
+            rt.counts[e] = c;
+            if (c > 0) {
+                s.act[ex[1]] = (int)e;
+                s.pb[ex[1]] = ex[2];
+                rt.act[ex[1]] = (int)e;
             }
         }
-        mx = __reduce_max_sync(LFM_FULL_MASK, mx);
-        const int tot = __shfl_sync(LFM_FULL_MASK, isum, 31), uniq = __shfl_sync(LFM_FULL_MASK, iact, 31),
-                  pairs = __shfl_sync(LFM_FULL_MASK, ipair, 31);
-        if (lane == 0) {
+        if (threadIdx.x == 0) {
+            const int tot = s.tot[0], uniq = s.tot[1];
             s.off[E] = tot;
+            rt.offsets[E] = tot;
             s.uniq = uniq;
             rt.summary[0] = uniq;
-            rt.summary[1] = mx;
+            rt.summary[1] = s.tot[3];
             rt.summary[2] = tot;
-            rt.summary[3] = pairs;
-            if (rt.loads && !L.dense) { rt.loads[0] += (unsigned long long)uniq; rt.loads[1] += 1ull; }
+            rt.summary[3] = s.tot[2];
+            if (rt.loads && !L.dense) { /* reductions: nothing waits for them */
+                atomicAdd(rt.loads, (unsigned long long)uniq);
+                atomicAdd(rt.loads + 1, 1ull);
+            }
         }
     }
     __syncthreads();
-    for (uint32_t e = threadIdx.x; e <= E; e += blockDim.x) {
-        rt.offsets[e] = s.off[e];
-        if (e < E) rt.counts[e] = s.cnt[e];
-    }
     /* active experts and their (expert, 8-token chunk) work pairs */
     for (int u = warp; u < s.uniq; u += nwarps) {
         const int e = s.act[u];
-        if (lane == 0) rt.act[u] = e;
         const int nch = (s.cnt[e] + LFM_GEMV_CHUNK - 1) / LFM_GEMV_CHUNK;
         for (int c = lane; c < nch; c += 32) rt.pairs[s.pb[u] + c] = make_int2(u, c);
     }
@@ -206,12 +229,22 @@ __device__ void route_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTabl
     const int lane = threadIdx.x & 31;
     /* up to kPre ids per thread are loaded once, all in flight together, and
      * serve both passes; larger n falls back to loads in each pass */
-    constexpr int kPre = 16;
+    constexpr int kPre = 4;
     const uint32_t npass = (n + blockDim.x - 1) / blockDim.x;
     const bool pre = npass <= (uint32_t)kPre;
     int ev[kPre];
 #pragma unroll
-    for (int i = 0; i < kPre; ++i) ev[i] = pre ? dispatch_id(rt, threadIdx.x + i * blockDim.x, n, E, true) : -1;
+    for (int i = 0; i < kPre; ++i) {
+        const uint32_t a = threadIdx.x + i * blockDim.x;
+        ev[i] = pre && a < n ? __ldcg(rt.idx + a) : -1;
+    }
+    bool bad_id = false;
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        const uint32_t a = threadIdx.x + i * blockDim.x;
+        if (pre && a < n && (unsigned)ev[i] >= E) { bad_id = true; ev[i] = -1; }
+    }
+    if (bad_id) atomicOr(rt.err, LFM_DEVERR_EXPERT_ID);
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) { s.cnt[e] = 0; s.cur[e] = 0; }
     __syncthreads();
     /* histogram: one shared-memory atomic per run of equal expert ids in a warp */
@@ -269,21 +302,34 @@ __device__ __forceinline__ uint32_t route_key(float v) {
 }
 
 /* Top-K of token t from its E logits (global memory written by other blocks,
- * read through L2; or this block's shared memory). */
-__device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &rt, const float *logits_t,
-                           bool global_logits) {
+ * read through L2; or this block's shared memory), kPer experts a lane
+ * (E <= 32 * kPer).  The loops are unrolled kPer times only: this tail runs
+ * once per token group on a cold instruction cache, so the code it executes
+ * is kept short. */
+template <int kPer>
+__device__ void route_topk_n(const MoeLayerDev &L, uint32_t t, const RouteTables &rt,
+                                          const float *logits_t, bool global_logits) {
     const int lane = threadIdx.x & 31;
     const uint32_t E = L.E, K = L.K;
-    float sig[8], sel[8]; /* experts lane + 32*i, E <= 256 */
+    float z[kPer], b[kPer], sig[kPer], sel[kPer]; /* experts lane + 32*i */
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kPer; ++i) { /* every load first */
+        const uint32_t e = lane + 32u * i;
+        z[i] = 0.0f;
+        b[i] = 0.0f;
+        if (e < E) {
+            z[i] = global_logits ? __ldcg(logits_t + e) : logits_t[e];
+            if (L.bias) b[i] = __ldg(L.bias + e);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
         const uint32_t e = lane + 32u * i;
         sig[i] = 0.0f;
         sel[i] = -INFINITY;
         if (e < E) {
-            const float z = global_logits ? __ldcg(logits_t + e) : logits_t[e];
-            sig[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, lfm_expf(-z)));
-            sel[i] = L.bias ? __fadd_rn(sig[i], L.bias[e]) : sig[i];
+            sig[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, lfm_expf(-z[i])));
+            sel[i] = L.bias ? __fadd_rn(sig[i], b[i]) : sig[i];
         }
     }
     /* K rounds of argmax under the reference's rule (strict >, the lowest id
@@ -296,7 +342,7 @@ __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &
         uint32_t bkey = 0u;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kPer; ++i) {
             const uint32_t e = lane + 32u * i, key = e < E ? route_key(sel[i]) : 0u;
             if (key > bkey) { bkey = key; bi = (int)e; }
         }
@@ -305,7 +351,7 @@ __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &
         const int win = mkey == 0u ? 0 : __reduce_min_sync(LFM_FULL_MASK, bkey == mkey ? bi : 0x7fffffff);
         float s_b = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kPer; ++i) {
             if (lane + 32u * i == (uint32_t)win) { s_b = sig[i]; sel[i] = -1e30f; }
         }
         const float wk = __shfl_sync(LFM_FULL_MASK, s_b, win & 31);
@@ -320,6 +366,16 @@ __device__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &
         rt.idx[(size_t)t * K + lane] = my_i;
         rt.w[(size_t)t * K + lane] = my_w;
     }
+}
+
+__device__ __forceinline__ void route_topk(const MoeLayerDev &L, uint32_t t, const RouteTables &rt,
+                                           const float *logits_t, bool global_logits) {
+    if (L.E <= 32)
+        route_topk_n<1>(L, t, rt, logits_t, global_logits);
+    else if (L.E <= 64)
+        route_topk_n<2>(L, t, rt, logits_t, global_logits);
+    else
+        route_topk_n<8>(L, t, rt, logits_t, global_logits);
 }
 
 /*
@@ -937,7 +993,10 @@ __global__ void __launch_bounds__(1024) k_ep_plan(EpStep st, uint32_t first, uin
         s.bad = acc < 0 || (uint32_t)acc > st.max_recv;
         if (s.bad) atomicOr(st.err, LFM_DEVERR_SEGMENT);
         *st.self.n_recv = s.bad ? 0 : acc;
-        if (rt.loads) { rt.loads[0] += (unsigned long long)uniq; rt.loads[1] += 1ull; }
+        if (rt.loads) {
+            atomicAdd(rt.loads, (unsigned long long)uniq);
+            atomicAdd(rt.loads + 1, 1ull);
+        }
     }
     __syncthreads();
     if (s.bad) {

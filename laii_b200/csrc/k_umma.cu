@@ -172,6 +172,24 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+}
+/* N = 4 or 8 consecutive 32-bit columns of this thread's TMEM lane. */
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&v)[N]) {
+    if constexpr (N == 8) tmem_ld8(taddr, v);
+    else tmem_ld4(taddr, v);
+}
+template <int N>
+__device__ __forceinline__ void tmem_tien(uint32_t (&a)[N]) {
+    if constexpr (N == 8)
+        asm volatile("" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7])::"memory");
+    else
+        asm volatile("" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3])::"memory");
+}
 /* Wait for this thread's TMEM loads; the registers are tied to the wait so no
  * use of them is scheduled before it. */
 __device__ __forceinline__ void tmem_wait(uint32_t (&a)[8], uint32_t (&b)[8]) {
@@ -218,7 +236,7 @@ __device__ __forceinline__ void sts128(uint8_t *p, uint32_t x, uint32_t y, uint3
 __device__ __forceinline__ bool uwait(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *err) {
     if (lfm_mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = lfm_globaltimer();
-    while (!lfm_mbar_try_wait(bar, parity)) {
+    while (!lfm_mbar_try_wait_sleep(bar, parity, LFM_WAIT_SLEEP_NS)) {
         if (*abort) return false;
         if (lfm_globaltimer() - t0 > LFM_WAIT_LIMIT_NS) {
             atomicOr(err, LFM_DEVERR_TIMEOUT);
@@ -439,8 +457,8 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
             const UTile tile = tile_at(gg / nb);
             uint64_t *bar = &bars.r_full[gg % C::kSR];
             lfm_mbar_arrive_tx(bar, kRawSlot);
-            lfm_tma_load_2d(sR + (gg % C::kSR) * kRawSlot, tile.mat ? &tmw1 : &tmw0, (gg % nb) * kRaw,
-                            (uint32_t)tile.expert * A.rows + tile.row0, bar);
+            lfm_tma_load_2d_hint(sR + (gg % C::kSR) * kRawSlot, tile.mat ? &tmw1 : &tmw0, (gg % nb) * kRaw,
+                                 (uint32_t)tile.expert * A.rows + tile.row0, bar, lfm_policy_evict_first());
         };
         bool ok = true;
         if (pt == 0)
@@ -623,27 +641,33 @@ __global__ void __launch_bounds__(UCfg<kDec>::kThreads, 1) k_q4k_umma(const __gr
  * super-block each MMA thread waits twice, issues 8 MMAs back to back and
  * commits twice.
  *
- * TMEM: the A slots (as many as the two accumulator buffers of 2*nt columns,
- * D1 | D2, leave room for: 3 for nt <= 32, 2 for nt <= 64), then the
- * accumulators.
+ * TMEM: the A slots (as many as the accumulator buffers leave room for: two
+ * buffers of 2*nt columns, D1 | D2, leave 3 slots for nt <= 32 and 2 for
+ * nt <= 64), then the accumulators.
  *
  * Decode variant (kDec, token blocks of 16): A is the raw nibbles (64 TMEM
  * columns a super-block, no scale multiply) and every 32-wide sub-block j gets
  * its own accumulator D_j = q4 . q8 (8 x 16 columns a buffer), so a super-block
  * takes 8 MMAs instead of 16; MMA stream s issues the four sub-blocks of half
  * s, so the streams never share an accumulator.  The epilogue forms
- * acc = sum_j sc_j * D_j exactly.  At a few tokens per expert the MMA count,
- * not the arithmetic, sets the pace.
+ * acc = sum_j sc_j * D_j exactly.  At a few tokens per expert the round trip
+ * MMA -> epilogue -> free buffer and the issue slots the warps share set the
+ * pace; every wait therefore suspends the warp (mbarrier try_wait with a
+ * time hint) instead of spinning.
  * Warps: epilogue (8 for the decode variant, else 16: two or four per TMEM
- * lane quarter, splitting the tokens), 4 expanders, two MMA-issuing warps (one thread each:
- * A1 -> D1 and A2 -> D2; the first also allocates TMEM), then one warp each
- * for the weight TMA and the token loader.
+ * lane quarter, splitting the tokens), 4 expanders, two MMA-issuing warps (one
+ * thread each: A1 -> D1 and A2 -> D2; the first also allocates TMEM), then one
+ * warp each for the weight TMA and the token loader.
  * --------------------------------------------------------------------------- */
 template <bool kDec>
 struct TCfg {
     static constexpr int kEpi = kDec ? 8 : 16;       /* epilogue warps: 2 / 4 per TMEM lane quarter */
-    static constexpr int kWarpExp = kEpi;            /* 4 expander warps: lane quarter = warp & 3 */
-    static constexpr int kWarpMma = kEpi + 4;        /* two MMA-issuing warps: A1 -> D1, A2 -> D2 */
+    static constexpr int kExp = 4;                   /* expander warps: lane quarter = warp & 3 (with 8,
+                                                        two a quarter each taking half of every
+                                                        super-block's chunks, the decode GEMM ran
+                                                        1.6x slower) */
+    static constexpr int kWarpExp = kEpi;
+    static constexpr int kWarpMma = kEpi + kExp;     /* two MMA-issuing warps: A1 -> D1, A2 -> D2 */
     static constexpr int kWarpTma = kWarpMma + 2;
     static constexpr int kWarpLoad = kWarpMma + 3;
     static constexpr int kThreads = (kWarpLoad + 1) * 32;
@@ -652,6 +676,8 @@ struct TCfg {
     static constexpr int kRowInfo = kM * (kDec ? 32 : 16); /* d, dmin, m0..3, m4..7 (, sc0..3, sc4..7) per row */
     static constexpr uint32_t kSlotCols = kDec ? 64 : 128; /* TMEM columns of one A slot (a super-block)  */
     static constexpr uint32_t kAccTok = kDec ? 8 : 2;      /* accumulator columns per token in a buffer   */
+    static constexpr uint32_t kAccBufs = 2;                /* accumulator buffers (a third measured no
+                                                              faster in the decode variant) */
     static constexpr uint32_t kMaxSlotsC = kDec ? 4 : 3;
     static constexpr int kOffB = 0;
     static constexpr int kOffR = kOffB + kBBytes;
@@ -663,19 +689,21 @@ static_assert(TCfg<false>::kSmem <= 227 * 1024 && TCfg<true>::kSmem <= 227 * 102
 constexpr uint32_t kNtTm = 64;      /* most tokens per block: two A slots + two 2*nt buffers = 512 columns */
 constexpr uint32_t kNtTmDec = 16;   /* token block of the decode variant: four A slots + two 8*16 buffers */
 constexpr uint32_t kMaxSlots = 4;
-static_assert(2 * 128 + 4 * kNtTm <= kTmemCols && 2 * 64 + 16 * kNtTmDec <= kTmemCols, "tensor memory");
+constexpr uint32_t kMaxAccBufs = 3;
+static_assert(2 * 128 + 4 * kNtTm <= kTmemCols && 2 * 64 + 3 * 8 * kNtTmDec <= kTmemCols, "tensor memory");
 /* input ring slots for nt tokens a block: TMEM (A) and the shared-memory token slots (B) */
 template <bool kDec>
 __host__ __device__ constexpr uint32_t tm_slots(uint32_t nt) {
     using C = TCfg<kDec>;
-    const uint32_t a = (kTmemCols - 2 * C::kAccTok * nt) / C::kSlotCols, b = (uint32_t)C::kBBytes / (2 * nt * kHalf);
+    const uint32_t a = (kTmemCols - C::kAccBufs * C::kAccTok * nt) / C::kSlotCols,
+                   b = (uint32_t)C::kBBytes / (2 * nt * kHalf);
     const uint32_t n = a < b ? a : b;
     return n < C::kMaxSlotsC ? n : C::kMaxSlotsC;
 }
 
 struct TmBars {
     uint64_t in_full[kMaxSlots], in_empty[kMaxSlots], r_full[8], r_empty[8];
-    uint64_t t_full[2], t_empty[2], ti_full[kSI], ri_full[kSI], i_empty[kSI];
+    uint64_t t_full[kMaxAccBufs], t_empty[kMaxAccBufs], ti_full[kSI], ri_full[kSI], i_empty[kSI];
     uint32_t tmem;
     int abort;
 };
@@ -711,20 +739,20 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
     if (kEp && tid < LFM_EP_MAX_RANKS) s_yh[tid] = ep.yhome[tid];
     if (tid == 0) {
         for (uint32_t i = 0; i < ns; ++i) {
-            lfm_mbar_init(&bars.in_full[i], 5); /* the 4 expander warps and the loader's expect_tx */
+            lfm_mbar_init(&bars.in_full[i], C::kExp + 1); /* the expander warps and the loader's expect_tx */
             lfm_mbar_init(&bars.in_empty[i], 2); /* one commit per MMA stream */
         }
-        for (int i = 0; i < 2; ++i) {
+        for (uint32_t i = 0; i < C::kAccBufs; ++i) {
             lfm_mbar_init(&bars.t_full[i], 2);
             lfm_mbar_init(&bars.t_empty[i], C::kEpi);
         }
         for (int i = 0; i < C::kSR; ++i) {
             lfm_mbar_init(&bars.r_full[i], 1);
-            lfm_mbar_init(&bars.r_empty[i], 4);
+            lfm_mbar_init(&bars.r_empty[i], C::kExp);
         }
         for (uint32_t i = 0; i < kSI; ++i) {
             lfm_mbar_init(&bars.ti_full[i], 1);
-            lfm_mbar_init(&bars.ri_full[i], 4);
+            lfm_mbar_init(&bars.ri_full[i], 4); /* the first expander warp of each lane quarter */
             lfm_mbar_init(&bars.i_empty[i], C::kEpi);
         }
         bars.abort = 0;
@@ -766,7 +794,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
         const int r = 32 * q4 + lane;
         const int half = (int)nt / (C::kEpi / 4);
         const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
-        uint32_t g = 0;
+        uint32_t g = 0, buf = 0, ph = 0; /* accumulator buffer ring position and phase */
         bool ok = true;
         for (uint32_t it = 0; it < my_tiles && ok; ++it) {
             const UTile tile = tile_at(it);
@@ -776,7 +804,6 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
 #pragma unroll
             for (int i = 0; i < kCols; ++i) S[i] = 0.0f;
             for (uint32_t sb = 0; sb < nb; ++sb, ++g) {
-                const uint32_t buf = g & 1u, ph = (g >> 1) & 1u;
                 ok = __all_sync(LFM_FULL_MASK, uwait(&bars.t_full[buf], ph, abort, A.err) &&
                                                    uwait(&bars.ti_full[g % kSI], (g / kSI) & 1u, abort, A.err) &&
                                                    uwait(&bars.ri_full[g % kSI], (g / kSI) & 1u, abort, A.err));
@@ -794,7 +821,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                 const uint64_t nm = pk2(-__uint_as_float(ri.y), -__uint_as_float(ri.y)); /* -dmin */
                 const float *d8s = reinterpret_cast<const float *>(sT + is * kTokInfo) + ch * half;
                 const uint4 *bps = reinterpret_cast<const uint4 *>(sT + is * kTokInfo + nt * 4) + ch * half;
-                constexpr int kStep = 8; /* columns per TMEM round trip */
+                constexpr int kStep = kCols < 8 ? kCols : 8; /* columns per TMEM round trip */
 #pragma unroll
                 for (int c = 0; c < kCols / kStep; ++c) {
                     if (kStep * c < nv) { /* warp-uniform */
@@ -802,14 +829,14 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                         int acc[kStep];
                         if constexpr (kDec) {
                             /* acc = sum_j sc_j * D_j, D_j at column block j * nt */
-                            uint32_t v[8][8];
+                            uint32_t v[8][kStep];
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) tmem_ld8(tl + col + (uint32_t)j * nt, v[j]);
+                            for (int j = 0; j < 8; ++j) tmem_ldn<kStep>(tl + col + (uint32_t)j * nt, v[j]);
                             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) tmem_tie(v[j]);
+                            for (int j = 0; j < 8; ++j) tmem_tien<kStep>(v[j]);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) {
+                            for (int i = 0; i < kStep; ++i) {
                                 int a = 0;
 #pragma unroll
                                 for (int j = 0; j < 8; ++j) a += sc[j] * (int)v[j][i];
@@ -843,6 +870,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                     lfm_mbar_arrive(&bars.t_empty[buf]);
                     lfm_mbar_arrive(&bars.i_empty[is]);
                 }
+                if (++buf == C::kAccBufs) { buf = 0; ph ^= 1u; }
             }
             if (!ok) break;
             if constexpr (kEp) {
@@ -867,6 +895,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
     } else if (warp < C::kWarpMma) {
         /* ---------------- expanders: raw Q4_K rows -> A1 | A2 in TMEM ---------------- */
         const int q4 = warp & 3;
+        const int eh = C::kExp > 4 ? (warp - C::kWarpExp) >> 2 : 0; /* which expander of the lane quarter */
         const int p = 32 * q4 + lane;                     /* weight row of the tile = TMEM lane */
         const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
         bool ok = true;
@@ -881,22 +910,27 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
             const uint32_t scB = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
             const uint32_t mA = s1 & 0x3F3F3F3Fu;
             const uint32_t mB = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-            ok = __all_sync(LFM_FULL_MASK, g < kSI || uwait(&bars.i_empty[g % kSI], ((g / kSI) & 1u) ^ 1u, abort, A.err));
-            if (!ok) break;
-            uint8_t *rinfo = sW + (g % kSI) * C::kRowInfo + p * (kDec ? 32 : 16);
-            sts128(rinfo, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
-                   __float_as_uint(lfm_h2f((uint16_t)(hdr.x >> 16))), mA, mB);
-            if (kDec) sts128(rinfo + 16, scA, scB, 0u, 0u);
-            __syncwarp();
-            if (lane == 0) lfm_mbar_arrive(&bars.ri_full[g % kSI]);
+            if (eh == 0) { /* the row's scales for the epilogue */
+                ok = __all_sync(LFM_FULL_MASK,
+                                g < kSI || uwait(&bars.i_empty[g % kSI], ((g / kSI) & 1u) ^ 1u, abort, A.err));
+                if (!ok) break;
+                uint8_t *rinfo = sW + (g % kSI) * C::kRowInfo + p * (kDec ? 32 : 16);
+                sts128(rinfo, __float_as_uint(lfm_h2f((uint16_t)(hdr.x & 0xFFFFu))),
+                       __float_as_uint(lfm_h2f((uint16_t)(hdr.x >> 16))), mA, mB);
+                if (kDec) sts128(rinfo + 16, scA, scB, 0u, 0u);
+                __syncwarp();
+                if (lane == 0) lfm_mbar_arrive(&bars.ri_full[g % kSI]);
+            }
             ok = __all_sync(LFM_FULL_MASK, g < ns || uwait(&bars.in_empty[slot], spar ^ 1u, abort, A.err));
             if (!ok) break;
             tc_fence_after();
             const uint32_t abase = tl + slot * C::kSlotCols;
             if constexpr (kDec) {
-                /* the nibbles themselves: chunk hc's low nibbles in columns 16hc.., high in 16hc+8.. */
+                /* the nibbles themselves: chunk hc's low nibbles in columns 16hc.., high in 16hc+8..;
+                 * expander eh of the quarter takes its share of the four chunks */
+                constexpr int kHc = 4 / (C::kExp / 4); /* chunks per expander warp */
 #pragma unroll
-                for (int hc = 0; hc < 4; ++hc) {
+                for (int hc = kHc * eh; hc < kHc * eh + kHc; ++hc) {
                     const uint4 w0 = lfm_ld16<true>(raw + 16 + 32 * hc);
                     const uint4 w1 = lfm_ld16<true>(raw + 16 + 32 * hc + 16);
                     const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -965,11 +999,10 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
             const uint32_t dstep = (2 * blbo) >> 4;      /* one K step (32 bytes) in descriptor address units */
             const uint32_t hstep = opb >> 4;             /* one half super-block                              */
             const uint32_t aoff = tmem + stream * 32u;   /* A1 or A2 columns of a half                         */
-            uint32_t slot = 0, spar = 0, g = 0;
+            uint32_t slot = 0, spar = 0, g = 0, buf = 0, bpar = 0;
             for (uint32_t it = 0; it < my_tiles && ok; ++it) {
                 for (uint32_t sbk = 0; sbk < nb; ++sbk, ++g) {
-                    const uint32_t buf = g & 1u;
-                    if ((g >= 2 && !uwait(&bars.t_empty[buf], ((g >> 1) & 1u) ^ 1u, abort, A.err)) ||
+                    if ((g >= C::kAccBufs && !uwait(&bars.t_empty[buf], bpar ^ 1u, abort, A.err)) ||
                         !uwait(&bars.in_full[slot], spar, abort, A.err)) {
                         ok = false;
                         break;
@@ -995,6 +1028,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                     umma_commit(&bars.in_empty[slot]);
                     umma_commit(&bars.t_full[buf]);
                     if (++slot == ns) { slot = 0; spar ^= 1u; }
+                    if (++buf == C::kAccBufs) { buf = 0; bpar ^= 1u; }
                 }
             }
             if (!ok) *abort = 1;
@@ -1004,6 +1038,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
         if (lane == 0) {
             bool ok = true;
             uint32_t rs = 0, rpar = 0, g = 0;
+            const uint64_t policy = lfm_policy_evict_first(); /* weights are read once a layer */
             for (uint32_t it = 0; it < my_tiles && ok; ++it) {
                 const UTile tile = tile_at(it);
                 const CUtensorMap *tm = tile.mat ? &tmw1 : &tmw0;
@@ -1011,7 +1046,7 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                 for (uint32_t sbk = 0; sbk < nb; ++sbk, ++g) {
                     if (g >= (uint32_t)C::kSR && !uwait(&bars.r_empty[rs], rpar ^ 1u, abort, A.err)) { ok = false; break; }
                     lfm_mbar_arrive_tx(&bars.r_full[rs], kRawSlot);
-                    lfm_tma_load_2d(sR + rs * kRawSlot, tm, sbk * kRaw, row, &bars.r_full[rs]);
+                    lfm_tma_load_2d_hint(sR + rs * kRawSlot, tm, sbk * kRaw, row, &bars.r_full[rs], policy);
                     if (++rs == (uint32_t)C::kSR) { rs = 0; rpar ^= 1u; }
                 }
             }

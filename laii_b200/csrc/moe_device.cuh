@@ -85,6 +85,22 @@ __device__ __forceinline__ bool lfm_mbar_try_wait(uint64_t *bar, uint32_t parity
     return ok != 0;
 }
 
+/* The same test, but the thread may be suspended (for at most hint_ns) until
+ * the phase completes: a waiting warp then takes no issue slots from the
+ * warps doing the work. */
+__device__ __forceinline__ bool lfm_mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(lfm_smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+#define LFM_WAIT_SLEEP_NS 20000u /* longest single suspension inside a bounded wait */
+
 __device__ __forceinline__ uint64_t lfm_globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -96,7 +112,7 @@ __device__ __forceinline__ uint64_t lfm_globaltimer() {
 __device__ __forceinline__ bool lfm_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err) {
     if (lfm_mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = lfm_globaltimer();
-    while (!lfm_mbar_try_wait(bar, parity)) {
+    while (!lfm_mbar_try_wait_sleep(bar, parity, LFM_WAIT_SLEEP_NS)) {
         if (lfm_globaltimer() - t0 > LFM_WAIT_LIMIT_NS) {
             atomicOr(err, LFM_DEVERR_TIMEOUT);
             return false;
@@ -170,6 +186,17 @@ __device__ __forceinline__ void lfm_tma_load_2d(void *dst, const CUtensorMap *tm
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             lfm_smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(lfm_smem_u32(bar))
+        : "memory");
+}
+
+/* The same copy with an L2 cache policy (lfm_policy_evict_first for data read
+ * once, so it leaves the rest of the working set in L2). */
+__device__ __forceinline__ void lfm_tma_load_2d_hint(void *dst, const CUtensorMap *tm, uint32_t x, uint32_t y,
+                                                     uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(
+            lfm_smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(lfm_smem_u32(bar)), "l"(policy)
         : "memory");
 }
 
