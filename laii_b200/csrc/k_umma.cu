@@ -716,6 +716,14 @@ __device__ __forceinline__ void umma_i8_ta(uint32_t d, uint32_t a_tmem, uint64_t
         : "memory");
 }
 
+/* 16 consecutive 32-bit columns of this thread's TMEM lane. */
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+                 "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+                 : "memory");
+}
+
 /* 8 consecutive 32-bit columns of this thread's TMEM lane. */
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
@@ -934,14 +942,13 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                     const uint4 w0 = lfm_ld16<true>(raw + 16 + 32 * hc);
                     const uint4 w1 = lfm_ld16<true>(raw + 16 + 32 * hc + 16);
                     const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    uint32_t v1[8], v2[8];
+                    uint32_t v[16]; /* low nibbles, then high nibbles: 16 columns, one store */
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        v1[i] = wv[i] & 0x0F0F0F0Fu;
-                        v2[i] = (wv[i] >> 4) & 0x0F0F0F0Fu;
+                        v[i] = wv[i] & 0x0F0F0F0Fu;
+                        v[8 + i] = (wv[i] >> 4) & 0x0F0F0F0Fu;
                     }
-                    tmem_st8(abase + 16 * hc, v1);
-                    tmem_st8(abase + 16 * hc + 8, v2);
+                    tmem_st16(abase + 16 * hc, v);
                 }
             } else
 #pragma unroll
@@ -955,24 +962,18 @@ __global__ void __launch_bounds__(TCfg<kDec>::kThreads, 1) k_q4k_tm(const __grid
                     const uint4 w1 = lfm_ld16<true>(raw + 16 + 32 * (2 * h + cc) + 16);
                     const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
                     const uint32_t c0 = abase + 64 * h + 16 * cc;
-                    uint32_t v1[8], v2[8];
+                    uint32_t v1[16], v2[16]; /* A1, A2: low-nibble columns then high-nibble columns */
                     /* bytes of a nibble word times a scalar <= 15 stay below 256: no carries */
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const uint32_t lo = wv[i] & 0x0F0F0F0Fu;
+                        const uint32_t lo = wv[i] & 0x0F0F0F0Fu, hi = (wv[i] >> 4) & 0x0F0F0F0Fu;
                         v1[i] = lo * bl;
                         v2[i] = lo * al;
+                        v1[8 + i] = hi * bh;
+                        v2[8 + i] = hi * ah;
                     }
-                    tmem_st8(c0, v1);
-                    tmem_st8(c0 + 32, v2);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const uint32_t hi = (wv[i] >> 4) & 0x0F0F0F0Fu;
-                        v1[i] = hi * bh;
-                        v2[i] = hi * ah;
-                    }
-                    tmem_st8(c0 + 8, v1);
-                    tmem_st8(c0 + 40, v2);
+                    tmem_st16(c0, v1);
+                    tmem_st16(c0 + 32, v2);
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
