@@ -684,6 +684,7 @@ def measure(cfg_id, cfg, args, ws, rank, local, use_ep, hbm, int8, steps, warmup
                    "layers_in_ring": run.ring if run.single else None},
            "roofline": dict(roof or {}, step=sroof) if roof else sroof,
            "kernel_us_per_launch": {k: round(u, 2) for k, (_, u) in prof.items()},
+           "limiting_kernel": limiting_kernel(prof),
            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": run.Tl * cfg["D"] * 4 * ws,
                    "d2h_bytes_per_step": run.Tl * cfg["D"] * 4 * ws},
            "gpu_launches": t["launches_per_step"] * steps, "clocks": t["clocks"],
@@ -697,6 +698,16 @@ def measure(cfg_id, cfg, args, ws, rank, local, use_ep, hbm, int8, steps, warmup
     if cpu and rank == 0 and ws == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg, seconds=args.cpu_seconds)
     return out
+
+
+def limiting_kernel(prof):
+    """The kernel with the most device time a layer in the per-kernel profile (the slowest rank's
+    mean per launch times its launches), and its share of the profiled kernel time."""
+    if not prof:
+        return None
+    tot = {k: n * u for k, (n, u) in prof.items()}
+    k = max(tot, key=tot.get)
+    return {"kernel": k, "us_per_launch": round(prof[k][1], 2), "share": round(tot[k] / max(sum(tot.values()), 1e-9), 3)}
 
 
 def run_ours(args, cfg_id, cfg):
@@ -732,13 +743,14 @@ def run_ours(args, cfg_id, cfg):
                          else "u8 x s8 -> s32 (q4_k x q8_k), fp32 accum"),
                "config": m["config"], "run": m["run"], "roofline": m["roofline"],
                "cpu_baseline": m.get("cpu_baseline"), "e2e": m["e2e"], "gpu_launches": m["gpu_launches"],
-               "clocks": m["clocks"], "kernel_us_per_launch": m["kernel_us_per_launch"]}
+               "clocks": m["clocks"], "kernel_us_per_launch": m["kernel_us_per_launch"],
+               "limiting_kernel": m["limiting_kernel"]}
         if "parity" in m:
             out["parity"] = m["parity"]
         if pre is not None:
             out["prefill"] = {k: pre[k] for k in ("config", "run", "value", "ms_per_step", "steps", "warmup",
                                                   "roofline", "e2e", "gpu_launches", "clocks", "kernel_us_per_launch",
-                                                  "cpu_baseline", "parity") if k in pre}
+                                                  "limiting_kernel", "cpu_baseline", "parity") if k in pre}
             out["prefill"]["unit"] = "tok/s"
         print(json.dumps(out), flush=True)
     if ws > 1:
