@@ -60,14 +60,35 @@ def _run(cmd):
     return r.stdout
 
 
+class _BuildLock:
+    """Exclusive lock over the build folder, so that several processes started together (one per
+    GPU) build once: the others wait, then find the library fresh."""
+
+    def __enter__(self):
+        import fcntl
+        os.makedirs(LIB, exist_ok=True)
+        self.f = open(os.path.join(LIB, ".build.lock"), "w")
+        fcntl.flock(self.f, fcntl.LOCK_EX)
+        return self
+
+    def __exit__(self, *exc):
+        import fcntl
+        fcntl.flock(self.f, fcntl.LOCK_UN)
+        self.f.close()
+
+
 def build_synth(force: bool = False) -> str:
     src = os.path.join(CSRC, "lfm_synth.c")
     deps = [src] + [os.path.join(CSRC, h) for h in ("lfm_formats.h", "lfm_synth_core.h")]
-    if force or _stale(SYNTH_SO, deps):
-        os.makedirs(LIB, exist_ok=True)
-        cc = os.environ.get("CC", "gcc")
-        _run([cc, "-std=c11", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-o", SYNTH_SO, src,
-              "-lm", "-lpthread"])
+    if not (force or _stale(SYNTH_SO, deps)):
+        return SYNTH_SO
+    with _BuildLock():
+        if force or _stale(SYNTH_SO, deps):
+            cc = os.environ.get("CC", "gcc")
+            tmp = f"{SYNTH_SO}.{os.getpid()}.tmp"
+            _run([cc, "-std=c11", "-O2", "-fPIC", "-shared", "-fvisibility=hidden", "-o", tmp, src,
+                  "-lm", "-lpthread"])
+            os.replace(tmp, SYNTH_SO)
     return SYNTH_SO
 
 
@@ -77,8 +98,14 @@ def build_gpu(force: bool = False, verbose_ptxas: bool = False) -> str:
                                                               os.path.abspath(__file__)]
     if not (force or _stale(GPU_SO, deps)):
         return GPU_SO
+    with _BuildLock():
+        if force or _stale(GPU_SO, deps):
+            _build_gpu_locked(srcs, verbose_ptxas)
+    return GPU_SO
+
+
+def _build_gpu_locked(srcs, verbose_ptxas: bool) -> None:
     os.makedirs(BUILD, exist_ok=True)
-    os.makedirs(LIB, exist_ok=True)
     nvcc = _nvcc()
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []
 
@@ -93,11 +120,10 @@ def build_gpu(force: bool = False, verbose_ptxas: bool = False) -> str:
         for _, out in results:
             sys.stdout.write(out)
     objs = [o for o, _ in results]
-    tmp = GPU_SO + ".tmp"
+    tmp = f"{GPU_SO}.{os.getpid()}.tmp"
     _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static", "-o", tmp, *objs,
           "-Xlinker", "--exclude-libs,ALL"])
     os.replace(tmp, GPU_SO)
-    return GPU_SO
 
 
 def build_all(force: bool = False) -> None:

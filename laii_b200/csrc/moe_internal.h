@@ -41,10 +41,10 @@ struct Q8Rows {
 /* tcgen05 GEMM work (k_umma.cu): a tile is weight rows [row0, row0 + 128) of
  * `expert` in matrix `mat` (0: gate or down, 1: up) against token block `tb`;
  * a token block is dispatch slots [slot0, slot0 + ntok), ntok <= nt. */
-struct LfmUTile {
+struct __align__(16) LfmUTile { /* one 16-byte store / load */
     int32_t expert, tb, row0, mat;
 };
-struct LfmUTokBlock {
+struct __align__(8) LfmUTokBlock {
     int32_t slot0, ntok;
 };
 /* Tile plans the dispatch step writes for the tcgen05 GEMMs (nt == 0: none):
