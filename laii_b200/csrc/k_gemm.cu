@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(256) k_swiglu_quant(const float *__restrict__ 
     const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
     float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, lfm_expf(-g[i]))), u[i]);
+    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, lfm_silu_expf(-g[i]))), u[i]);
     lfm_quant_block_warp(v, dst, r, b);
 }
 

@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) k_gemv(GemvArgs A) {
             if (kMats == 2) {
                 const float u = __shfl_down_sync(LFM_FULL_MASK, run, 16);
                 if (lane < 16 && h < nt) {
-                    const float silu = __fdiv_rn(run, __fadd_rn(1.0f, lfm_expf(-run)));
+                    const float silu = __fdiv_rn(run, __fadd_rn(1.0f, lfm_silu_expf(-run)));
                     A.out[(size_t)(slot0 + h) * L.I + row0 + g] = __fmul_rn(silu, u);
                 }
             } else {

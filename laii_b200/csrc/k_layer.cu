@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(kW * 32, 1) k_moe_layer(LayerArgs A) {
             if (stop) break;
             const float u = __shfl_down_sync(LFM_FULL_MASK, run, 16);
             if (lane < 16 && h < nt) {
-                const float silu = __fdiv_rn(run, __fadd_rn(1.0f, lfm_expf(-run)));
+                const float silu = __fdiv_rn(run, __fadd_rn(1.0f, lfm_silu_expf(-run)));
                 A.h[(size_t)(slot0 + h) * I + row0 + g] = __fmul_rn(silu, u);
             }
             cc.next(W, gpp_gu);

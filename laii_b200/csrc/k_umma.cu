@@ -1331,7 +1331,7 @@ __global__ void __launch_bounds__(256) k_swiglu_xt(const float *__restrict__ G, 
             const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
             const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, lfm_expf(-g[i]))), u[i]);
+            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, lfm_silu_expf(-g[i]))), u[i]);
         }
         quant_block_xt(v, dst, nt, t);
     }

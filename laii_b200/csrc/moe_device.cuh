@@ -29,6 +29,12 @@
  * keeps our sigmoid/SiLU within rounding of it far more often than a
  * single-precision expf would.  Calls CUDA's double exp. */
 __device__ __forceinline__ float lfm_expf(float x) { return (float)exp((double)x); }
+/* exp for SwiGLU's SiLU: CUDA's single-precision expf (within 2 ulp).  The
+ * layer's fp32 outputs are compared under a tolerance, so the double-precision
+ * round trip above (one double exp per element of h: the cost of the SwiGLU
+ * kernel at prefill sizes) is kept for the router, where an ulp can decide a
+ * top-K near-tie. */
+__device__ __forceinline__ float lfm_silu_expf(float x) { return expf(x); }
 
 __device__ __forceinline__ float lfm_h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 

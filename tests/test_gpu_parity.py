@@ -54,6 +54,9 @@ def routing_mismatch_ok(sel_row, idx_gpu, idx_orc, K):
     return True
 
 
+TIGHT = 1e-5  # rel-L2 of the MoE output (the layer's delta) against the reference: 100x inside the bar
+
+
 def compare_layer(oracle, gpu, L, x, layer_id):
     from laii_b200 import synth  # noqa: F401
     gpu.upload_layer(layer_id, L)
@@ -100,8 +103,9 @@ def test_q6k_down_layer_parity(oracle, gpu, D, E, K, I, T):
     L = cached_layer(D, E, K, I, down_type=14)
     x = synth.make_hidden(T, D, seed_offset=11)
     xg, xo, match = compare_layer(oracle, gpu, L, x, 1)
-    # exact integers and the reference's fp32 order: equal on almost every element
-    assert np.mean(xg[match] == xo[match]) > 0.9
+    # exact integers and the reference's fp32 order: only the exp of SiLU (CUDA's expf, within 2 ulp of
+    # glibc's) moves the layer's output, far inside the tolerance
+    assert rel_l2(xg[match] - x[match], xo[match] - x[match]) <= TIGHT
     assert gpu.last_stats()["tokens"] == T
 
 
@@ -125,9 +129,9 @@ def test_moe_layer_parity(oracle, gpu, D, E, K, I, T):
     L = cached_layer(D, E, K, I)
     x = synth.make_hidden(T, D, seed_offset=7)
     xg, xo, match = compare_layer(oracle, gpu, L, x, 0)
-    # the integer path is exact and the fp32 order is the reference's: expect equality
-    # on almost every element (only exp() ulps can differ)
-    assert np.mean(xg[match] == xo[match]) > 0.9
+    # the integer path is exact and the fp32 order is the reference's: only exp() ulps (the router's
+    # sigmoid, SiLU's single-precision expf) move the MoE output, far inside the tolerance
+    assert rel_l2(xg[match] - x[match], xo[match] - x[match]) <= TIGHT
 
 
 @pytest.mark.parametrize("D,E,K,I,T", [(512, 8, 2, 512, 64), (2048, 32, 4, 1792, 64)])
@@ -183,7 +187,7 @@ def test_dense_layer_parity(oracle, gpu):
     xg = gpu.forward(2, np.array(x, copy=True))
     xo = oracle.dense_forward(L, x)
     assert rel_l2(xg, xo) <= REL_L2 and np.abs(xg - xo).max() <= MAX_ABS
-    assert np.mean(xg == xo) > 0.9
+    assert rel_l2(xg - x, xo - x) <= TIGHT  # only SiLU's exp ulps move the FFN's output
 
 
 def test_prefill_zipf_subset(oracle, gpu):
