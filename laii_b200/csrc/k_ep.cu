@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(256) k_ep_publish(EpStep st, const int32_t *__
 __global__ void __launch_bounds__(256) k_ep_combine_wait(EpStep st, float *__restrict__ x, uint32_t T,
                                                          const float *__restrict__ w, int advance) {
     __shared__ int ok;
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* x and the routing tables belong to the preceding kernels */
     if (threadIdx.x == 0) {
         const uint32_t epoch = __ldcg(st.self.step) + st.ahead;
         ok = lfm_wait_flags(st.self.y_flag, st.world, epoch, st.wait_ns, st.err) ? 1 : 0;
@@ -86,12 +88,20 @@ cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaS
 }
 
 cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, bool advance,
-                                       cudaStream_t s) {
+                                       cudaStream_t s, bool pdl) {
     if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.D % 4) return cudaErrorInvalidValue;
     const uint64_t n = (uint64_t)T * (st.D / 4);
     uint64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks == 0) blocks = 1; /* T == 0 still waits: no rank runs ahead of the step */
-    k_ep_combine_wait<<<(unsigned)blocks, 256, 0, s>>>(st, x, T, w, advance ? 1 : 0);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_ep_combine_wait, st, x, T, w, advance ? 1 : 0);
 }

@@ -951,6 +951,8 @@ __global__ void __launch_bounds__(1024) k_ep_plan(EpStep st, uint32_t first, uin
     const UmmaPlanOut &P = rt.plan;
     const uint32_t W = st.world, E = st.E;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* the step counter, tables and plans belong to the preceding kernels */
     const uint32_t epoch = __ldcg(st.self.step) + st.ahead;
     if (threadIdx.x == 0) ok = lfm_wait_flags(st.self.cnt_flag, W, epoch, st.wait_ns, st.err) ? 1 : 0;
     __syncthreads();
@@ -1014,12 +1016,20 @@ __global__ void __launch_bounds__(1024) k_ep_plan(EpStep st, uint32_t first, uin
 }  // namespace
 
 cudaError_t lfm_launch_ep_plan(const EpStep &st, uint32_t first, uint32_t count, const RouteTables &rt,
-                               cudaStream_t s) {
+                               cudaStream_t s, bool pdl) {
     if (st.world == 0 || st.world > LFM_EP_MAX_RANKS || st.E > LFM_GPU_MAX_EXPERTS_DEV || count > st.E ||
         first + count > st.E || !rt.plan.nt)
         return cudaErrorInvalidValue;
-    k_ep_plan<<<1, 1024, 0, s>>>(st, first, count, rt);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_ep_plan, st, first, count, rt);
 }
 
 cudaError_t lfm_launch_dispatch(const MoeLayerDev &L, uint32_t T, const RouteTables &rt, cudaStream_t s) {

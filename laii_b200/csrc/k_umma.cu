@@ -1207,6 +1207,8 @@ __global__ void __launch_bounds__(kXtThreads) k_xt_gather_ep(EpGather g, const U
                                                              uint32_t nb, uint32_t nt, uint8_t *xt) {
     extern __shared__ __align__(128) uint8_t gx_raw[];
     GatherSmem &S = *reinterpret_cast<GatherSmem *>(gx_raw);
+    lfm_pdl_launch_dependents();
+    lfm_pdl_wait(); /* the plan (token blocks, rowmap) belongs to the preceding kernel */
     const int tb = blockIdx.x;
     if (tb >= __ldcg(n_tb)) return;
     const uint32_t sb = blockIdx.y, cols = nb * 256;
@@ -1363,15 +1365,14 @@ cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, cons
 }
 
 cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
-                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s) {
+                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl) {
     const uint32_t nb = cols / 256;
     if (max_tb == 0 || nb == 0) return cudaSuccess;
     static size_t cache[16];
     const cudaError_t e = lfm_smem_attr((const void *)k_xt_gather_ep, sizeof(GatherSmem), cache);
     if (e != cudaSuccess) return e;
-    k_xt_gather_ep<<<dim3(max_tb, nb), kXtThreads, sizeof(GatherSmem), s>>>(g, static_cast<const UTokBlock *>(tbs), n_tb,
-                                                                             nb, nt, xt);
-    return cudaGetLastError();
+    return launch_pdl(k_xt_gather_ep, dim3(max_tb, nb), dim3(kXtThreads), sizeof(GatherSmem), s, pdl, g,
+                      static_cast<const UTokBlock *>(tbs), n_tb, nb, nt, xt);
 }
 
 /* cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link). */

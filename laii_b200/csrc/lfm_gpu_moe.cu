@@ -1401,6 +1401,9 @@ lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x
     Workspace &w = h->ws;
     const int grid = h->sm_count;
     const EpStep es = ep_step_args(h, 1);
+    /* chained with programmatic dependent launch like the single-GPU layer: every kernel waits
+     * (griddepcontrol.wait) before it touches what its predecessor writes */
+    const bool pdl = !h->prof && h->use_pdl;
 
     /* home role: route this rank's tokens into the arena (Q8_K rows, slots); the dispatch publishes the counts */
     RouteTables rt = w.rt;
@@ -1417,7 +1420,7 @@ lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x
         pub.world = p.world;
         pub.rank = p.rank;
         pub.E = p.E;
-        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, false, &pub); },
+        LFM_CUDA(h, timed(h, K_ROUTE, s, [&] { return lfm_launch_route(L, x, T, es.self.xq, rt, s, pdl, &pub); },
                           lfm_route_kernels(L, T)));
     } else {
         LFM_CUDA(h, cudaMemsetAsync(rt.counts, 0, sizeof(int32_t) * p.E, s));
@@ -1456,13 +1459,17 @@ lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x
         eg.d[r] = a.xq.d;
         eg.bs[r] = a.xq.bs;
     }
-    LFM_CUDA(h, timed(h, K_EP_PLAN, s, [&] { return lfm_launch_ep_plan(es, first, count, rx, s); }));
-    LFM_CUDA(h, timed(h, K_XT, s, [&] { return lfm_launch_xt_gather_ep(eg, L.D, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s); }));
+    LFM_CUDA(h, timed(h, K_EP_PLAN, s, [&] { return lfm_launch_ep_plan(es, first, count, rx, s, pdl); }));
+    LFM_CUDA(h, timed(h, K_XT, s, [&] {
+        return lfm_launch_xt_gather_ep(eg, L.D, w.utbs, w.ucounts + 1, mtb, nt, w.xt, s, pdl);
+    }));
     LFM_CUDA(h, timed(h, K_GEMM_GU, s, [&] {
         return lfm_launch_q4k_umma(L.gate, L.up, count, L.I, L.D, w.xt, nt, w.utiles_gu, w.utbs, w.ucounts, w.h, w.u,
-                                   h->dev_err, grid, s);
+                                   h->dev_err, grid, s, nullptr, pdl);
     }));
-    LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] { return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s); }));
+    LFM_CUDA(h, timed(h, K_SWIGLU, s, [&] {
+        return lfm_launch_swiglu_xt(w.h, w.u, L.I, w.utbs, w.ucounts + 3, mtb, nt, w.xt, s, pdl);
+    }));
     /* down: every output row stored at its home rank from the epilogue (peer stores over NVLink),
      * y_flag raised on every rank by the last CTA */
     UmmaEpOut eo{};
@@ -1478,11 +1485,11 @@ lfm_gpu_status_t ep_forward_layer(lfm_gpu_moe_t *h, const LayerSlot &S, float *x
     eo.max_assign = es.max_assign;
     LFM_CUDA(h, timed(h, K_GEMM_D, s, [&] {
         return lfm_launch_q4k_umma(L.down, L.down, count, L.D, L.I, w.xt, nt, w.utiles_dn, w.utbs, w.ucounts + 2, w.y,
-                                   w.y, h->dev_err, grid, s, &eo);
+                                   w.y, h->dev_err, grid, s, &eo, pdl);
     }));
 
     /* home role: combine the outputs the expert ranks stored here; the step is done */
-    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, true, s); }));
+    LFM_CUDA(h, timed(h, K_COMBINE, s, [&] { return lfm_launch_ep_combine_wait(es, x, T, rt.w, true, s, pdl); }));
     return LFM_GPU_OK;
 }
 

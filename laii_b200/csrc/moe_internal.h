@@ -211,7 +211,7 @@ cudaError_t lfm_launch_ep_publish(const EpStep &st, const int32_t *counts, cudaS
  * (rowmap, n_recv) and the tcgen05 tile plans of the local experts
  * [first, first + count) */
 cudaError_t lfm_launch_ep_plan(const EpStep &st, uint32_t first, uint32_t count, const RouteTables &rt,
-                               cudaStream_t s);
+                               cudaStream_t s, bool pdl = false);
 /* Where an expert rank's down GEMM stores its output rows: the row of slot j
  * goes to home rank (ret[j] >> 24)'s yhome row ret[j] & 0xffffff (a peer
  * store over NVLink, or local); the GEMM's last CTA then raises y_flag[rank]
@@ -227,7 +227,7 @@ struct UmmaEpOut {
 /* home rank: wait for every expert rank's y_flag, then x[t] += w . yhome[t] in k order;
  * advance: then the rank's step counter moves to this step's epoch */
 cudaError_t lfm_launch_ep_combine_wait(const EpStep &st, float *x, uint32_t T, const float *w, bool advance,
-                                       cudaStream_t s);
+                                       cudaStream_t s, bool pdl = false);
 
 /* k_gemm.cu: prefill grouped GEMM (tensor cores) */
 size_t lfm_gemm_tiles_max(uint32_t rows, uint32_t slots, uint32_t experts);
@@ -256,7 +256,7 @@ cudaError_t lfm_launch_xt_gather(Q8Rows X, const int32_t *perm, uint32_t K, cons
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl = false);
 /* the same from other ranks' Q8_K rows (expert parallelism, g.rowmap set); X.cols gives D */
 cudaError_t lfm_launch_xt_gather_ep(const EpGather &g, uint32_t cols, const void *tbs, const int32_t *n_tb,
-                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s);
+                                    uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl = false);
 /* SwiGLU of the gate|up outputs, Q8_K, written as the down GEMM's token blocks */
 cudaError_t lfm_launch_swiglu_xt(const float *G, const float *U, uint32_t cols, const void *tbs, const int32_t *n_tb,
                                  uint32_t max_tb, uint32_t nt, uint8_t *xt, cudaStream_t s, bool pdl = false);
