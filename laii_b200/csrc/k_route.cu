@@ -13,7 +13,7 @@
  *   Q8_K of xb (tools/lfm2_decode_1x4.c:150-186).
  * Three implementations by size:
  *   T <= 16        k_route_cluster, one thread-block cluster (below);
- *   16 < T <= 128  k_route_dec, one launch (4 tokens x 8 experts a CTA);
+ *   16 < T <= 256  k_route_dec, one launch (4 tokens x 8 experts a CTA);
  *   above          k_norm_q8 + k_router_tiles + the dispatch launches.
  * Dispatch tables (route_dispatch): per-expert histogram, exclusive scan,
  * slot permutation and its inverse, the active experts and their (expert,
@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
 }
 
 /*
- * Decode-size route in one launch (16 < T <= kDecMaxT): CTA (g, p) takes tokens
+ * Decode-size route in one launch (16 < T <= kDecMaxT = 256): CTA (g, p) takes tokens
  * [4g, 4g + 4) and experts [8p, 8p + 8).  Its router rows and ffn_norm arrive
  * by bulk copy before griddepcontrol.wait (they do not depend on the preceding
  * kernel), the tokens' x after it.  Warp w takes token w: its RMSNorm in the
@@ -698,7 +698,8 @@ __global__ void __launch_bounds__(256) k_router_tiles(const __grid_constant__ CU
  * the dispatch tables and the tcgen05 tile plans.  Replaces k_norm_q8 +
  * k_router_tiles + k_dispatch_wide at these sizes.
  */
-constexpr uint32_t kDecMaxT = 128;
+constexpr uint32_t kDecMaxT = 256; /* measured against the three launches below: 25 vs 35 us at T=256, E=32;
+                                     34 vs 37 at E=64; at T=512 (E=64) 52 vs 46, so they take over there */
 constexpr uint32_t kDecTok = 4, kDecExp = 8;
 constexpr uint32_t kDecThreads = 256;
 static_assert(kDecTok <= kDecThreads / 32, "a warp per token");
